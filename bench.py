@@ -1,0 +1,586 @@
+#!/usr/bin/env python
+"""Benchmark of the int8 weight-only dequant-matmul path on B200.
+
+One step = one pass of the hot path over one batch of synthetic input: one
+call of popcornDequantizeMatmul_i8f32 (popcorn src/quantize.cu:86-112) on the
+headline workload, the memory-bound decode GEMV M=1, K=4096, N=4096. With
+--gpus N > 1 the weight rows are N-sharded (column-parallel) across ranks and
+every step ends with an NCCL all-gather of the output shards, so the whole
+job still computes the full 4096-wide output per step (strong scaling).
+
+Timing: W eager warm-up steps, then an untimed soak of CUDA-graph replays
+(clocks settle, NVML samples them), then EXACTLY K steps replayed from one
+CUDA graph, bracketed by barrier + synchronize, timed with CUDA events on the
+launching stream; the max over ranks is reported. Weights rotate over a pool
+of independent weight sets larger than 2x L2, so every step streams its
+weights from HBM.
+
+Arms:
+  (default)          this library, through its C ABI (ctypes on the in-tree .so)
+  --impl reference   popcorn's own CPU loop (test/test_quantize.cu:24-41,
+                     compiled from the reference sources into oracle/_ref) on
+                     all host cores of rank 0; also reports popcorn's own CUDA
+                     kernel rebuilt for sm_100a as an extra key.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "W8 dequant-matmul: int8-weight GB/s at M=1; TFLOPS at M=2048 (1/2/4/8 B200)"
+
+# Workloads: the headline plus the other single-GPU configurations reported as
+# extra keys. bytes = int8 weight bytes per step; flops = 2*M*N*K.
+WORKLOADS = {
+    "decode": dict(M=1, K=4096, N=4096, unit="GB/s", bound="hbm"),
+    "skinny": dict(M=32, K=4096, N=11008, unit="GB/s", bound="hbm"),
+    "prefill": dict(M=2048, K=4096, N=4096, unit="TFLOP/s", bound="tensor"),
+}
+
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of
+# the dominant kernel from one ncu capture of that workload; the command that
+# produced each figure is in the profiles/ summary named beside it.
+NCU_TRAFFIC = {}
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2000)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
+    p.add_argument("--extras", default="skinny,prefill",
+                   help="comma-separated extra single-GPU workloads reported beside the headline (N=1 only)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--soak-s", type=float, default=0.6)
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# Environment helpers
+# ---------------------------------------------------------------------------
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return dict(hbm=float(d["hbm_gbs"]), tc=float(d["bf16_tflops"]),
+                    tc_sustained=float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), source="measured")
+    except (OSError, KeyError, ValueError):
+        return dict(hbm=6650.0, tc=1590.0, tc_sustained=1400.0, source="fallback")
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+class ClockSampler:
+    """NVML sampling of SM clock and throttle reasons in a background thread."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, device, period_s=0.01):
+        self.samples = []  # (t, sm_mhz, reasons_mask)
+        self.period = period_s
+        self.ok = False
+        self.max_mhz = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            # Map the CUDA device to its NVML handle by PCI address (NVML does
+            # not see CUDA_VISIBLE_DEVICES renumbering).
+            p = torch.cuda.get_device_properties(device)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self.ok = False
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                mhz = self.nvml.nvmlDeviceGetClockInfo(self.h, self.nvml.NVML_CLOCK_SM)
+                rs = self.nvml.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+                self.samples.append((time.perf_counter(), mhz, rs))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.period)
+
+    def start(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        if self._t is not None:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self, t0, t1, t_timed0, t_timed1):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        window = [s for s in self.samples if t0 <= s[0] <= t1]
+        in_timed = [s for s in window if t_timed0 <= s[0] <= t_timed1]
+        loaded = [s for s in window if not (s[2] & self.REASONS["gpu_idle"])] or window
+        mhz = statistics.median([s[1] for s in loaded]) if loaded else None
+        mask = 0
+        for s in loaded:
+            mask |= s[2]
+        reasons = [k for k, v in self.REASONS.items() if mask & v and k != "gpu_idle"]
+        return {"sm_mhz": mhz, "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(loaded), "samples_in_timed_region": len(in_timed),
+                "window": "soak+timed (same graph replays)"}
+
+
+# ---------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------
+class Setup:
+    """Device-resident synthetic inputs for one workload on one rank."""
+
+    def __init__(self, torch, pc, wl, rank, world, device, pool_bytes):
+        self.torch = torch
+        self.pc = pc
+        M, K, N = wl["M"], wl["K"], wl["N"]
+        assert N % world == 0, "N must divide evenly across ranks"
+        self.M, self.K, self.N = M, K, N
+        self.Nl = N // world
+        self.world = world
+        per_set = self.Nl * K + (M * K * 4 if wl["bound"] == "tensor" else 0)
+        self.sets = max(2, math.ceil(pool_bytes / per_set))
+        if wl["bound"] == "tensor":
+            self.sets = min(self.sets, 4)
+        g = torch.Generator(device=device)
+        g.manual_seed(1234 + rank)
+        self.q, self.s, self.x, self.out = [], [], [], []
+        for i in range(self.sets):
+            # W ~ N(0, 0.02) f32 quantized per row by this library's quantizer.
+            w = torch.randn((self.Nl, K), generator=g, device=device) * 0.02
+            q, s = pc.quantize(w)
+            del w
+            self.q.append(q)
+            self.s.append(s)
+            if wl["bound"] == "tensor" or i == 0:
+                self.x.append(torch.randn((M, K), generator=g, device=device))
+            self.out.append(torch.empty((M, self.Nl), dtype=torch.float32, device=device))
+        self.gathered = torch.empty((world * M * self.Nl,), dtype=torch.float32, device=device)
+        torch.cuda.synchronize()
+        self.lib = pc.load_library()
+
+    def xi(self, i):
+        return self.x[i % len(self.x)]
+
+    def step(self, i, stream_handle, group=None):
+        j = i % self.sets
+        x = self.xi(i)
+        st = self.lib.popcornDequantizeMatmul_i8f32(self.out[j].data_ptr(), x.data_ptr(), self.q[j].data_ptr(),
+                                                    self.s[j].data_ptr(), self.M, self.Nl, self.K, stream_handle)
+        if st != 0:
+            raise RuntimeError(f"popcornDequantizeMatmul_i8f32 failed: {st} "
+                               f"{self.lib.popcornGetLastCudaErrorString().decode()}")
+        if self.world > 1:
+            self.torch.distributed.all_gather_into_tensor(self.gathered, self.out[j].view(-1), group=group)
+
+    def launches_per_step(self):
+        return self.pc.launch_count(self.x[0].data_ptr(), self.q[0].data_ptr(), self.M, self.Nl, self.K)
+
+    def path(self):
+        return self.pc.PATH_NAMES[self.pc.select_path(self.x[0].data_ptr(), self.q[0].data_ptr(),
+                                                      self.M, self.Nl, self.K)]
+
+
+def time_graph(torch, setup, steps, warmup, soak_s, sampler, dist_on):
+    """Warm up, soak, then time exactly `steps` steps from one CUDA graph."""
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            setup.step(i, stream.cuda_stream)
+    stream.synchronize()
+
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(steps):
+            setup.step(i, stream.cuda_stream)
+    torch.cuda.synchronize()
+
+    t_soak0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        graph.replay()
+    stream.synchronize()
+    once = time.perf_counter() - t_soak0
+    reps = max(1, int(soak_s / max(once, 1e-6)))
+    with torch.cuda.stream(stream):
+        for _ in range(reps):
+            graph.replay()
+    stream.synchronize()
+
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    t_timed0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        graph.replay()
+        end.record(stream)
+    torch.cuda.synchronize()
+    t_timed1 = time.perf_counter()
+    if dist_on:
+        torch.distributed.barrier()
+    ms = start.elapsed_time(end)
+    clocks = sampler.summary(t_soak0, t_timed1, t_timed0, t_timed1) if sampler else None
+    del graph
+    return ms, clocks
+
+
+def time_e2e(torch, setup, steps, warmup, dist_on):
+    """Same steps through the C ABI with host buffers: pinned H2D of x, the
+    call, pinned D2H of the (gathered) result, every step, stream-synchronized."""
+    M, K, N = setup.M, setup.K, setup.N
+    stream = torch.cuda.Stream()
+    x_host = torch.randn((M, K)).pin_memory()
+    y_host = torch.empty((M * N,), dtype=torch.float32).pin_memory()
+    x_dev = torch.empty((M, K), dtype=torch.float32, device=setup.x[0].device)
+
+    def one(i):
+        j = i % setup.sets
+        x_dev.copy_(x_host, non_blocking=True)
+        st = setup.lib.popcornDequantizeMatmul_i8f32(setup.out[j].data_ptr(), x_dev.data_ptr(), setup.q[j].data_ptr(),
+                                                     setup.s[j].data_ptr(), M, setup.Nl, K, stream.cuda_stream)
+        if st != 0:
+            raise RuntimeError("popcornDequantizeMatmul_i8f32 failed in e2e loop")
+        if setup.world > 1:
+            torch.distributed.all_gather_into_tensor(setup.gathered, setup.out[j].view(-1))
+            y_host.copy_(setup.gathered, non_blocking=True)
+        else:
+            y_host.copy_(setup.out[j].view(-1), non_blocking=True)
+        stream.synchronize()
+
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            one(i)
+        if dist_on:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for i in range(steps):
+            one(i)
+        end.record(stream)
+        torch.cuda.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    ms = start.elapsed_time(end)
+    return ms, M * K * 4, M * N * 4
+
+
+def max_over_ranks(torch, value, dist_on, device):
+    if not dist_on:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def throughput(wl, ms_per_step):
+    if wl["unit"] == "GB/s":
+        return wl["N"] * wl["K"] / (ms_per_step * 1e-3) / 1e9
+    return 2.0 * wl["M"] * wl["N"] * wl["K"] / (ms_per_step * 1e-3) / 1e12
+
+
+def roofline(wl, ms_per_launch, peaks, workload_name):
+    if wl["bound"] == "hbm":
+        achieved = wl["N"] * wl["K"] / (ms_per_launch * 1e-3) / 1e9
+        peak, unit = peaks["hbm"], "GB/s"
+    else:
+        achieved = 2.0 * wl["M"] * wl["N"] * wl["K"] / (ms_per_launch * 1e-3) / 1e12
+        peak, unit = peaks["tc"], "TFLOP/s"
+    return {"bound": wl["bound"], "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+            "frac": round(achieved / peak, 4), "peak_source": peaks["source"],
+            "traffic": NCU_TRAFFIC.get(workload_name)}
+
+
+def cpu_baseline(torch, setup, wl):
+    """popcorn's own CPU loop (oracle/_ref), all host threads, bounded sample."""
+    import oracle
+
+    threads = host_threads()
+    M, K, N = wl["M"], wl["K"], wl["N"]
+    use_ref = oracle.have_ref_loops()
+    kind = "reference" if use_ref else "port"
+    x = setup.x[0][:M].cpu().numpy()
+    q = setup.q[0].cpu().numpy()
+    s = setup.s[0].cpu().numpy()
+    rows = q.shape[0]
+
+    def run():
+        if use_ref:
+            oracle.ref_dequant_matmul(x, q, s, threads=threads)
+        else:
+            oracle.dequant_matmul(x, q, s, threads=threads)
+
+    t0 = time.perf_counter()
+    run()
+    one = time.perf_counter() - t0
+    reps = max(1, min(200, int(2.0 / max(one, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        run()
+    dt = (time.perf_counter() - t0) / reps
+    wbytes = rows * K
+    if wl["unit"] == "GB/s":
+        value = wbytes / dt / 1e9
+    else:
+        value = 2.0 * M * rows * K / dt / 1e12
+    return {"value": round(value, 4), "unit": wl["unit"], "cores": threads, "kind": kind,
+            "sample": f"{reps} full calls M={M} K={K} N={rows} (one weight set), {dt*1e3:.2f} ms each, "
+                      f"wall-clock, {threads} threads"}
+
+
+def run_ours(args):
+    import torch
+
+    import popcorn_b200 as pc
+
+    rank, world, local = dist_env()
+    dist_on = world > 1
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if dist_on:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    peaks = measured_peaks()
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    pool = 2.5 * l2
+
+    wl = WORKLOADS[args.workload]
+    setup = Setup(torch, pc, wl, rank, world, device, pool)
+    sampler = ClockSampler(device)
+    sampler.start()
+    ms, clocks = time_graph(torch, setup, args.steps, args.warmup, args.soak_s, sampler, dist_on)
+    sampler.stop()
+    ms = max_over_ranks(torch, ms, dist_on, device)
+    ms_step = ms / args.steps
+    value = throughput(wl, ms_step)
+    launches = setup.launches_per_step()
+
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": wl["unit"],
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 6),
+        "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None,
+        "dtype": "f32" if setup.path() == "simt_f32" else "f16xf16->f32",
+        "data": "synthetic: X ~ N(0,1), W ~ N(0,0.02) (torch.randn, fixed seed), int8 per-row via popcornQuantize_f32i8",
+        "config": {
+            "workload": f"{args.workload} M={wl['M']} K={wl['K']} N={wl['N']}",
+            "M": wl["M"], "K": wl["K"], "N": wl["N"],
+            "parallelism": f"column-parallel N-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+            "path": setup.path(),
+            "l2": f"weights rotate over {setup.sets} sets "
+                  f"({setup.sets * setup.Nl * wl['K'] / 1e6:.0f} MB per rank > 2x L2 {l2 / 1e6:.0f} MB)",
+            "timing": "K steps replayed from one CUDA graph, CUDA events, max over ranks",
+        },
+        "gpu_launches": launches * args.steps,
+        "roofline": roofline(dict(wl, N=setup.Nl), ms_step, peaks, args.workload) if world == 1 else
+        roofline(wl, ms_step, dict(peaks, hbm=peaks["hbm"] * world, tc=peaks["tc"] * world), args.workload),
+        "clocks": clocks,
+    }
+
+    if not args.no_e2e:
+        e2e_steps = min(args.steps, 2000)
+        ems, h2d, d2h = time_e2e(torch, setup, e2e_steps, max(3, args.warmup), dist_on)
+        ems = max_over_ranks(torch, ems, dist_on, device)
+        line["e2e"] = {"value": round(throughput(wl, ems / e2e_steps), 2), "unit": wl["unit"],
+                       "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                       "ms_per_step": round(ems / e2e_steps, 6),
+                       "how": "pinned H2D of x + popcornDequantizeMatmul_i8f32 via ctypes + pinned D2H of y, "
+                              "stream-synchronized every step"}
+
+    if world == 1 and rank == 0:
+        extras = {}
+        for name in [e for e in args.extras.split(",") if e and e != args.workload]:
+            ewl = WORKLOADS[name]
+            es = Setup(torch, pc, ewl, 0, 1, device, pool)
+            esteps = 200 if ewl["bound"] == "hbm" else 20
+            ems, _ = time_graph(torch, es, esteps, 3, 0.0, None, False)
+            eval_ = throughput(ewl, ems / esteps)
+            extras[name] = {"value": round(eval_, 2), "unit": ewl["unit"], "M": ewl["M"], "K": ewl["K"],
+                            "N": ewl["N"], "path": es.path(), "steps": esteps,
+                            "ms_per_step": round(ems / esteps, 6),
+                            "roofline": roofline(ewl, ems / esteps, peaks, name)}
+            del es
+            torch.cuda.empty_cache()
+        if extras:
+            line["extra_workloads"] = extras
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(torch, setup, wl)
+
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# Reference arm: popcorn's own CPU loop on the host cores (rank 0 only).
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    rank, world, local = dist_env()
+    if rank != 0:
+        return
+    import numpy as np
+
+    import oracle
+
+    wl = WORKLOADS[args.workload]
+    M, K, N = wl["M"], wl["K"], wl["N"]
+    threads = host_threads()
+    use_ref = oracle.have_ref_loops()
+    kind = "reference" if use_ref else "port"
+    x = oracle.fill_normal(M * K, 0, 1.0).reshape(M, K)
+    w = oracle.fill_normal(N * K, 1, 0.02).reshape(N, K)
+    q, s = oracle.quantize(w)
+
+    def call(rows):
+        if use_ref:
+            oracle.ref_dequant_matmul(x, q[:rows], s[:rows], threads=threads)
+        else:
+            oracle.dequant_matmul(x, q[:rows], s[:rows], threads=threads)
+
+    t0 = time.perf_counter()
+    call(N)
+    full = time.perf_counter() - t0
+    # Bound the run: each step is the full call if K steps fit in ~90 s,
+    # otherwise a leading block of output channels (same per-row work).
+    budget = 90.0 / max(1, args.steps + args.warmup)
+    rows = N if full <= budget else max(threads, int(N * budget / full))
+    for _ in range(args.warmup):
+        call(rows)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        call(rows)
+    dt = (time.perf_counter() - t0) / args.steps
+    if wl["unit"] == "GB/s":
+        value = rows * K / dt / 1e9
+    else:
+        value = 2.0 * M * rows * K / dt / 1e12
+    sample = (f"each step: popcorn test loop on M={M} K={K} N={rows} of {N} rows, "
+              f"{dt * 1e3:.3f} ms, {threads} threads, wall clock")
+    line = {
+        "metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": wl["unit"], "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 * N / rows, 6),
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic: X ~ N(0,1), W ~ N(0,0.02) (SplitMix64 + Irwin-Hall), int8 per-row",
+        "config": {"workload": f"{args.workload} M={M} K={K} N={N}", "M": M, "K": K, "N": N,
+                   "parallelism": "host cores of rank 0"},
+        "cpu_baseline": {"value": round(value, 4), "unit": wl["unit"], "cores": threads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": wl["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    try:
+        line["reference_gpu_kernel"] = reference_gpu_kernel(args, wl, x, q, s)
+    except Exception as e:  # noqa: BLE001 - the CPU arm stands on its own
+        line["reference_gpu_kernel"] = {"unavailable": str(e)[:200]}
+    print(json.dumps(line), flush=True)
+
+
+def reference_gpu_kernel(args, wl, x, q, s):
+    """popcorn's own CUDA kernel (src/quantize.cu rebuilt for sm_100a), timed
+    like ours: weights rotated beyond L2, K launches from one CUDA graph."""
+    import torch
+
+    import oracle
+
+    if not oracle.have_popcorn_ref_gpu() or not torch.cuda.is_available():
+        return {"unavailable": "oracle/_ref/libpopcorn_ref.so or GPU missing"}
+    lib = oracle.popcorn_ref_gpu()
+    dev = torch.device("cuda", 0)
+    M, K, N = wl["M"], wl["K"], wl["N"]
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    sets = max(2, math.ceil(2.5 * l2 / (N * K)))
+    qd = torch.from_numpy(q).to(dev)
+    sd = torch.from_numpy(s).to(dev)
+    qs = [qd] + [qd.clone() for _ in range(sets - 1)]
+    xd = torch.from_numpy(x).to(dev)
+    out = torch.empty((M, N), dtype=torch.float32, device=dev)
+    steps = min(args.steps, 200)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            assert lib.popcornDequantizeMatmul_i8f32(out.data_ptr(), xd.data_ptr(), qs[i % sets].data_ptr(),
+                                                     sd.data_ptr(), M, N, K, stream.cuda_stream) == 0
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(steps):
+            lib.popcornDequantizeMatmul_i8f32(out.data_ptr(), xd.data_ptr(), qs[i % sets].data_ptr(),
+                                              sd.data_ptr(), M, N, K, stream.cuda_stream)
+    with torch.cuda.stream(stream):
+        g.replay()
+    stream.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        a.record(stream)
+        g.replay()
+        b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    ref = oracle.dequant_matmul(x, q, s, fused=True, threads=host_threads())
+    got = out.cpu().numpy()
+    return {"value": round(throughput(wl, ms), 2), "unit": wl["unit"], "ms_per_step": round(ms, 6),
+            "steps": steps, "what": "popcorn src/quantize.cu dequantizeMatmulKernel_i8f32, nvcc -O3 sm_100a",
+            "normwise_err_vs_oracle": oracle.normwise_rel_err(got, ref)}
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

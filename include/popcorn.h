@@ -1,0 +1,120 @@
+/*
+ * popcorn.h -- C ABI of the int8 weight-only dequant-matmul path, built for
+ * NVIDIA B200 (sm_100a).
+ *
+ * Every declaration below has the same name, parameter list, parameter
+ * meaning, status codes and enumerator values as popcorn's public header
+ * (popcorn include/popcorn.h), so a cgo or C caller that was built against
+ * popcorn links against this library without source changes. Only the
+ * quantized-linear subset of popcorn's ABI is provided here; the other popcorn
+ * operators (elementwise, norms, backward, optimizer) are not part of this
+ * library.
+ *
+ * Conventions shared by every entry point:
+ *   - all buffers are device pointers owned by the caller;
+ *   - a null buffer pointer returns POPCORN_ERROR_INVALID_VALUE before any
+ *     size is looked at;
+ *   - any size <= 0 is a no-op that returns POPCORN_SUCCESS;
+ *   - work is enqueued asynchronously on `stream` (NULL = legacy default
+ *     stream); only launch-time CUDA errors are reported, and the CUDA error
+ *     code behind a POPCORN_ERROR_CUDA is kept per host thread.
+ */
+#ifndef POPCORN_H
+#define POPCORN_H
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (popcorn include/popcorn.h:11-16). */
+typedef enum {
+    POPCORN_SUCCESS = 0,
+    POPCORN_ERROR_INVALID_VALUE = 1,
+    POPCORN_ERROR_CUDA = 2,
+} popcornStatus_t;
+
+/* Short description of a status code (popcorn include/popcorn.h:19,
+ * src/unary.cu:91-102). */
+const char* popcornGetErrorString(popcornStatus_t status);
+
+/* The CUDA error behind the most recent POPCORN_ERROR_CUDA returned on the
+ * calling host thread; cudaSuccess if there was none (popcorn
+ * include/popcorn.h:21-23, src/common.cuh:16-27). */
+cudaError_t popcornGetLastCudaError(void);
+
+/* cudaGetErrorString() of popcornGetLastCudaError() (popcorn
+ * include/popcorn.h:25-27, src/unary.cu:104-110). */
+const char* popcornGetLastCudaErrorString(void);
+
+/*
+ * out[m, n] = sum_k x[m, k] * (qweight[n, k] * scale[n])
+ *
+ * Replaces popcorn's popcornDequantizeMatmul_i8f32 (include/popcorn.h:464-473,
+ * src/quantize.cu:86-112). x is row-major [M, K] f32, qweight is row-major
+ * [N, K] int8 (one row per output channel), scale is [N] f32 and out is
+ * row-major [M, N] f32. Accumulation is f32. Small problems and M <= 4 run on
+ * an f32 CUDA-core path; large problems run on the tcgen05 tensor-core path,
+ * whose activations are rounded to f16 after a per-row power-of-two
+ * rescaling (normwise relative error well below 2e-3).
+ */
+popcornStatus_t popcornDequantizeMatmul_i8f32(
+    float* out,
+    const float* x,
+    const int8_t* qweight,
+    const float* scale,
+    int64_t M,
+    int64_t N,
+    int64_t K,
+    cudaStream_t stream
+);
+
+/*
+ * Batched form with weights shared across the batch:
+ * out[b, m, n] = sum_k x[b, m, k] * (qweight[n, k] * scale[n]).
+ *
+ * Replaces popcorn's popcornDequantizeMatmulBatched_i8f32
+ * (include/popcorn.h:491-501, src/quantize.cu:300-327). x is contiguous
+ * [B, M, K] and out contiguous [B, M, N], so the call is the single matmul
+ * above with B*M rows; the weights are streamed once, not once per batch.
+ */
+popcornStatus_t popcornDequantizeMatmulBatched_i8f32(
+    float* out,
+    const float* x,
+    const int8_t* qweight,
+    const float* scale,
+    int64_t B,
+    int64_t M,
+    int64_t N,
+    int64_t K,
+    cudaStream_t stream
+);
+
+/*
+ * Symmetric per-output-channel int8 quantization of a row-major [N, K] f32
+ * matrix:
+ *   scale[n]  = max_k |input[n, k]| / 127   (1.0 when that maximum is 0)
+ *   out[n, k] = rint(input[n, k] / scale[n]) clamped to [-128, 127]
+ *
+ * Replaces popcorn's popcornQuantize_f32i8 (include/popcorn.h:527-534,
+ * src/quantize.cu:452-565). Codes and scales are bit-identical to popcorn's
+ * GPU kernels (IEEE division, round-half-to-even, NaN skipped by the row
+ * maximum). Unlike popcorn's version it allocates no temporary device memory
+ * and does not synchronize the device, so it is stream-ordered.
+ */
+popcornStatus_t popcornQuantize_f32i8(
+    int8_t* out,
+    float* scale,
+    const float* input,
+    int64_t N,
+    int64_t K,
+    cudaStream_t stream
+);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* POPCORN_H */

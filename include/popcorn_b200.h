@@ -1,0 +1,89 @@
+/*
+ * popcorn_b200.h -- entry points that this B200 build adds beside the popcorn
+ * ABI in popcorn.h. None of them changes or replaces a popcorn entry point.
+ * Conventions (device pointers, null -> POPCORN_ERROR_INVALID_VALUE, sizes
+ * <= 0 -> no-op, asynchronous on `stream`) are those of popcorn.h.
+ */
+#ifndef POPCORN_B200_H
+#define POPCORN_B200_H
+
+#include "popcorn.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Kernel paths of the dequant-matmul. */
+typedef enum {
+    /* What popcornDequantizeMatmul_i8f32 picks for the shape and pointers. */
+    POPCORN_MATMUL_PATH_AUTO = 0,
+    /* f32 CUDA-core path: int8 codes are widened exactly to f32 and every
+     * product is accumulated in f32 (max relative error ~1e-6 normwise).
+     * Runs any shape and any alignment. */
+    POPCORN_MATMUL_PATH_SIMT_F32 = 1,
+    /* tcgen05 tensor-core path: codes become f16 (exact), each activation row
+     * is rescaled by a power of two and rounded to f16, products accumulate
+     * in f32 in tensor memory. Needs K % 16 == 0 and 16-byte aligned x and
+     * qweight. */
+    POPCORN_MATMUL_PATH_TENSOR_F16 = 2,
+} popcornMatmulPath_t;
+
+/*
+ * Dequantize (expand) per-channel int8 weights to f32:
+ *   out[n, k] = (float)qweight[n, k] * scale[n]
+ * popcorn has no kernel for this; the arithmetic is the per-element weight
+ * expansion inside popcorn's fused matmul (src/quantize.cu:71) and in its
+ * round-trip test (test/test_quantize.cu:996-1000). Results are bit-exact.
+ */
+popcornStatus_t popcornDequantize_i8f32(
+    float* out,
+    const int8_t* qweight,
+    const float* scale,
+    int64_t N,
+    int64_t K,
+    cudaStream_t stream
+);
+
+/*
+ * popcornDequantizeMatmul_i8f32 with the kernel path chosen by the caller.
+ * Returns POPCORN_ERROR_INVALID_VALUE when `path` cannot run this shape or
+ * these pointers (for example the tensor path with K % 16 != 0).
+ */
+popcornStatus_t popcornDequantizeMatmulPath_i8f32(
+    float* out,
+    const float* x,
+    const int8_t* qweight,
+    const float* scale,
+    int64_t M,
+    int64_t N,
+    int64_t K,
+    popcornMatmulPath_t path,
+    cudaStream_t stream
+);
+
+/* The path popcornDequantizeMatmul_i8f32 takes for these sizes and pointers
+ * (never POPCORN_MATMUL_PATH_AUTO). Pure host function, launches nothing. */
+popcornMatmulPath_t popcornDequantizeMatmulSelectPath(
+    const float* x,
+    const int8_t* qweight,
+    int64_t M,
+    int64_t N,
+    int64_t K
+);
+
+/* Number of kernel launches the call with these arguments enqueues (0 for a
+ * no-op or an argument error). Pure host function. */
+int popcornDequantizeMatmulLaunchCount(
+    const float* x,
+    const int8_t* qweight,
+    int64_t M,
+    int64_t N,
+    int64_t K,
+    popcornMatmulPath_t path
+);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* POPCORN_B200_H */

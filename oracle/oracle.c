@@ -1,0 +1,157 @@
+/*
+ * CPU oracle of popcorn's int8 dequant-matmul path -- TEST INFRASTRUCTURE,
+ * never part of the product path. See oracle.h for what each function
+ * restates and how the restatement is pinned to the reference.
+ *
+ * Build flags matter for bit-exactness: -ffp-contract=off keeps the
+ * unfused variant's multiply and add separately rounded.
+ */
+#include "oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+
+void oracle_dequant_matmul_i8(float* out, const float* x, const int8_t* q, const float* scale,
+                              int64_t M, int64_t N, int64_t K, int fused) {
+    /* popcorn test/test_quantize.cu:31-39 and src/quantize.cu:47-83: for each
+     * output, walk k upward, widen the code, multiply by the channel scale,
+     * then multiply-add with the activation. */
+    for (int64_t m = 0; m < M; m++) {
+        const float* xr = x + m * K;
+        for (int64_t n = 0; n < N; n++) {
+            const int8_t* qr = q + n * K;
+            const float sc = scale[n];
+            float acc = 0.0f;
+            if (fused) {
+                for (int64_t k = 0; k < K; k++) {
+                    const float w = (float)qr[k] * sc;
+                    acc = fmaf(xr[k], w, acc);
+                }
+            } else {
+                for (int64_t k = 0; k < K; k++) {
+                    const float w = (float)qr[k] * sc;
+                    const float p = xr[k] * w;
+                    acc = acc + p;
+                }
+            }
+            out[m * N + n] = acc;
+        }
+    }
+}
+
+typedef struct {
+    float* out;
+    const float* x;
+    const int8_t* q;
+    const float* scale;
+    int64_t M, N, K, n0, n1;
+    int fused;
+} mm_job;
+
+static void* mm_worker(void* arg) {
+    const mm_job* j = (const mm_job*)arg;
+    for (int64_t m = 0; m < j->M; m++) {
+        /* One activation row against this thread's channel range; the output
+         * row pointer is offset so the layout stays [M, N]. */
+        for (int64_t n = j->n0; n < j->n1; n++) {
+            const int8_t* qr = j->q + n * j->K;
+            const float* xr = j->x + m * j->K;
+            const float sc = j->scale[n];
+            float acc = 0.0f;
+            if (j->fused) {
+                for (int64_t k = 0; k < j->K; k++) acc = fmaf(xr[k], (float)qr[k] * sc, acc);
+            } else {
+                for (int64_t k = 0; k < j->K; k++) {
+                    const float w = (float)qr[k] * sc;
+                    const float p = xr[k] * w;
+                    acc = acc + p;
+                }
+            }
+            j->out[m * j->N + n] = acc;
+        }
+    }
+    return NULL;
+}
+
+void oracle_dequant_matmul_i8_mt(float* out, const float* x, const int8_t* q, const float* scale,
+                                 int64_t M, int64_t N, int64_t K, int fused, int threads) {
+    if (threads < 1) threads = 1;
+    if (threads > N) threads = (int)N;
+    if (threads <= 1) {
+        oracle_dequant_matmul_i8(out, x, q, scale, M, N, K, fused);
+        return;
+    }
+    pthread_t* tid = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)threads);
+    mm_job* jobs = (mm_job*)malloc(sizeof(mm_job) * (size_t)threads);
+    for (int t = 0; t < threads; t++) {
+        jobs[t].out = out;
+        jobs[t].x = x;
+        jobs[t].q = q;
+        jobs[t].scale = scale;
+        jobs[t].M = M;
+        jobs[t].N = N;
+        jobs[t].K = K;
+        jobs[t].n0 = N * t / threads;
+        jobs[t].n1 = N * (t + 1) / threads;
+        jobs[t].fused = fused;
+        pthread_create(&tid[t], NULL, mm_worker, &jobs[t]);
+    }
+    for (int t = 0; t < threads; t++) pthread_join(tid[t], NULL);
+    free(jobs);
+    free(tid);
+}
+
+void oracle_quantize_i8(int8_t* out, float* scale, const float* in, int64_t N, int64_t K, int ties) {
+    for (int64_t n = 0; n < N; n++) {
+        const float* r = in + n * K;
+        /* Row max of |v|: NaN fails the compare and is skipped
+         * (src/quantize.cu:470-477, test/test_quantize.cu:686-691). */
+        float max_abs = 0.0f;
+        for (int64_t k = 0; k < K; k++) {
+            const float v = r[k];
+            const float a = v < 0 ? -v : v;
+            if (a > max_abs) max_abs = a;
+        }
+        float sc = max_abs / 127.0f;
+        if (sc == 0.0f) sc = 1.0f;
+        scale[n] = sc;
+        for (int64_t k = 0; k < K; k++) {
+            const float d = r[k] / sc;
+            float qv = ties ? roundf(d) : rintf(d);
+            if (qv > 127.0f) qv = 127.0f;
+            if (qv < -128.0f) qv = -128.0f;
+            /* A NaN code converts to 0 on the GPU (PTX float->int conversion
+             * maps NaN to 0); state it explicitly rather than rely on the
+             * host compiler's undefined cast. */
+            out[n * K + k] = (qv != qv) ? (int8_t)0 : (int8_t)qv;
+        }
+    }
+}
+
+void oracle_dequantize_i8(float* out, const int8_t* q, const float* scale, int64_t N, int64_t K) {
+    for (int64_t n = 0; n < N; n++) {
+        const float sc = scale[n];
+        for (int64_t k = 0; k < K; k++) out[n * K + k] = (float)q[n * K + k] * sc;
+    }
+}
+
+static uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+void oracle_fill_normal(float* out, int64_t n, uint64_t seed, float sigma) {
+    const double s = (double)sigma;
+    for (int64_t i = 0; i < n; i++) {
+        double acc = 0.0;
+        for (int j = 0; j < 12; j++) {
+            const uint64_t z = splitmix64(seed + (uint64_t)(12 * i + j) * 0x9E3779B97F4A7C15ull);
+            /* 24-bit uniform, centred in its cell: ((z >> 40) + 0.5) / 2^24. */
+            acc += ((double)(z >> 40) + 0.5) * (1.0 / 16777216.0);
+        }
+        out[i] = (float)((acc - 6.0) * s);
+    }
+}

@@ -1,0 +1,53 @@
+/*
+ * CPU oracle of popcorn's int8 dequant-matmul path -- TEST INFRASTRUCTURE.
+ *
+ * Only the tests, the smoke check and the benchmark's CPU-baseline leg use
+ * this library, and only as the checker / baseline; the product path never
+ * links or calls it. Parity is pinned: the restatement is checked against
+ * the reference's own CPU loops (built from popcorn's sources into
+ * oracle/_ref by oracle/Makefile) and against golden vectors made by those
+ * loops (tests/golden), and on the GPU against popcorn's own CUDA kernels
+ * rebuilt for sm_100a.
+ */
+#ifndef POPCORN_ORACLE_H
+#define POPCORN_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* out[m,n] = sum_k x[m,k] * ((float)q[n,k] * scale[n]), k ascending, f32.
+ * fused = 0: product and sum rounded separately, as popcorn's test loop
+ *            (test/test_quantize.cu:24-41) compiles on x86-64;
+ * fused = 1: acc = fmaf(x, w, acc), as popcorn's GPU kernel executes
+ *            (src/quantize.cu:69-73, nvcc contracts the multiply-add). */
+void oracle_dequant_matmul_i8(float* out, const float* x, const int8_t* q, const float* scale,
+                              int64_t M, int64_t N, int64_t K, int fused);
+
+/* Same arithmetic split over `threads` POSIX threads by output channel. */
+void oracle_dequant_matmul_i8_mt(float* out, const float* x, const int8_t* q, const float* scale,
+                                 int64_t M, int64_t N, int64_t K, int fused, int threads);
+
+/* Per-row symmetric int8 quantization (src/quantize.cu:458-528).
+ * ties = 0: rintf (half to even), popcorn's GPU kernel (:524);
+ * ties = 1: roundf (half away from zero), popcorn's test loop
+ *           (test/test_quantize.cu:700). */
+void oracle_quantize_i8(int8_t* out, float* scale, const float* in, int64_t N, int64_t K, int ties);
+
+/* out[n,k] = (float)q[n,k] * scale[n]. */
+void oracle_dequantize_i8(float* out, const int8_t* q, const float* scale, int64_t N, int64_t K);
+
+/* Deterministic synthetic data: SplitMix64 stream (Steele, Lea & Flood 2014)
+ * feeding an Irwin-Hall(12) normal approximation, sum of twelve 24-bit
+ * uniforms minus 6, scaled by sigma. Integer and exactly-rounded float
+ * arithmetic only, so every IEEE-754 machine produces the same bits.
+ * Element i of a stream seeded `seed` depends only on (seed, i). */
+void oracle_fill_normal(float* out, int64_t n, uint64_t seed, float sigma);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* POPCORN_ORACLE_H */

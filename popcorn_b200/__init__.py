@@ -1,0 +1,215 @@
+"""popcorn_b200 -- host-side mirror of popcorn's int8 dequant-matmul C ABI.
+
+The product is the sm_100a library ``popcorn_b200/libpopcorn.so`` (and the
+static archive ``lib/libpopcorn.a`` for cgo callers), built from
+``popcorn_b200/csrc`` by ``make -C popcorn_b200``. This module loads that
+library in-tree through ctypes and exposes
+
+* the raw entry points under popcorn's own names (``popcornDequantizeMatmul_i8f32``
+  and friends), taking device pointers as integers and returning the
+  ``popcornStatus_t`` value, exactly as a cgo caller sees them
+  (popcorn include/popcorn.h:11-27, :464-534);
+* tensor-level helpers (``dequantize_matmul``, ``quantize``, ``dequantize``)
+  that take CUDA torch tensors, pass the current torch stream, and raise
+  :class:`PopcornError` on a non-success status, the way tendo turns a status
+  into a Go error (popcorn README.md:85-107).
+
+There is no fallback: if the library is missing, loading raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libpopcorn.so")
+
+POPCORN_SUCCESS = 0
+POPCORN_ERROR_INVALID_VALUE = 1
+POPCORN_ERROR_CUDA = 2
+
+PATH_AUTO = 0
+PATH_SIMT_F32 = 1
+PATH_TENSOR_F16 = 2
+PATH_NAMES = {PATH_AUTO: "auto", PATH_SIMT_F32: "simt_f32", PATH_TENSOR_F16: "tensor_f16"}
+
+# Every symbol declared in include/popcorn.h and include/popcorn_b200.h.
+ABI_SYMBOLS = (
+    "popcornGetErrorString",
+    "popcornGetLastCudaError",
+    "popcornGetLastCudaErrorString",
+    "popcornDequantizeMatmul_i8f32",
+    "popcornDequantizeMatmulBatched_i8f32",
+    "popcornQuantize_f32i8",
+)
+EXT_SYMBOLS = (
+    "popcornDequantize_i8f32",
+    "popcornDequantizeMatmulPath_i8f32",
+    "popcornDequantizeMatmulSelectPath",
+    "popcornDequantizeMatmulLaunchCount",
+)
+
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+
+_SIGNATURES = {
+    "popcornGetErrorString": (ctypes.c_char_p, [_int]),
+    "popcornGetLastCudaError": (_int, []),
+    "popcornGetLastCudaErrorString": (ctypes.c_char_p, []),
+    "popcornDequantizeMatmul_i8f32": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "popcornDequantizeMatmulBatched_i8f32": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "popcornQuantize_f32i8": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
+    "popcornDequantize_i8f32": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
+    "popcornDequantizeMatmulPath_i8f32": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
+    "popcornDequantizeMatmulSelectPath": (_int, [_vp, _vp, _i64, _i64, _i64]),
+    "popcornDequantizeMatmulLaunchCount": (_int, [_vp, _vp, _i64, _i64, _i64, _int]),
+}
+
+_lib = None
+
+
+class PopcornError(RuntimeError):
+    """A non-success popcornStatus_t, with the CUDA error behind it if any."""
+
+    def __init__(self, status: int, where: str):
+        lib = load_library()
+        msg = lib.popcornGetErrorString(status).decode()
+        self.status = status
+        self.cuda_error = None
+        if status == POPCORN_ERROR_CUDA:
+            self.cuda_error = lib.popcornGetLastCudaError()
+            msg += ": " + lib.popcornGetLastCudaErrorString().decode()
+        super().__init__(f"{where}: {msg}")
+
+
+def load_library(path: str | None = None) -> ctypes.CDLL:
+    """Load the in-tree sm_100a library (raises OSError if it is not built)."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = path or LIB_PATH
+    if not os.path.exists(p):
+        raise OSError(f"popcorn_b200 library not built: {p} (run `make -C popcorn_b200`)")
+    lib = ctypes.CDLL(p)
+    for name, (res, args) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def _stream_handle(stream) -> int | None:
+    if stream is None:
+        import torch
+
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+# ---------------------------------------------------------------------------
+# Raw entry points: device pointers as ints, popcornStatus_t returned.
+# ---------------------------------------------------------------------------
+def popcornDequantizeMatmul_i8f32(out, x, qweight, scale, M, N, K, stream=0) -> int:
+    return load_library().popcornDequantizeMatmul_i8f32(out, x, qweight, scale, M, N, K, stream)
+
+
+def popcornDequantizeMatmulBatched_i8f32(out, x, qweight, scale, B, M, N, K, stream=0) -> int:
+    return load_library().popcornDequantizeMatmulBatched_i8f32(out, x, qweight, scale, B, M, N, K, stream)
+
+
+def popcornQuantize_f32i8(out, scale, inp, N, K, stream=0) -> int:
+    return load_library().popcornQuantize_f32i8(out, scale, inp, N, K, stream)
+
+
+def popcornDequantize_i8f32(out, qweight, scale, N, K, stream=0) -> int:
+    return load_library().popcornDequantize_i8f32(out, qweight, scale, N, K, stream)
+
+
+def popcornDequantizeMatmulPath_i8f32(out, x, qweight, scale, M, N, K, path, stream=0) -> int:
+    return load_library().popcornDequantizeMatmulPath_i8f32(out, x, qweight, scale, M, N, K, path, stream)
+
+
+def select_path(x_ptr: int, q_ptr: int, M: int, N: int, K: int) -> int:
+    return load_library().popcornDequantizeMatmulSelectPath(x_ptr, q_ptr, M, N, K)
+
+
+def launch_count(x_ptr: int, q_ptr: int, M: int, N: int, K: int, path: int = PATH_AUTO) -> int:
+    return load_library().popcornDequantizeMatmulLaunchCount(x_ptr, q_ptr, M, N, K, path)
+
+
+def _check(status: int, where: str) -> None:
+    if status != POPCORN_SUCCESS:
+        raise PopcornError(status, where)
+
+
+# ---------------------------------------------------------------------------
+# Tensor helpers (CUDA torch tensors, contiguous).
+# ---------------------------------------------------------------------------
+def dequantize_matmul(x, qweight, scale, out=None, path: int = PATH_AUTO, stream=None):
+    """out[M, N] = x[M, K] @ (qweight[N, K] * scale[N, None]).T in f32."""
+    import torch
+
+    M, K = x.shape
+    N = qweight.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    st = _stream_handle(stream)
+    _check(
+        popcornDequantizeMatmulPath_i8f32(
+            out.data_ptr(), x.data_ptr(), qweight.data_ptr(), scale.data_ptr(), M, N, K, path, st
+        ),
+        "popcornDequantizeMatmulPath_i8f32",
+    )
+    return out
+
+
+def dequantize_matmul_batched(x, qweight, scale, out=None, stream=None):
+    """out[B, M, N] = x[B, M, K] @ (qweight * scale[:, None]).T in f32."""
+    import torch
+
+    B, M, K = x.shape
+    N = qweight.shape[0]
+    if out is None:
+        out = torch.empty((B, M, N), dtype=torch.float32, device=x.device)
+    st = _stream_handle(stream)
+    _check(
+        popcornDequantizeMatmulBatched_i8f32(
+            out.data_ptr(), x.data_ptr(), qweight.data_ptr(), scale.data_ptr(), B, M, N, K, st
+        ),
+        "popcornDequantizeMatmulBatched_i8f32",
+    )
+    return out
+
+
+def quantize(w, out=None, scale=None, stream=None):
+    """Per-row symmetric int8 quantization of f32 [N, K] -> (codes, scales)."""
+    import torch
+
+    N, K = w.shape
+    if out is None:
+        out = torch.empty((N, K), dtype=torch.int8, device=w.device)
+    if scale is None:
+        scale = torch.empty((N,), dtype=torch.float32, device=w.device)
+    st = _stream_handle(stream)
+    _check(popcornQuantize_f32i8(out.data_ptr(), scale.data_ptr(), w.data_ptr(), N, K, st), "popcornQuantize_f32i8")
+    return out, scale
+
+
+def dequantize(qweight, scale, out=None, stream=None):
+    """f32 [N, K] = qweight[N, K] * scale[N, None]."""
+    import torch
+
+    N, K = qweight.shape
+    if out is None:
+        out = torch.empty((N, K), dtype=torch.float32, device=qweight.device)
+    st = _stream_handle(stream)
+    _check(
+        popcornDequantize_i8f32(out.data_ptr(), qweight.data_ptr(), scale.data_ptr(), N, K, st),
+        "popcornDequantize_i8f32",
+    )
+    return out

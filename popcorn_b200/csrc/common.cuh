@@ -1,0 +1,56 @@
+// Shared host/device plumbing of the B200 dequant-matmul library.
+//
+// Status handling follows popcorn's convention (src/common.cuh:16-27): a CUDA
+// failure becomes POPCORN_ERROR_CUDA and the CUDA error code is remembered per
+// host thread for popcornGetLastCudaError().
+#ifndef POPCORN_B200_COMMON_CUH
+#define POPCORN_B200_COMMON_CUH
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "popcorn.h"
+#include "popcorn_b200.h"
+
+namespace pcb {
+
+// Number of streaming multiprocessors on a B200.
+constexpr int kB200Sms = 148;
+
+// Records `err` for popcornGetLastCudaError() and maps it to a status.
+popcornStatus_t record_cuda(cudaError_t err);
+
+// Launch-time check after a kernel launch: picks up launch-configuration
+// errors (and, like popcorn, any sticky error left on the context).
+inline popcornStatus_t check_launch() { return record_cuda(cudaGetLastError()); }
+
+inline bool aligned16(const void* p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Streaming-multiprocessor count of the current device (cached per device).
+int device_sm_count();
+
+// ---------------------------------------------------------------------------
+// Kernel-path entry points (implemented in gemv.cu / tc_gemm.cu).
+// Each takes already validated arguments (non-null, all sizes > 0).
+// ---------------------------------------------------------------------------
+
+// f32 CUDA-core path, any shape and alignment.
+popcornStatus_t simt_dequant_matmul(float* out, const float* x, const int8_t* q,
+                                    const float* scale, int64_t M, int64_t N,
+                                    int64_t K, cudaStream_t stream);
+int simt_launch_count(const float* x, const int8_t* q, int64_t M, int64_t N, int64_t K);
+
+// tcgen05 path; requires tc_supported(...).
+bool tc_supported(const float* x, const int8_t* q, int64_t M, int64_t N, int64_t K);
+popcornStatus_t tc_dequant_matmul(float* out, const float* x, const int8_t* q,
+                                  const float* scale, int64_t M, int64_t N,
+                                  int64_t K, cudaStream_t stream);
+int tc_launch_count(int64_t M, int64_t N, int64_t K);
+
+}  // namespace pcb
+
+#endif  // POPCORN_B200_COMMON_CUH

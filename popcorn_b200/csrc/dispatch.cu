@@ -1,0 +1,93 @@
+// popcorn ABI entry points of the dequant-matmul and the path selection.
+//
+// Argument handling is popcorn's (src/quantize.cu:96-102, :311-317): null
+// buffers -> POPCORN_ERROR_INVALID_VALUE, checked before sizes; any size <= 0
+// -> POPCORN_SUCCESS without work; launch errors -> POPCORN_ERROR_CUDA.
+#include "common.cuh"
+
+namespace pcb {
+namespace {
+
+// Below this many multiply-adds a call is launch-bound on any path, so it
+// stays on the f32 path, whose results match popcorn's to f32 rounding.
+constexpr int64_t kTensorMinMacs = int64_t(1) << 27;
+// Up to this many activation rows the CUDA cores keep up with HBM.
+constexpr int64_t kSimtMaxRows = 4;
+
+bool mul_overflows(int64_t a, int64_t b) {
+    return a != 0 && b > INT64_MAX / a;
+}
+
+popcornMatmulPath_t select_path(const float* x, const int8_t* q, int64_t M, int64_t N, int64_t K) {
+    if (M > kSimtMaxRows && !mul_overflows(M, N) && !mul_overflows(M * N, K) &&
+        M * N * K >= kTensorMinMacs && tc_supported(x, q, M, N, K)) {
+        return POPCORN_MATMUL_PATH_TENSOR_F16;
+    }
+    return POPCORN_MATMUL_PATH_SIMT_F32;
+}
+
+popcornStatus_t run(float* out, const float* x, const int8_t* q, const float* scale,
+                    int64_t M, int64_t N, int64_t K, popcornMatmulPath_t path, cudaStream_t stream) {
+    if (path == POPCORN_MATMUL_PATH_AUTO) path = select_path(x, q, M, N, K);
+    switch (path) {
+        case POPCORN_MATMUL_PATH_SIMT_F32:
+            return simt_dequant_matmul(out, x, q, scale, M, N, K, stream);
+        case POPCORN_MATMUL_PATH_TENSOR_F16:
+            if (!tc_supported(x, q, M, N, K)) return POPCORN_ERROR_INVALID_VALUE;
+            return tc_dequant_matmul(out, x, q, scale, M, N, K, stream);
+        default:
+            return POPCORN_ERROR_INVALID_VALUE;
+    }
+}
+
+}  // namespace
+}  // namespace pcb
+
+extern "C" popcornStatus_t popcornDequantizeMatmul_i8f32(float* out, const float* x, const int8_t* qweight,
+                                                         const float* scale, int64_t M, int64_t N, int64_t K,
+                                                         cudaStream_t stream) {
+    if (out == nullptr || x == nullptr || qweight == nullptr || scale == nullptr) {
+        return POPCORN_ERROR_INVALID_VALUE;
+    }
+    if (M <= 0 || N <= 0 || K <= 0) return POPCORN_SUCCESS;
+    return pcb::run(out, x, qweight, scale, M, N, K, POPCORN_MATMUL_PATH_AUTO, stream);
+}
+
+extern "C" popcornStatus_t popcornDequantizeMatmulBatched_i8f32(float* out, const float* x, const int8_t* qweight,
+                                                                const float* scale, int64_t B, int64_t M, int64_t N,
+                                                                int64_t K, cudaStream_t stream) {
+    if (out == nullptr || x == nullptr || qweight == nullptr || scale == nullptr) {
+        return POPCORN_ERROR_INVALID_VALUE;
+    }
+    if (B <= 0 || M <= 0 || N <= 0 || K <= 0) return POPCORN_SUCCESS;
+    if (pcb::mul_overflows(B, M)) return POPCORN_ERROR_INVALID_VALUE;
+    // x is contiguous [B, M, K] and out contiguous [B, M, N]: one matmul over
+    // B*M rows reads the shared weights once instead of once per batch.
+    return pcb::run(out, x, qweight, scale, B * M, N, K, POPCORN_MATMUL_PATH_AUTO, stream);
+}
+
+extern "C" popcornStatus_t popcornDequantizeMatmulPath_i8f32(float* out, const float* x, const int8_t* qweight,
+                                                             const float* scale, int64_t M, int64_t N, int64_t K,
+                                                             popcornMatmulPath_t path, cudaStream_t stream) {
+    if (out == nullptr || x == nullptr || qweight == nullptr || scale == nullptr) {
+        return POPCORN_ERROR_INVALID_VALUE;
+    }
+    if (M <= 0 || N <= 0 || K <= 0) return POPCORN_SUCCESS;
+    return pcb::run(out, x, qweight, scale, M, N, K, path, stream);
+}
+
+extern "C" popcornMatmulPath_t popcornDequantizeMatmulSelectPath(const float* x, const int8_t* qweight,
+                                                                 int64_t M, int64_t N, int64_t K) {
+    if (M <= 0 || N <= 0 || K <= 0) return POPCORN_MATMUL_PATH_SIMT_F32;
+    return pcb::select_path(x, qweight, M, N, K);
+}
+
+extern "C" int popcornDequantizeMatmulLaunchCount(const float* x, const int8_t* qweight, int64_t M, int64_t N,
+                                                  int64_t K, popcornMatmulPath_t path) {
+    if (x == nullptr || qweight == nullptr || M <= 0 || N <= 0 || K <= 0) return 0;
+    if (path == POPCORN_MATMUL_PATH_AUTO) path = pcb::select_path(x, qweight, M, N, K);
+    if (path == POPCORN_MATMUL_PATH_TENSOR_F16) {
+        return pcb::tc_supported(x, qweight, M, N, K) ? pcb::tc_launch_count(M, N, K) : 0;
+    }
+    return pcb::simt_launch_count(x, qweight, M, N, K);
+}

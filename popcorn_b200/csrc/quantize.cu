@@ -1,0 +1,176 @@
+// Per-output-channel int8 quantize and dequantize (expand) kernels.
+//
+// Quantize follows popcorn's two-kernel algorithm (src/quantize.cu:458-528):
+// row maximum of |w| with NaN skipped (the `abs_v > max` compare, :473-476),
+// scale = max / 127 with 0 mapped to 1 (:513-515), code = rint(w / scale)
+// clamped to [-128, 127] (:523-527). Here both steps run in one kernel, one
+// warp per row, so no temporary buffer, no cudaMalloc/cudaFree and no device
+// synchronisation is needed (popcorn allocates one, :547-562). The division
+// and rint are the IEEE round-to-nearest-even operations popcorn uses, so
+// codes and scales are bit-identical.
+//
+// Traffic per element: 4 B read from HBM (the second pass over a row is served
+// by L2), 1 B written; plus 4 B per row for the scale.
+#include "common.cuh"
+
+namespace pcb {
+namespace {
+
+constexpr int kQuantThreads = 256;
+constexpr int kWarpsPerBlock = kQuantThreads / 32;
+
+__device__ __forceinline__ float absmax_step(float m, float v) {
+    float a = fabsf(v);
+    // NaN compares false and is skipped, exactly like popcorn's `abs_v > max`.
+    return (a > m) ? a : m;
+}
+
+__device__ __forceinline__ int8_t quantize_one(float v, float sc) {
+    float q = rintf(v / sc);
+    if (q > 127.0f) q = 127.0f;
+    if (q < -128.0f) q = -128.0f;
+    return static_cast<int8_t>(q);
+}
+
+// kVec: K % 16 == 0 and both row bases 16-byte aligned; each lane then owns
+// 16 consecutive elements per step (four 16-byte loads, one 16-byte store).
+template <bool kVec>
+__global__ void __launch_bounds__(kQuantThreads)
+quantize_rows_kernel(int8_t* __restrict__ out, float* __restrict__ scale,
+                     const float* __restrict__ in, int64_t N, int64_t K) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock) + (threadIdx.x >> 5);
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarpsPerBlock;
+
+    for (int64_t row = warp; row < N; row += nwarps) {
+        const float* r = in + row * K;
+        int8_t* o = out + row * K;
+
+        float m = 0.0f;
+        if (kVec) {
+            const float4* r4 = reinterpret_cast<const float4*>(r);
+            const int64_t n4 = K >> 2;
+            #pragma unroll 4
+            for (int64_t i = lane; i < n4; i += 32) {
+                float4 v = __ldg(r4 + i);
+                m = absmax_step(m, v.x);
+                m = absmax_step(m, v.y);
+                m = absmax_step(m, v.z);
+                m = absmax_step(m, v.w);
+            }
+        } else {
+            for (int64_t k = lane; k < K; k += 32) m = absmax_step(m, __ldg(r + k));
+        }
+        #pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            float other = __shfl_xor_sync(0xffffffffu, m, off);
+            m = (other > m) ? other : m;
+        }
+
+        float sc = m / 127.0f;
+        if (sc == 0.0f) sc = 1.0f;
+        if (lane == 0) scale[row] = sc;
+
+        if (kVec) {
+            const float4* r4 = reinterpret_cast<const float4*>(r);
+            uint4* o16 = reinterpret_cast<uint4*>(o);
+            const int64_t n16 = K >> 4;
+            for (int64_t c = lane; c < n16; c += 32) {
+                uint32_t w[4];
+                #pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float4 v = __ldg(r4 + c * 4 + j);
+                    uint32_t b0 = static_cast<uint8_t>(quantize_one(v.x, sc));
+                    uint32_t b1 = static_cast<uint8_t>(quantize_one(v.y, sc));
+                    uint32_t b2 = static_cast<uint8_t>(quantize_one(v.z, sc));
+                    uint32_t b3 = static_cast<uint8_t>(quantize_one(v.w, sc));
+                    w[j] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+                }
+                o16[c] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        } else {
+            for (int64_t k = lane; k < K; k += 32) o[k] = quantize_one(__ldg(r + k), sc);
+        }
+    }
+}
+
+// out[n, k] = float(q[n, k]) * scale[n]; kVec: K % 16 == 0 and aligned bases,
+// each thread expands 16 codes (one 16-byte load, four 16-byte stores).
+template <bool kVec>
+__global__ void __launch_bounds__(256)
+dequantize_kernel(float* __restrict__ out, const int8_t* __restrict__ q,
+                  const float* __restrict__ scale, int64_t N, int64_t K) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (kVec) {
+        const int64_t per_row = K >> 4;
+        const int64_t total = N * per_row;
+        for (; t < total; t += stride) {
+            const int64_t row = t / per_row;
+            const float sc = __ldg(scale + row);
+            const uint4 packed = __ldg(reinterpret_cast<const uint4*>(q) + t);
+            const uint32_t w[4] = {packed.x, packed.y, packed.z, packed.w};
+            float4* o = reinterpret_cast<float4*>(out) + t * 4;
+            #pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float4 v;
+                v.x = static_cast<float>(static_cast<int8_t>(w[j] & 0xffu)) * sc;
+                v.y = static_cast<float>(static_cast<int8_t>((w[j] >> 8) & 0xffu)) * sc;
+                v.z = static_cast<float>(static_cast<int8_t>((w[j] >> 16) & 0xffu)) * sc;
+                v.w = static_cast<float>(static_cast<int8_t>(w[j] >> 24)) * sc;
+                o[j] = v;
+            }
+        }
+    } else {
+        const int64_t total = N * K;
+        for (; t < total; t += stride) {
+            out[t] = static_cast<float>(q[t]) * __ldg(scale + t / K);
+        }
+    }
+}
+
+int grid_for(int64_t work_items, int threads) {
+    const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
+    int64_t g = ceil_div(work_items, threads);
+    if (g > cap) g = cap;
+    if (g < 1) g = 1;
+    return static_cast<int>(g);
+}
+
+}  // namespace
+}  // namespace pcb
+
+extern "C" popcornStatus_t popcornQuantize_f32i8(int8_t* out, float* scale, const float* input,
+                                                 int64_t N, int64_t K, cudaStream_t stream) {
+    using namespace pcb;
+    if (out == nullptr || scale == nullptr || input == nullptr) return POPCORN_ERROR_INVALID_VALUE;
+    if (N <= 0 || K <= 0) return POPCORN_SUCCESS;
+
+    const bool vec = (K % 16 == 0) && aligned16(input) && aligned16(out);
+    // One warp per row; at most 16 resident blocks per SM worth of warps, the
+    // grid-stride loop covers the rest.
+    int64_t blocks = ceil_div(N, kWarpsPerBlock);
+    const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
+    if (blocks > cap) blocks = cap;
+    if (vec) {
+        quantize_rows_kernel<true><<<static_cast<int>(blocks), kQuantThreads, 0, stream>>>(out, scale, input, N, K);
+    } else {
+        quantize_rows_kernel<false><<<static_cast<int>(blocks), kQuantThreads, 0, stream>>>(out, scale, input, N, K);
+    }
+    return check_launch();
+}
+
+extern "C" popcornStatus_t popcornDequantize_i8f32(float* out, const int8_t* qweight, const float* scale,
+                                                   int64_t N, int64_t K, cudaStream_t stream) {
+    using namespace pcb;
+    if (out == nullptr || qweight == nullptr || scale == nullptr) return POPCORN_ERROR_INVALID_VALUE;
+    if (N <= 0 || K <= 0) return POPCORN_SUCCESS;
+
+    const bool vec = (K % 16 == 0) && aligned16(qweight) && aligned16(out);
+    if (vec) {
+        dequantize_kernel<true><<<grid_for(N * (K / 16), 256), 256, 0, stream>>>(out, qweight, scale, N, K);
+    } else {
+        dequantize_kernel<false><<<grid_for(N * K, 256), 256, 0, stream>>>(out, qweight, scale, N, K);
+    }
+    return check_launch();
+}

@@ -1,0 +1,128 @@
+"""CPU: the C-ABI library loads, exports what include/*.h declares, and keeps
+popcorn's argument conventions for calls that launch nothing.
+
+popcorn's conventions (src/quantize.cu:96-102, :311-317, :538-544): a null
+buffer returns POPCORN_ERROR_INVALID_VALUE before sizes are looked at; any
+size <= 0 returns POPCORN_SUCCESS without work. These paths return before any
+CUDA call, so they run without a GPU.
+"""
+import os
+import re
+import subprocess
+
+import pytest
+
+import popcorn_b200 as pc
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADERS = [os.path.join(ROOT, "include", h) for h in ("popcorn.h", "popcorn_b200.h")]
+
+
+def declared_functions():
+    names = []
+    for h in HEADERS:
+        text = open(h).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names += re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(popcorn\w+)\s*\(", text, flags=re.M)
+    return sorted(set(names))
+
+
+def test_header_declarations_are_the_python_symbol_list():
+    assert declared_functions() == sorted(pc.ABI_SYMBOLS + pc.EXT_SYMBOLS)
+
+
+def test_popcorn_h_keeps_the_reference_signatures():
+    # The exact C prototypes popcorn declares for this path
+    # (include/popcorn.h:11-27, :464-473, :491-501, :527-534), whitespace-normalised.
+    text = re.sub(r"/\*.*?\*/", "", open(HEADERS[0]).read(), flags=re.S)
+    norm = " ".join(text.split())
+    for proto in [
+        "POPCORN_SUCCESS = 0, POPCORN_ERROR_INVALID_VALUE = 1, POPCORN_ERROR_CUDA = 2, } popcornStatus_t;",
+        "const char* popcornGetErrorString(popcornStatus_t status);",
+        "cudaError_t popcornGetLastCudaError(void);",
+        "const char* popcornGetLastCudaErrorString(void);",
+        "popcornStatus_t popcornDequantizeMatmul_i8f32( float* out, const float* x, const int8_t* qweight, "
+        "const float* scale, int64_t M, int64_t N, int64_t K, cudaStream_t stream );",
+        "popcornStatus_t popcornDequantizeMatmulBatched_i8f32( float* out, const float* x, const int8_t* qweight, "
+        "const float* scale, int64_t B, int64_t M, int64_t N, int64_t K, cudaStream_t stream );",
+        "popcornStatus_t popcornQuantize_f32i8( int8_t* out, float* scale, const float* input, int64_t N, "
+        "int64_t K, cudaStream_t stream );",
+    ]:
+        assert proto in norm, proto
+
+
+def test_shared_library_exports_every_declared_symbol(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_static_archive_exports_every_declared_symbol():
+    archive = os.path.join(ROOT, "lib", "libpopcorn.a")
+    assert os.path.exists(archive), "lib/libpopcorn.a not built"
+    out = subprocess.run(["nm", "-g", "--defined-only", archive], capture_output=True, text=True, check=True).stdout
+    defined = set(re.findall(r" T (\w+)$", out, flags=re.M))
+    for name in declared_functions():
+        assert name in defined, name
+
+
+def test_library_is_sm100a_only():
+    out = subprocess.run(["cuobjdump", "--list-elf", pc.LIB_PATH], capture_output=True, text=True)
+    if out.returncode != 0:
+        pytest.skip("cuobjdump unavailable")
+    archs = set(re.findall(r"sm_(\d+a?)", out.stdout))
+    assert archs == {"100a"}, archs
+
+
+def test_error_strings(lib):
+    assert lib.popcornGetErrorString(0) == b"success"
+    assert lib.popcornGetErrorString(1) == b"invalid value"
+    assert lib.popcornGetErrorString(2) == b"CUDA error"
+    assert lib.popcornGetErrorString(7) == b"unknown error"
+    assert lib.popcornGetLastCudaError() == 0
+    assert lib.popcornGetLastCudaErrorString() == b"no error"
+
+
+FAKE = 0x1000  # never dereferenced: these calls return before any CUDA work
+
+
+def test_null_pointers_are_invalid_before_sizes(lib):
+    for args in [(0, FAKE, FAKE, FAKE), (FAKE, 0, FAKE, FAKE), (FAKE, FAKE, 0, FAKE), (FAKE, FAKE, FAKE, 0)]:
+        assert lib.popcornDequantizeMatmul_i8f32(*args, 1, 1, 4, None) == pc.POPCORN_ERROR_INVALID_VALUE
+        assert lib.popcornDequantizeMatmul_i8f32(*args, 0, 0, 0, None) == pc.POPCORN_ERROR_INVALID_VALUE
+        assert lib.popcornDequantizeMatmulBatched_i8f32(*args, 1, 1, 1, 4, None) == pc.POPCORN_ERROR_INVALID_VALUE
+        assert lib.popcornDequantizeMatmulPath_i8f32(*args, 1, 1, 4, 0, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    for args in [(0, FAKE, FAKE), (FAKE, 0, FAKE), (FAKE, FAKE, 0)]:
+        assert lib.popcornQuantize_f32i8(*args, 1, 4, None) == pc.POPCORN_ERROR_INVALID_VALUE
+        assert lib.popcornDequantize_i8f32(*args, 1, 4, None) == pc.POPCORN_ERROR_INVALID_VALUE
+
+
+@pytest.mark.parametrize("sizes", [(0, 1, 1), (1, 0, 1), (1, 1, 0), (-1, 5, 5), (5, -3, 5), (5, 5, -9)])
+def test_nonpositive_sizes_are_noops(lib, sizes):
+    M, N, K = sizes
+    assert lib.popcornDequantizeMatmul_i8f32(FAKE, FAKE, FAKE, FAKE, M, N, K, None) == pc.POPCORN_SUCCESS
+    assert lib.popcornDequantizeMatmulBatched_i8f32(FAKE, FAKE, FAKE, FAKE, 1, M, N, K, None) == pc.POPCORN_SUCCESS
+    assert lib.popcornDequantizeMatmulBatched_i8f32(FAKE, FAKE, FAKE, FAKE, 0, 1, 1, 1, None) == pc.POPCORN_SUCCESS
+    if N <= 0 or K <= 0:
+        assert lib.popcornQuantize_f32i8(FAKE, FAKE, FAKE, N, K, None) == pc.POPCORN_SUCCESS
+        assert lib.popcornDequantize_i8f32(FAKE, FAKE, FAKE, N, K, None) == pc.POPCORN_SUCCESS
+    assert pc.launch_count(FAKE, FAKE, M, N, K) == 0
+
+
+def test_batched_size_overflow_is_rejected(lib):
+    big = 1 << 62
+    assert lib.popcornDequantizeMatmulBatched_i8f32(FAKE, FAKE, FAKE, FAKE, big, 4, 1, 1, None) == \
+        pc.POPCORN_ERROR_INVALID_VALUE
+
+
+def test_path_selection_rules():
+    a16 = 0x10000  # 16-byte aligned stand-in pointers
+    # Decode shapes stay on the f32 CUDA-core path.
+    assert pc.select_path(a16, a16, 1, 4096, 4096) == pc.PATH_SIMT_F32
+    assert pc.select_path(a16, a16, 4, 4096, 4096) == pc.PATH_SIMT_F32
+    # popcorn's own small test shapes stay on the f32 path (1e-5 absolute tolerance there).
+    assert pc.select_path(a16, a16, 64, 256, 128) == pc.PATH_SIMT_F32
+    # Unaligned pointers or K % 16 != 0 can never take the tensor path.
+    assert pc.select_path(a16 + 4, a16, 2048, 4096, 4096) == pc.PATH_SIMT_F32
+    assert pc.select_path(a16, a16 + 8, 2048, 4096, 4096) == pc.PATH_SIMT_F32
+    assert pc.select_path(a16, a16, 2048, 4096, 4100) == pc.PATH_SIMT_F32
+    assert pc.launch_count(a16, a16, 1, 4096, 4096) == 1

@@ -1,0 +1,324 @@
+"""GPU parity of the sm_100a library, called through its C ABI.
+
+Checks, in the spirit of popcorn's own suite (test/test_quantize.cu):
+* the reference suite's fixtures through popcornDequantizeMatmul_i8f32 /
+  ...Batched_i8f32 / popcornQuantize_f32i8 against golden vectors made by the
+  reference's CPU loops (absolute tolerance 1e-5 as in TOL_PERCHANNEL, :4);
+* quantize codes and scales bit-exact against the oracle (rint) and against
+  popcorn's own quantize kernels rebuilt for sm_100a, special values included;
+* the oracle itself bit-exact against popcorn's own matmul kernel (pin);
+* the f32 path within 1e-5 normwise and the tensor path within 2e-3 normwise
+  (max|got - ref| / max|ref|) on shapes with tails and unaligned pointers;
+* no writes outside the output (guard bytes around every output).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+import popcorn_b200 as pc
+
+pytestmark = pytest.mark.gpu
+
+TOL_ABS = 1e-5          # popcorn test/test_quantize.cu:4
+TOL_F32 = 1e-5          # normwise, f32 CUDA-core path
+TOL_TENSOR = 2e-3       # normwise, f16 tensor-core path
+GUARD = 4096            # guard elements on each side of an output
+
+
+def dev(a, torch, cuda):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+
+
+class Guarded:
+    """Device output with canary-filled guard regions on both sides."""
+
+    def __init__(self, torch, cuda, n, dtype, fill):
+        self.torch = torch
+        self.n = n
+        self.buf = torch.full((n + 2 * GUARD,), fill, dtype=dtype, device=cuda)
+        self.fill = fill
+        self.view = self.buf[GUARD:GUARD + n]
+
+    def ptr(self):
+        return self.view.data_ptr()
+
+    def check(self):
+        b = self.buf.cpu()
+        lo, hi = b[:GUARD], b[GUARD + self.n:]
+        if b.dtype.is_floating_point and self.fill != self.fill:
+            assert bool(self.torch.isnan(lo).all()) and bool(self.torch.isnan(hi).all()), "guard overwritten"
+        else:
+            assert bool((lo == self.fill).all()) and bool((hi == self.fill).all()), "guard overwritten"
+        return self.view.cpu().numpy()
+
+
+def abi_matmul(torch, cuda, x, q, s, path=pc.PATH_AUTO, x_offset=0, q_offset=0):
+    """Run the dequant-matmul through the C ABI; x/q may sit at odd byte offsets."""
+    M, K = x.shape
+    N = q.shape[0]
+    xs = torch.zeros(M * K + x_offset + 4, dtype=torch.float32, device=cuda)
+    xs[x_offset:x_offset + M * K] = dev(x.reshape(-1), torch, cuda)
+    qs = torch.zeros(N * K + q_offset + 16, dtype=torch.int8, device=cuda)
+    qs[q_offset:q_offset + N * K] = dev(q.reshape(-1), torch, cuda)
+    sd = dev(s, torch, cuda)
+    out = Guarded(torch, cuda, M * N, torch.float32, float("nan"))
+    xp = xs.data_ptr() + 4 * x_offset
+    qp = qs.data_ptr() + q_offset
+    if path == pc.PATH_AUTO:
+        st = pc.popcornDequantizeMatmul_i8f32(out.ptr(), xp, qp, sd.data_ptr(), M, N, K, None)
+    else:
+        st = pc.popcornDequantizeMatmulPath_i8f32(out.ptr(), xp, qp, sd.data_ptr(), M, N, K, path, None)
+    assert st == pc.POPCORN_SUCCESS, pc.load_library().popcornGetLastCudaErrorString()
+    torch.cuda.synchronize()
+    return out.check().reshape(M, N)
+
+
+def random_case(M, N, K, seed):
+    x = oracle.fill_normal(M * K, seed, 1.0).reshape(M, K)
+    w = oracle.fill_normal(N * K, seed + 1000, 0.02).reshape(N, K)
+    q, s = oracle.quantize(w)
+    return x, q, s
+
+
+# ---------------------------------------------------------------------------
+# The reference suite's fixtures (golden vectors from its own CPU loops).
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("case", ["basic", "identity", "large", "single_row"])
+def test_reference_matmul_fixtures(golden, cuda, case):
+    import torch
+
+    x, q, s = golden[f"{case}/x"], golden[f"{case}/q"], golden[f"{case}/scale"]
+    got = abi_matmul(torch, cuda, x, q, s)
+    np.testing.assert_allclose(got, golden[f"{case}/out"], rtol=0, atol=TOL_ABS)
+
+
+@pytest.mark.parametrize("case", ["batched_basic", "batched_large"])
+def test_reference_batched_fixtures(golden, cuda, case):
+    import torch
+
+    x, q, s = golden[f"{case}/x"], golden[f"{case}/q"], golden[f"{case}/scale"]
+    B, M, K = x.shape
+    N = q.shape[0]
+    out = Guarded(torch, cuda, B * M * N, torch.float32, float("nan"))
+    xd, qd, sd = dev(x, torch, cuda), dev(q, torch, cuda), dev(s, torch, cuda)
+    st = pc.popcornDequantizeMatmulBatched_i8f32(out.ptr(), xd.data_ptr(), qd.data_ptr(), sd.data_ptr(),
+                                                 B, M, N, K, None)
+    assert st == pc.POPCORN_SUCCESS
+    torch.cuda.synchronize()
+    got = out.check().reshape(B, M, N)
+    np.testing.assert_allclose(got, golden[f"{case}/out"], rtol=0, atol=TOL_ABS)
+
+
+@pytest.mark.parametrize("case", ["q_basic", "q_large", "q_roundtrip", "q_ties"])
+def test_reference_quantize_fixtures(golden, cuda, case):
+    import torch
+
+    w = golden[f"{case}/w"]
+    N, K = w.shape
+    q_out = Guarded(torch, cuda, N * K, torch.int8, 77)
+    s_out = Guarded(torch, cuda, N, torch.float32, -3.0)
+    wd = dev(w, torch, cuda)
+    assert pc.popcornQuantize_f32i8(q_out.ptr(), s_out.ptr(), wd.data_ptr(), N, K, None) == pc.POPCORN_SUCCESS
+    torch.cuda.synchronize()
+    q = q_out.check().reshape(N, K)
+    s = s_out.check()
+    qo, so = oracle.quantize(w)  # rint, popcorn's GPU semantics
+    np.testing.assert_array_equal(q, qo)
+    np.testing.assert_array_equal(s, so)
+    np.testing.assert_array_equal(s, golden[f"{case}/scale"])
+    # Where the test loop's roundf differs, the input is an exact tie.
+    ref = golden[f"{case}/codes_test_loop"]
+    quot = w / s[:, None]
+    assert np.all(np.abs(quot[q != ref] - np.trunc(quot[q != ref])) == 0.5)
+
+
+def test_config1_host_parity(golden, cuda):
+    import torch
+    from tests.golden.make_golden import config1_inputs
+
+    x, w = config1_inputs()
+    wd = dev(w, torch, cuda)
+    q, s = pc.quantize(wd)
+    torch.cuda.synchronize()
+    qo, so = oracle.quantize(w)
+    np.testing.assert_array_equal(q.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s.cpu().numpy(), golden["config1/scale"])
+    got = abi_matmul(torch, cuda, x, qo, so)
+    ref = golden["config1/out"]
+    assert oracle.normwise_rel_err(got, ref) <= TOL_F32
+    np.testing.assert_allclose(got, ref, rtol=0, atol=5e-5)
+
+
+# ---------------------------------------------------------------------------
+# popcorn's own kernels rebuilt for sm_100a.
+# ---------------------------------------------------------------------------
+needs_ref_gpu = pytest.mark.skipif(not oracle.have_popcorn_ref_gpu(), reason="oracle/_ref not built")
+
+
+def special_rows(K):
+    rng = np.random.default_rng(3)
+    rows = [
+        rng.standard_normal(K).astype(np.float32),
+        np.zeros(K, np.float32),
+        np.full(K, -0.0, np.float32),
+        np.full(K, 1e-42, np.float32),                       # denormals
+        (rng.standard_normal(K) * 1e30).astype(np.float32),
+        np.where(np.arange(K) % 5 == 0, np.nan, 1.0).astype(np.float32),
+        np.full(K, np.nan, np.float32),
+        np.where(np.arange(K) == 3, np.inf, 2.0).astype(np.float32),
+        np.where(np.arange(K) == 1, -np.inf, np.arange(K, dtype=np.float32)).astype(np.float32),
+        (np.arange(K, dtype=np.float32) - K / 2) * np.float32(0.5),  # many .5 ties
+        np.full(K, 3.4e38, np.float32),
+    ]
+    return np.stack(rows)
+
+
+@needs_ref_gpu
+@pytest.mark.parametrize("K", [1, 4, 37, 256, 4096, 4100])
+def test_quantize_bitexact_vs_popcorn_kernel(cuda, K):
+    import torch
+
+    w = special_rows(K)
+    w = np.concatenate([w, oracle.fill_normal(40 * K, K, 0.02).reshape(40, K)])
+    N = w.shape[0]
+    wd = dev(w, torch, cuda)
+    q1, s1 = pc.quantize(wd)
+    q2 = torch.empty_like(q1)
+    s2 = torch.empty_like(s1)
+    ref = oracle.popcorn_ref_gpu()
+    assert ref.popcornQuantize_f32i8(q2.data_ptr(), s2.data_ptr(), wd.data_ptr(), N, K, None) == 0
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(q1.cpu().numpy(), q2.cpu().numpy())
+    np.testing.assert_array_equal(s1.cpu().numpy().view(np.uint32), s2.cpu().numpy().view(np.uint32))
+    qo, so = oracle.quantize(w)
+    np.testing.assert_array_equal(q1.cpu().numpy(), qo)
+    np.testing.assert_array_equal(s1.cpu().numpy().view(np.uint32), so.view(np.uint32))
+
+
+@needs_ref_gpu
+@pytest.mark.parametrize("shape", [(1, 64, 64), (3, 40, 96), (16, 256, 1024), (33, 100, 512)])
+def test_oracle_pinned_to_popcorn_matmul_kernel(cuda, shape):
+    # popcorn's kernel accumulates sequentially in k with a fused multiply-add;
+    # the oracle's fused variant must reproduce it bit for bit (K % 32 == 0, the
+    # shapes where popcorn's kernel has no tail bug, src/quantize.cu:57-58).
+    import torch
+
+    M, N, K = shape
+    x, q, s = random_case(M, N, K, 21)
+    xd, qd, sd = dev(x, torch, cuda), dev(q, torch, cuda), dev(s, torch, cuda)
+    out = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    ref = oracle.popcorn_ref_gpu()
+    assert ref.popcornDequantizeMatmul_i8f32(out.data_ptr(), xd.data_ptr(), qd.data_ptr(), sd.data_ptr(),
+                                             M, N, K, None) == 0
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), oracle.dequant_matmul(x, q, s, fused=True))
+
+
+@needs_ref_gpu
+@pytest.mark.parametrize("shape", [(1, 4096, 4096), (4, 1024, 4096), (32, 512, 2048)])
+def test_matmul_vs_popcorn_kernel(cuda, shape):
+    import torch
+
+    M, N, K = shape
+    x, q, s = random_case(M, N, K, 31)
+    xd, qd, sd = dev(x, torch, cuda), dev(q, torch, cuda), dev(s, torch, cuda)
+    ref_out = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    assert oracle.popcorn_ref_gpu().popcornDequantizeMatmul_i8f32(
+        ref_out.data_ptr(), xd.data_ptr(), qd.data_ptr(), sd.data_ptr(), M, N, K, None) == 0
+    got = pc.dequantize_matmul(xd, qd, sd)
+    torch.cuda.synchronize()
+    path = pc.select_path(xd.data_ptr(), qd.data_ptr(), M, N, K)
+    tol = TOL_TENSOR if path == pc.PATH_TENSOR_F16 else TOL_F32
+    assert oracle.normwise_rel_err(got.cpu().numpy(), ref_out.cpu().numpy()) <= tol
+
+
+# ---------------------------------------------------------------------------
+# Shapes with tails, odd K, unaligned pointers, every path.
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 7, 33])
+@pytest.mark.parametrize("N,K", [(1, 16), (7, 48), (129, 512), (64, 1000), (17, 4112), (300, 8192)])
+def test_simt_path_shapes(cuda, M, N, K):
+    import torch
+
+    x, q, s = random_case(M, N, K, M * 7 + N)
+    got = abi_matmul(torch, cuda, x, q, s, path=pc.PATH_SIMT_F32)
+    ref = oracle.dequant_matmul(x, q, s, fused=True, threads=8)
+    assert oracle.normwise_rel_err(got, ref) <= TOL_F32
+
+
+@pytest.mark.parametrize("x_off,q_off", [(1, 0), (0, 3), (2, 5)])
+def test_unaligned_pointers(cuda, x_off, q_off):
+    import torch
+
+    M, N, K = 5, 70, 256
+    x, q, s = random_case(M, N, K, 41)
+    got = abi_matmul(torch, cuda, x, q, s, x_offset=x_off, q_offset=q_off)
+    assert oracle.normwise_rel_err(got, oracle.dequant_matmul(x, q, s)) <= TOL_F32
+
+
+def test_tensor_path_rejects_what_it_cannot_run(cuda):
+    import torch
+
+    x, q, s = random_case(8, 64, 40, 5)  # K % 16 != 0
+    xd, qd, sd = dev(x, torch, cuda), dev(q, torch, cuda), dev(s, torch, cuda)
+    out = torch.empty((8, 64), dtype=torch.float32, device=cuda)
+    st = pc.popcornDequantizeMatmulPath_i8f32(out.data_ptr(), xd.data_ptr(), qd.data_ptr(), sd.data_ptr(),
+                                              8, 64, 40, pc.PATH_TENSOR_F16, None)
+    assert st == pc.POPCORN_ERROR_INVALID_VALUE
+
+
+@pytest.mark.parametrize("N,K", [(1, 1), (3, 5), (64, 4096), (130, 4112), (7, 100)])
+def test_dequantize_bitexact(cuda, N, K):
+    import torch
+
+    w = oracle.fill_normal(N * K, N + K, 0.02).reshape(N, K)
+    q, s = oracle.quantize(w)
+    out = Guarded(torch, cuda, N * K, torch.float32, float("nan"))
+    qd, sd = dev(q, torch, cuda), dev(s, torch, cuda)
+    assert pc.popcornDequantize_i8f32(out.ptr(), qd.data_ptr(), sd.data_ptr(), N, K, None) == pc.POPCORN_SUCCESS
+    torch.cuda.synchronize()
+    got = out.check().reshape(N, K)
+    np.testing.assert_array_equal(got.view(np.uint32), oracle.dequantize(q, s).view(np.uint32))
+
+
+def test_runs_on_caller_stream(cuda):
+    import torch
+
+    x, q, s = random_case(2, 512, 1024, 9)
+    xd, qd, sd = dev(x, torch, cuda), dev(q, torch, cuda), dev(s, torch, cuda)
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        out = pc.dequantize_matmul(xd, qd, sd, stream=st)
+    st.synchronize()
+    assert oracle.normwise_rel_err(out.cpu().numpy(), oracle.dequant_matmul(x, q, s)) <= TOL_F32
+
+
+def test_quantize_full_size_roundtrip_property(cuda):
+    # 4096 x 4096 ~ N(0, 0.02): codes from the GPU equal the oracle's, and the
+    # dequantized weights are within half a step of the input.
+    import torch
+
+    g = torch.Generator(device=cuda)
+    g.manual_seed(0)
+    w = torch.randn((4096, 4096), generator=g, device=cuda) * 0.02
+    q, s = pc.quantize(w)
+    d = pc.dequantize(q, s)
+    torch.cuda.synchronize()
+    assert bool(((d - w).abs() <= 0.5000001 * s[:, None]).all())
+    assert int(q.abs().max()) == 127
+    qo, so = oracle.quantize(w.cpu().numpy())
+    assert np.array_equal(q.cpu().numpy(), qo) and np.array_equal(s.cpu().numpy(), so)
+
+
+def test_error_record_is_per_thread(lib):
+    import threading
+
+    # A fresh thread starts with no recorded CUDA error.
+    seen = []
+    t = threading.Thread(target=lambda: seen.append(lib.popcornGetLastCudaError()))
+    t.start()
+    t.join()
+    assert seen == [0]
+    assert isinstance(ctypes.c_int(lib.popcornGetLastCudaError()).value, int)

@@ -1,0 +1,138 @@
+"""CPU: the oracle restatement against the golden vectors and the reference loops.
+
+The golden vectors were made by popcorn's own test-side CPU loops
+(test/test_quantize.cu:24-41, :677-706) on the reference suite's own inputs
+(tests/golden/make_golden.py). The restatement must reproduce them bit for
+bit; the rintf/roundf difference is confined to exact .5 quotients.
+"""
+import hashlib
+
+import numpy as np
+import pytest
+
+import oracle
+
+MATMUL_CASES = ["basic", "identity", "large", "single_row"]
+QUANT_CASES = ["q_basic", "q_large", "q_roundtrip", "q_ties"]
+
+
+@pytest.mark.parametrize("case", MATMUL_CASES)
+def test_matmul_matches_reference_loop_bitwise(golden, case):
+    out = oracle.dequant_matmul(golden[f"{case}/x"], golden[f"{case}/q"], golden[f"{case}/scale"])
+    np.testing.assert_array_equal(out, golden[f"{case}/out"])
+
+
+def test_identity_literal(golden):
+    out = oracle.dequant_matmul(golden["identity/x"], golden["identity/q"], golden["identity/scale"])
+    np.testing.assert_array_equal(out, golden["identity/expected_literal"])
+
+
+@pytest.mark.parametrize("case", ["batched_basic", "batched_large"])
+def test_batched_matches_reference_loop_bitwise(golden, case):
+    x, q, s = golden[f"{case}/x"], golden[f"{case}/q"], golden[f"{case}/scale"]
+    B, M, K = x.shape
+    # Batched == one matmul over B*M rows (x, out contiguous).
+    out = oracle.dequant_matmul(x.reshape(B * M, K), q, s).reshape(B, M, -1)
+    np.testing.assert_array_equal(out, golden[f"{case}/out"])
+
+
+@pytest.mark.parametrize("case", QUANT_CASES)
+def test_quantize_roundf_matches_reference_loop(golden, case):
+    q, s = oracle.quantize(golden[f"{case}/w"], ties_away=True)
+    np.testing.assert_array_equal(q, golden[f"{case}/codes_test_loop"])
+    np.testing.assert_array_equal(s, golden[f"{case}/scale"])
+
+
+@pytest.mark.parametrize("case", QUANT_CASES)
+def test_quantize_rint_differs_only_on_ties(golden, case):
+    w = golden[f"{case}/w"]
+    q, s = oracle.quantize(w)
+    np.testing.assert_array_equal(s, golden[f"{case}/scale"])
+    ref = golden[f"{case}/codes_test_loop"]
+    quot = w / s[:, None]
+    tie = np.abs(quot - np.trunc(quot)) == 0.5
+    assert np.array_equal(q[~tie], ref[~tie])
+    # Every disagreement is a tie, and rint is half-to-even there.
+    assert np.all(q[q != ref].astype(np.int64) % 2 == 0)
+
+
+def test_quantize_ties_half_to_even(golden):
+    q, _ = oracle.quantize(golden["q_ties/w"])
+    assert q.tolist() == [[127, 0, 2, 2, 0, -2, -2, 126]]
+
+
+def test_roundtrip_bound(golden):
+    # popcorn test/test_quantize.cu:996-1016: |dequant - orig| <= 0.6 * scale.
+    w = golden["q_roundtrip/w"]
+    q, s = oracle.quantize(w)
+    d = oracle.dequantize(q, s)
+    assert np.all(np.abs(d - w) <= 0.6 * s[:, None])
+    assert s[3] == 1.0  # all-zero row
+
+
+def test_config1_generator_and_outputs(golden):
+    from tests.golden.make_golden import CONFIG1, config1_inputs
+
+    x, w = config1_inputs()
+    assert hashlib.sha256(x.tobytes()).hexdigest() == str(golden["config1/x_sha256"])
+    assert hashlib.sha256(w.tobytes()).hexdigest() == str(golden["config1/w_sha256"])
+    q, s = oracle.quantize(w, ties_away=True)
+    assert hashlib.sha256(q.tobytes()).hexdigest() == str(golden["config1/codes_test_loop_sha256"])
+    np.testing.assert_array_equal(s, golden["config1/scale"])
+    out = oracle.dequant_matmul(x, q, s)
+    np.testing.assert_array_equal(out, golden["config1/out"])
+    assert list(golden["config1/shape"]) == [CONFIG1["M"], CONFIG1["K"], CONFIG1["N"]]
+    # Generator statistics: mean ~0, std ~sigma, |x| < 6 sigma by construction.
+    assert abs(float(x.mean())) < 0.05 and abs(float(x.std()) - 1.0) < 0.05
+    assert abs(float(w.std()) - 0.02) < 0.001 and float(np.abs(w).max()) < 0.12
+
+
+def test_threaded_oracle_bitwise():
+    x = oracle.fill_normal(3 * 200, 5, 1.0).reshape(3, 200)
+    w = oracle.fill_normal(37 * 200, 6, 0.02).reshape(37, 200)
+    q, s = oracle.quantize(w)
+    for fused in (False, True):
+        a = oracle.dequant_matmul(x, q, s, fused=fused)
+        b = oracle.dequant_matmul(x, q, s, fused=fused, threads=5)
+        np.testing.assert_array_equal(a, b)
+
+
+def test_fused_and_unfused_agree_to_f32_rounding():
+    x = oracle.fill_normal(4 * 4096, 7, 1.0).reshape(4, 4096)
+    w = oracle.fill_normal(64 * 4096, 8, 0.02).reshape(64, 4096)
+    q, s = oracle.quantize(w)
+    a = oracle.dequant_matmul(x, q, s, fused=False)
+    b = oracle.dequant_matmul(x, q, s, fused=True)
+    assert oracle.normwise_rel_err(b, a) < 1e-5
+
+
+def test_normwise_metric_detects_a_planted_error():
+    ref = np.array([[1.0, -2.0, 4.0]], dtype=np.float32)
+    bad = ref.copy()
+    bad[0, 1] += 0.01
+    assert oracle.normwise_rel_err(ref, ref) == 0.0
+    assert abs(oracle.normwise_rel_err(bad, ref) - 0.0025) < 1e-7
+
+
+@pytest.mark.skipif(not oracle.have_ref_loops(), reason="reference loops not built (oracle/_ref)")
+@pytest.mark.parametrize("shape", [(1, 1, 1), (3, 7, 33), (5, 64, 1000), (16, 129, 512)])
+def test_oracle_equals_reference_loops_random(shape):
+    M, N, K = shape
+    x = oracle.fill_normal(M * K, 11 + M, 1.0).reshape(M, K)
+    w = oracle.fill_normal(N * K, 12 + N, 0.02).reshape(N, K)
+    qr, sr = oracle.ref_quantize(w)
+    qo, so = oracle.quantize(w, ties_away=True)
+    np.testing.assert_array_equal(qr, qo)
+    np.testing.assert_array_equal(sr, so)
+    np.testing.assert_array_equal(oracle.ref_dequant_matmul(x, qr, sr), oracle.dequant_matmul(x, qr, sr))
+    np.testing.assert_array_equal(oracle.ref_dequant_matmul(x, qr, sr, threads=3), oracle.dequant_matmul(x, qr, sr))
+
+
+@pytest.mark.skipif(not oracle.have_ref_loops(), reason="reference loops not built (oracle/_ref)")
+def test_planted_oracle_mistake_is_caught():
+    # A wrong restatement (scale applied twice) must not pass the pin.
+    x = oracle.fill_normal(2 * 64, 1, 1.0).reshape(2, 64)
+    w = oracle.fill_normal(8 * 64, 2, 0.02).reshape(8, 64)
+    q, s = oracle.ref_quantize(w)
+    wrong = oracle.dequant_matmul(x, q, s * s)
+    assert not np.array_equal(wrong, oracle.ref_dequant_matmul(x, q, s))
