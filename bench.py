@@ -437,7 +437,7 @@ def run_ours(args):
 
     if world == 1 and rank == 0:
         extras = {}
-        for name in [e for e in args.extras.split(",") if e and e != args.workload]:
+        for name in [e for e in args.extras.split(",") if e in WORKLOADS and e != args.workload]:
             ewl = WORKLOADS[name]
             es = Setup(torch, pc, ewl, 0, 1, device, pool)
             esteps = 200 if ewl["bound"] == "hbm" else 20

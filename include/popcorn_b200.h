@@ -23,8 +23,9 @@ typedef enum {
     POPCORN_MATMUL_PATH_SIMT_F32 = 1,
     /* tcgen05 tensor-core path: codes become f16 (exact), each activation row
      * is rescaled by a power of two and rounded to f16, products accumulate
-     * in f32 in tensor memory. Needs K % 16 == 0 and 16-byte aligned x and
-     * qweight. */
+     * in f32 in tensor memory (max relative error ~2e-4 normwise). Needs
+     * K % 16 == 0 and a 16-byte aligned qweight. Takes stream-ordered scratch
+     * of M*K*2 + M*4 bytes from a library-private memory pool. */
     POPCORN_MATMUL_PATH_TENSOR_F16 = 2,
 } popcornMatmulPath_t;
 
@@ -81,6 +82,12 @@ int popcornDequantizeMatmulLaunchCount(
     int64_t K,
     popcornMatmulPath_t path
 );
+
+/* Diagnostic: copies the current device's kernel error bits into *flags and
+ * clears them (synchronous). Non-zero bits mean a bounded wait inside a
+ * tensor-core kernel gave up (the kernel ended early instead of hanging);
+ * the results of that launch are not valid. */
+int popcornB200DeviceErrors(unsigned int* flags);
 
 #ifdef __cplusplus
 }

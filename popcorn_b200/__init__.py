@@ -47,6 +47,7 @@ EXT_SYMBOLS = (
     "popcornDequantizeMatmulPath_i8f32",
     "popcornDequantizeMatmulSelectPath",
     "popcornDequantizeMatmulLaunchCount",
+    "popcornB200DeviceErrors",
 )
 
 _vp = ctypes.c_void_p
@@ -64,6 +65,7 @@ _SIGNATURES = {
     "popcornDequantizeMatmulPath_i8f32": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "popcornDequantizeMatmulSelectPath": (_int, [_vp, _vp, _i64, _i64, _i64]),
     "popcornDequantizeMatmulLaunchCount": (_int, [_vp, _vp, _i64, _i64, _i64, _int]),
+    "popcornB200DeviceErrors": (_int, [ctypes.POINTER(ctypes.c_uint)]),
 }
 
 _lib = None
@@ -140,6 +142,15 @@ def select_path(x_ptr: int, q_ptr: int, M: int, N: int, K: int) -> int:
 
 def launch_count(x_ptr: int, q_ptr: int, M: int, N: int, K: int, path: int = PATH_AUTO) -> int:
     return load_library().popcornDequantizeMatmulLaunchCount(x_ptr, q_ptr, M, N, K, path)
+
+
+def device_errors() -> int:
+    """Read and clear the current device's kernel error bits (0 = none)."""
+    flags = ctypes.c_uint(0)
+    st = load_library().popcornB200DeviceErrors(ctypes.byref(flags))
+    if st != POPCORN_SUCCESS:
+        raise PopcornError(st, "popcornB200DeviceErrors")
+    return flags.value
 
 
 def _check(status: int, where: str) -> None:

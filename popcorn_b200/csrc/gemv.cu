@@ -1,37 +1,36 @@
 // f32 CUDA-core dequant-matmul path: out[m, n] = scale[n] * sum_k x[m, k] * q[n, k].
 //
-// This is the small-M (decode) kernel. Its arithmetic follows popcorn's
-// dequantizeMatmulKernel_i8f32 (src/quantize.cu:18-84): int8 codes widened
-// exactly to f32, products accumulated in f32. Two deliberate differences: the
-// per-channel scale is applied once to the finished sum instead of to every
-// code (the scale factors out of the k-sum), and the k-sum is split across
-// lanes and combined by a shuffle tree, so rounding differs from popcorn's
-// sequential sum by a few f32 ulps of the accumulated magnitude.
+// Arithmetic follows popcorn's dequantizeMatmulKernel_i8f32
+// (src/quantize.cu:18-84): int8 codes widened exactly to f32, products
+// accumulated in f32. Three kernels:
 //
-// Layout in HBM: x row-major [M, K] f32, q row-major [N, K] int8, out [M, N].
-// Each warp owns NR weight rows and streams them with 16-byte loads (lane l
-// reads bytes [16l, 16l+16) of every 512-byte segment, so one warp load
-// instruction is one fully used 512-byte span). The activation chunk is staged
-// once per block in shared memory with an XOR swizzle on 16-byte units so the
-// lane-strided 16-byte reads are bank-conflict free. Codes are widened with
-// the exponent trick: byte b^0x80 placed in the low mantissa of 2^23 gives
-// the float 2^23 + 128 + code; subtracting 2^23 + 128 is exact.
+//  * seq_kernel -- tiny problems (launch-bound anyway): one thread per output
+//    walks k upward with w = code * scale and acc = fma(x, w, acc), the exact
+//    operation sequence of popcorn's kernel, so results are bit-identical to
+//    it (and to the oracle's fused variant).
+//  * gemv_xs_kernel -- decode (M <= 4): "x-stationary" streaming GEMV. Each
+//    thread owns U 16-element slices of K and keeps those activations in
+//    registers; every weight row is read with one 16-byte load per thread
+//    (256 threads cover 4 KB of a row, fully coalesced), R rows at a time, so
+//    a block has R*U*4 KB of weights in flight with no shared-memory staging.
+//    The per-channel scale is applied once to the finished sum (it factors
+//    out of the k-sum). Per-lane partial sums are combined by a fixed
+//    butterfly reduce-scatter across the warp and a fixed-order sum across
+//    warps, so results are deterministic; they differ from popcorn's
+//    sequential order by f32 rounding only.
+//  * gemv_kernel -- other aligned shapes (larger K or M): activations staged
+//    in shared memory with cp.async, weights streamed per warp.
+//  * generic_kernel -- any shape / alignment.
 //
-// Roofline: HBM. Algorithmic bytes per launch = N*K (int8 weights); x, scale
-// and out add 4*(M*K + N + M*N).
+// Codes are widened with the exponent trick: byte (code ^ 0x80) in the low
+// mantissa byte of 2^23 is the float 2^23 + 128 + code; subtracting
+// 2^23 + 128 is exact.
+//
+// Roofline: HBM. Algorithmic bytes per launch = N*K (int8 weights).
 #include "common.cuh"
 
 namespace pcb {
 namespace {
-
-constexpr int kGemvWarps = 4;              // warps per block
-constexpr int kGemvThreads = kGemvWarps * 32;
-constexpr int kChunk = 4096;               // activations staged per pass (elements)
-constexpr int kSeg = 512;                  // weight bytes one warp load covers
-constexpr int kSegsPerChunk = kChunk / kSeg;
-constexpr int kUnitsPerChunk = kChunk / 4; // 16-byte units per staged row
-
-__device__ __forceinline__ int swz(int u) { return u ^ ((u >> 3) & 7); }
 
 // Four int8 codes (one 32-bit word) -> four exact floats.
 __device__ __forceinline__ void widen4(uint32_t word, float2& lo, float2& hi) {
@@ -44,6 +43,172 @@ __device__ __forceinline__ void widen4(uint32_t word, float2& lo, float2& hi) {
     c.y = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7443));
     lo = __fadd2_rn(a, magic);
     hi = __fadd2_rn(c, magic);
+}
+
+// ---------------------------------------------------------------- seq_kernel
+__global__ void __launch_bounds__(256)
+seq_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* __restrict__ q,
+           const float* __restrict__ scale, int64_t M, int64_t N, int64_t K) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < M * N; t += stride) {
+        const int64_t n = t % N;
+        const int64_t m = t / N;
+        const float* xr = x + m * K;
+        const int8_t* qr = q + n * K;
+        const float sc = __ldg(scale + n);
+        float acc = 0.0f;
+        for (int64_t k = 0; k < K; ++k) {
+            const float w = static_cast<float>(__ldg(qr + k)) * sc;
+            acc = __fmaf_rn(__ldg(xr + k), w, acc);
+        }
+        out[t] = acc;
+    }
+}
+
+constexpr int kMaxDevices = 64;
+
+// ------------------------------------------------------------ gemv_xs_kernel
+constexpr int kXsThreads = 256;
+constexpr int kXsWarps = kXsThreads / 32;
+
+// Butterfly reduce-scatter of V values across the warp: afterwards the lanes
+// with (lane % (32 / V)) == 0 hold the warp total of value index lane / (32 / V).
+template <int V>
+__device__ __forceinline__ float warp_reduce_scatter(float (&v)[V], int lane) {
+    int cnt = V;
+    #pragma unroll
+    for (int step = 16; step >= 1; step >>= 1) {
+        if (cnt > 1) {
+            const int half = cnt >> 1;
+            const bool upper = (lane & step) != 0;
+            #pragma unroll
+            for (int i = 0; i < V / 2; ++i) {
+                if (i < half) {
+                    const float send = upper ? v[i] : v[i + half];
+                    const float keep = upper ? v[i + half] : v[i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, step);
+                }
+            }
+            cnt = half;
+        } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], step);
+        }
+    }
+    return v[0];
+}
+
+// MT activation rows (<= 4), U 16-element K slices per thread, R weight rows
+// per iteration. Block b owns weight rows [b*rpc, min(N, (b+1)*rpc)).
+template <int MT, int U, int R>
+__global__ void __launch_bounds__(kXsThreads, (MT * U <= 1) ? 4 : 2)
+gemv_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* __restrict__ q,
+               const float* __restrict__ scale, int64_t M, int64_t N, int64_t K, int rpc) {
+    extern __shared__ float part[];  // [rpc][MT][kXsWarps]
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int64_t units = K >> 4;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rpc;
+    const int64_t r1 = (r0 + rpc < N) ? r0 + rpc : N;
+
+    for (int64_t m0 = static_cast<int64_t>(blockIdx.y) * MT; m0 < M; m0 += static_cast<int64_t>(gridDim.y) * MT) {
+        // Activations of this thread's K slices, kept in registers.
+        float2 xv[MT][U][8];
+        #pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t unit = tid + static_cast<int64_t>(u) * kXsThreads;
+            #pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                if (unit < units && m0 + m < M) {
+                    const float4* p = reinterpret_cast<const float4*>(x + (m0 + m) * K + unit * 16);
+                    #pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const float4 v = __ldg(p + c);
+                        xv[m][u][2 * c] = make_float2(v.x, v.y);
+                        xv[m][u][2 * c + 1] = make_float2(v.z, v.w);
+                    }
+                } else {
+                    #pragma unroll
+                    for (int c = 0; c < 8; ++c) xv[m][u][c] = make_float2(0.0f, 0.0f);
+                }
+            }
+        }
+
+        for (int64_t rb = r0; rb < r1; rb += R) {
+            uint4 w[R][U];
+            #pragma unroll
+            for (int r = 0; r < R; ++r) {
+                #pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int64_t unit = tid + static_cast<int64_t>(u) * kXsThreads;
+                    if (rb + r < r1 && unit < units) {
+                        w[r][u] = __ldg(reinterpret_cast<const uint4*>(q + (rb + r) * K) + unit);
+                    } else {
+                        w[r][u] = make_uint4(0u, 0u, 0u, 0u);  // code 0
+                    }
+                }
+            }
+            float acc[R * MT];
+            #pragma unroll
+            for (int r = 0; r < R; ++r) {
+                float2 a[MT];
+                #pragma unroll
+                for (int m = 0; m < MT; ++m) a[m] = make_float2(0.0f, 0.0f);
+                #pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const uint32_t words[4] = {w[r][u].x, w[r][u].y, w[r][u].z, w[r][u].w};
+                    #pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        float2 lo, hi;
+                        widen4(words[c], lo, hi);
+                        #pragma unroll
+                        for (int m = 0; m < MT; ++m) {
+                            a[m] = __ffma2_rn(xv[m][u][2 * c], lo, a[m]);
+                            a[m] = __ffma2_rn(xv[m][u][2 * c + 1], hi, a[m]);
+                        }
+                    }
+                }
+                #pragma unroll
+                for (int m = 0; m < MT; ++m) acc[r * MT + m] = a[m].x + a[m].y;
+            }
+            constexpr int V = R * MT;
+            const float total = warp_reduce_scatter<V>(acc, lane);
+            constexpr int span = 32 / V;
+            if ((lane % span) == 0) {
+                const int idx = lane / span;  // = r * MT + m
+                const int r = idx / MT;
+                const int m = idx % MT;
+                if (rb + r < r1) part[((rb + r - r0) * MT + m) * kXsWarps + warp] = total;
+            }
+        }
+        __syncthreads();
+        const int nvals = static_cast<int>(r1 - r0) * MT;
+        for (int i = tid; i < nvals; i += kXsThreads) {
+            const int r = i / MT;
+            const int m = i % MT;
+            float s = 0.0f;
+            #pragma unroll
+            for (int wv = 0; wv < kXsWarps; ++wv) s += part[i * kXsWarps + wv];
+            if (m0 + m < M) out[(m0 + m) * N + r0 + r] = s * __ldg(scale + r0 + r);
+        }
+        __syncthreads();
+    }
+}
+
+// --------------------------------------------------------------- gemv_kernel
+constexpr int kGemvWarps = 4;
+constexpr int kGemvThreads = kGemvWarps * 32;
+constexpr int kChunk = 4096;               // activations staged per pass (elements)
+constexpr int kSeg = 512;                  // weight bytes one warp load covers
+constexpr int kSegsPerChunk = kChunk / kSeg;
+constexpr int kUnitsPerChunk = kChunk / 4; // 16-byte units per staged row
+
+__device__ __forceinline__ int swz(int u) { return u ^ ((u >> 3) & 7); }
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+                 "l"(gmem)
+                 : "memory");
 }
 
 template <int MT, int NR>
@@ -65,8 +230,6 @@ gemv_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* 
         for (int64_t kc = 0; kc < K; kc += kChunk) {
             const int kn = static_cast<int>((K - kc) < kChunk ? (K - kc) : kChunk);  // multiple of 16
 
-            // Issue this chunk's weight loads first so they are in flight while
-            // the block stages the activations.
             uint4 w[kSegsPerChunk][NR];
             #pragma unroll
             for (int s = 0; s < kSegsPerChunk; ++s) {
@@ -88,11 +251,15 @@ gemv_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* 
                 const bool row_ok = (m0 + m) < M;
                 const float4* xr = reinterpret_cast<const float4*>(x + (m0 + m) * K + kc);
                 for (int u = threadIdx.x; u < units; u += kGemvThreads) {
-                    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    if (row_ok && u * 4 < kn) v = __ldg(xr + u);
-                    xs[m * kUnitsPerChunk + swz(u)] = v;
+                    float4* dst = &xs[m * kUnitsPerChunk + swz(u)];
+                    if (row_ok && u * 4 < kn) {
+                        cp_async16(dst, xr + u);  // all copies in flight at once
+                    } else {
+                        *dst = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    }
                 }
             }
+            asm volatile("cp.async.wait_all;" ::: "memory");
             __syncthreads();
 
             if (n0 < N) {
@@ -142,8 +309,7 @@ gemv_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* 
     }
 }
 
-// Any shape, any alignment: one warp per (weight row, activation row) pair,
-// scalar loads. Used when the vector kernel's K % 16 / alignment rules fail.
+// ------------------------------------------------------------ generic_kernel
 __global__ void __launch_bounds__(256)
 generic_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* __restrict__ q,
                const float* __restrict__ scale, int64_t M, int64_t N, int64_t K) {
@@ -162,12 +328,16 @@ generic_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_
     }
 }
 
+// ------------------------------------------------------------------- host
+bool g_smem_set[kMaxDevices][3] = {};
+
+// Up to this many multiply-adds the sequential kernel runs (bit-identical
+// to popcorn's kernel; the call is launch-bound at this size).
+constexpr int64_t kSeqMaxMacs = int64_t(1) << 22;
+
 bool vector_ok(const float* x, const int8_t* q, int64_t K) {
     return (K % 16 == 0) && aligned16(x) && aligned16(q);
 }
-
-constexpr int kMaxDevices = 64;
-bool g_smem_set[kMaxDevices][3] = {};
 
 template <int MT, int NR>
 popcornStatus_t launch_gemv(int slot, float* out, const float* x, const int8_t* q, const float* scale,
@@ -189,6 +359,42 @@ popcornStatus_t launch_gemv(int slot, float* out, const float* x, const int8_t* 
     return check_launch();
 }
 
+// Rows per block for the x-stationary kernel: every block of the grid is
+// resident at once (one wave), each owning an equal share of the rows.
+template <typename Kern>
+int xs_rows_per_block(Kern kernel, int slot, int64_t N) {
+    static int occ_cache[kMaxDevices][8] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int occ = (dev >= 0 && dev < kMaxDevices) ? occ_cache[dev][slot] : 0;
+    if (occ == 0) {
+        // Partial sums take at most 256 rows x 4 x 8 floats of shared memory.
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kXsThreads, 32 * 1024) != cudaSuccess ||
+            occ < 1) {
+            occ = 2;
+        }
+        if (dev >= 0 && dev < kMaxDevices) occ_cache[dev][slot] = occ;
+    }
+    const int64_t blocks = static_cast<int64_t>(device_sm_count()) * occ;
+    int64_t rpc = ceil_div(N, blocks);
+    if (rpc < 1) rpc = 1;
+    if (rpc > 256) rpc = 256;
+    return static_cast<int>(rpc);
+}
+
+template <int MT, int U, int R>
+popcornStatus_t launch_xs(int slot, float* out, const float* x, const int8_t* q, const float* scale, int64_t M,
+                          int64_t N, int64_t K, cudaStream_t stream) {
+    const int rpc = xs_rows_per_block(gemv_xs_kernel<MT, U, R>, slot, N);
+    const int smem = rpc * MT * kXsWarps * static_cast<int>(sizeof(float));
+    const int64_t gx = ceil_div(N, rpc);
+    int64_t gy = ceil_div(M, MT);
+    if (gy > 65535) gy = 65535;
+    dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
+    gemv_xs_kernel<MT, U, R><<<grid, kXsThreads, smem, stream>>>(out, x, q, scale, M, N, K, rpc);
+    return check_launch();
+}
+
 }  // namespace
 
 int simt_launch_count(const float*, const int8_t*, int64_t M, int64_t N, int64_t K) {
@@ -197,14 +403,33 @@ int simt_launch_count(const float*, const int8_t*, int64_t M, int64_t N, int64_t
 
 popcornStatus_t simt_dequant_matmul(float* out, const float* x, const int8_t* q, const float* scale,
                                     int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+    const bool tiny = (M * N <= kSeqMaxMacs) && (K <= kSeqMaxMacs / (M * N));
+    if (tiny) {
+        int64_t blocks = ceil_div(M * N, 256);
+        const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
+        if (blocks > cap) blocks = cap;
+        seq_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(out, x, q, scale, M, N, K);
+        return check_launch();
+    }
     if (!vector_ok(x, q, K)) {
-        int64_t warps = M * N;
-        int64_t blocks = ceil_div(warps, 8);
+        int64_t blocks = ceil_div(M * N, 8);
         const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
         if (blocks > cap) blocks = cap;
         generic_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(out, x, q, scale, M, N, K);
         return check_launch();
     }
+    const int64_t units = K / 16;
+    const int64_t slices = ceil_div(units, kXsThreads);  // U needed
+    if (M == 1 && slices <= 4) {
+        if (slices == 1) return launch_xs<1, 1, 8>(0, out, x, q, scale, M, N, K, stream);
+        if (slices == 2) return launch_xs<1, 2, 4>(1, out, x, q, scale, M, N, K, stream);
+        return launch_xs<1, 4, 2>(2, out, x, q, scale, M, N, K, stream);
+    }
+    if (M == 2 && slices <= 2) {
+        if (slices == 1) return launch_xs<2, 1, 8>(3, out, x, q, scale, M, N, K, stream);
+        return launch_xs<2, 2, 4>(4, out, x, q, scale, M, N, K, stream);
+    }
+    if (M <= 4 && slices == 1) return launch_xs<4, 1, 4>(5, out, x, q, scale, M, N, K, stream);
     if (M == 1) return launch_gemv<1, 2>(0, out, x, q, scale, M, N, K, stream);
     if (M == 2) return launch_gemv<2, 2>(1, out, x, q, scale, M, N, K, stream);
     return launch_gemv<4, 2>(2, out, x, q, scale, M, N, K, stream);

@@ -9,8 +9,10 @@
 // and rint are the IEEE round-to-nearest-even operations popcorn uses, so
 // codes and scales are bit-identical.
 //
-// Traffic per element: 4 B read from HBM (the second pass over a row is served
-// by L2), 1 B written; plus 4 B per row for the scale.
+// For 1024 <= K <= 16384 (K % 16 == 0, aligned) one block handles a row and
+// holds it in registers between the max and the quantize step; otherwise one
+// warp per row makes two passes (the second served by L2).
+// Traffic per element: 4 B read from HBM, 1 B written; plus 4 B per row.
 #include "common.cuh"
 
 namespace pcb {
@@ -94,6 +96,80 @@ quantize_rows_kernel(int8_t* __restrict__ out, float* __restrict__ scale,
     }
 }
 
+// One block per row, the whole row held in registers (U 16-float slices per
+// thread, K <= 16 * 256 * U): HBM is read exactly once, and each thread keeps
+// all of its loads in flight at once. Needs K % 16 == 0 and aligned bases.
+constexpr int kRowThreads = 256;
+
+template <int U>
+__global__ void __launch_bounds__(kRowThreads)
+quantize_row_block_kernel(int8_t* __restrict__ out, float* __restrict__ scale, const float* __restrict__ in,
+                          int64_t N, int64_t K) {
+    __shared__ float red[2][kRowThreads / 32];
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int64_t units = K >> 4;
+    int parity = 0;
+    for (int64_t row = blockIdx.x; row < N; row += gridDim.x, parity ^= 1) {
+        const float4* r4 = reinterpret_cast<const float4*>(in + row * K);
+        float4 v[U][4];
+        #pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t unit = tid + static_cast<int64_t>(u) * kRowThreads;
+            #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                v[u][c] = (unit < units) ? __ldg(r4 + unit * 4 + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+        }
+        float m = 0.0f;
+        #pragma unroll
+        for (int u = 0; u < U; ++u) {
+            #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                m = absmax_step(m, v[u][c].x);
+                m = absmax_step(m, v[u][c].y);
+                m = absmax_step(m, v[u][c].z);
+                m = absmax_step(m, v[u][c].w);
+            }
+        }
+        #pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float other = __shfl_xor_sync(0xffffffffu, m, off);
+            m = (other > m) ? other : m;
+        }
+        if (lane == 0) red[parity][warp] = m;
+        __syncthreads();
+        m = red[parity][0];
+        #pragma unroll
+        for (int w = 1; w < kRowThreads / 32; ++w) {
+            const float other = red[parity][w];
+            m = (other > m) ? other : m;
+        }
+        float sc = m / 127.0f;
+        if (sc == 0.0f) sc = 1.0f;
+        if (tid == 0) scale[row] = sc;
+
+        uint4* o16 = reinterpret_cast<uint4*>(out + row * K);
+        #pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t unit = tid + static_cast<int64_t>(u) * kRowThreads;
+            if (unit < units) {
+                uint32_t w[4];
+                #pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const uint32_t b0 = static_cast<uint8_t>(quantize_one(v[u][c].x, sc));
+                    const uint32_t b1 = static_cast<uint8_t>(quantize_one(v[u][c].y, sc));
+                    const uint32_t b2 = static_cast<uint8_t>(quantize_one(v[u][c].z, sc));
+                    const uint32_t b3 = static_cast<uint8_t>(quantize_one(v[u][c].w, sc));
+                    w[c] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+                }
+                o16[unit] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        }
+    }
+}
+
 // out[n, k] = float(q[n, k]) * scale[n]; kVec: K % 16 == 0 and aligned bases,
 // each thread expands 16 codes (one 16-byte load, four 16-byte stores).
 template <bool kVec>
@@ -147,6 +223,19 @@ extern "C" popcornStatus_t popcornQuantize_f32i8(int8_t* out, float* scale, cons
     if (N <= 0 || K <= 0) return POPCORN_SUCCESS;
 
     const bool vec = (K % 16 == 0) && aligned16(input) && aligned16(out);
+    if (vec && K >= 1024 && K <= 16 * kRowThreads * 4) {
+        // Block per row with the row in registers.
+        int64_t blocks = N;
+        const int64_t cap = static_cast<int64_t>(device_sm_count()) * 8;
+        if (blocks > cap) blocks = cap;
+        const int64_t slices = ceil_div(K / 16, kRowThreads);
+        const unsigned g = static_cast<unsigned>(blocks);
+        if (slices == 1) quantize_row_block_kernel<1><<<g, kRowThreads, 0, stream>>>(out, scale, input, N, K);
+        else if (slices == 2) quantize_row_block_kernel<2><<<g, kRowThreads, 0, stream>>>(out, scale, input, N, K);
+        else if (slices == 3) quantize_row_block_kernel<3><<<g, kRowThreads, 0, stream>>>(out, scale, input, N, K);
+        else quantize_row_block_kernel<4><<<g, kRowThreads, 0, stream>>>(out, scale, input, N, K);
+        return check_launch();
+    }
     // One warp per row; at most 16 resident blocks per SM worth of warps, the
     // grid-stride loop covers the rest.
     int64_t blocks = ceil_div(N, kWarpsPerBlock);

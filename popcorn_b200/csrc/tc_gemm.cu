@@ -1,15 +1,457 @@
-// tcgen05 tensor-core dequant-matmul path (large M). Not enabled yet.
+// tcgen05 tensor-core dequant-matmul path: out[m, n] = scale[n] * sum_k x[m, k] * q[n, k].
+//
+// Same arithmetic contract as popcorn's dequantizeMatmulKernel_i8f32
+// (src/quantize.cu:18-84) except that activations enter the tensor cores as
+// f16: int8 codes are exact in f16, each activation row m is first scaled by
+// a power of two 2^e_m (exact) so its largest |x| lands in [2^14, 2^15), then
+// rounded to f16 (relative error <= 2^-11 per element); products are exact
+// in the tensor core and accumulate in f32 in tensor memory; the epilogue
+// multiplies by 2^-e_m (exact) and by scale[n] (one rounding).
+//
+// Two launches per call:
+//  1. x_to_f16_kernel: x f32 [M, K] -> x16 f16 [M, K] + rowscale [M] = 2^-e_m
+//     in stream-ordered scratch from a private memory pool.
+//  2. tc_gemm_kernel<BM>: one CTA per 128 (weight rows) x BM (activation rows)
+//     output tile; swap-AB so the weight tile is the MMA "A" operand:
+//       warp 0      TMA producer: x16 tile [BM x 64] (128B swizzle) and the
+//                   int8 weight tile [128 x 64] (64B swizzle) per stage;
+//       warp 1      tcgen05.mma issuer (A from tensor memory, B = x16 tile
+//                   from shared memory, D = f32 [128 x BM] in tensor memory);
+//       warps 2-5   converters: each thread owns one weight row, widens its
+//                   64 codes to f16 with the exponent trick and writes them
+//                   to tensor memory (tcgen05.st) as the A operand;
+//       warps 6-9   epilogue: tcgen05.ld of the accumulator, one row per
+//                   lane, so each column m is a coalesced 128-byte store.
+// Keeping the widened weights in tensor memory means shared memory carries
+// only the int8 codes and the f16 activations, not a second f16 copy.
+//
+// Roofline: tensor (dense f16) for large M; algorithmic work 2*M*N*K.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace pcb {
 
-bool tc_supported(const float*, const int8_t*, int64_t, int64_t, int64_t) { return false; }
+// Error bits set by bounded waits that timed out (read by popcornB200DeviceErrors).
+__device__ unsigned int g_tc_error = 0;
 
-popcornStatus_t tc_dequant_matmul(float*, const float*, const int8_t*, const float*, int64_t, int64_t,
-                                  int64_t, cudaStream_t) {
-    return POPCORN_ERROR_INVALID_VALUE;
+namespace {
+
+using namespace sm100;
+
+constexpr int kBK = 64;        // K elements per pipeline stage
+constexpr int kTileN = 128;    // weight rows per CTA (MMA M)
+constexpr int kAStages = 4;    // tensor-memory A buffers, 32 columns each
+constexpr int kThreads = 320;  // 10 warps
+constexpr int kWarpTma = 0;
+constexpr int kWarpMma = 1;
+constexpr int kWarpEpi0 = 6;
+
+constexpr int pow2_at_least(int v) {
+    int p = 32;
+    while (p < v) p <<= 1;
+    return p;
 }
 
-int tc_launch_count(int64_t, int64_t, int64_t) { return 0; }
+template <int BM>
+struct Cfg {
+    static constexpr int kStages = BM >= 256 ? 4 : (BM >= 128 ? 6 : 8);
+    static constexpr int kXBytes = BM * kBK * 2;   // f16 activation tile per stage
+    static constexpr int kWBytes = kTileN * kBK;   // int8 weight tile per stage
+    static constexpr int kTmemCols = pow2_at_least(BM + kAStages * 32);
+    static constexpr int kNumBars = 2 * kStages + 2 * kAStages + 2;
+    static constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16;
+    static_assert(kXBytes % 1024 == 0, "x16 stages must stay 1024-byte aligned");
+};
+
+__device__ __forceinline__ float absmax_step(float m, float v) {
+    float a = fabsf(v);
+    return (a > m) ? a : m;
+}
+
+// x f32 [M, K] -> x16 f16 [M, K] with per-row power-of-two scaling; one warp per row.
+__global__ void __launch_bounds__(256)
+x_to_f16_kernel(__half* __restrict__ x16, float* __restrict__ rowscale, const float* __restrict__ x,
+                int64_t M, int64_t K, int vec) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M;
+         row += nwarps) {
+        const float* r = x + row * K;
+        __half* o = x16 + row * K;
+        float m = 0.0f;
+        if (vec) {
+            const float4* r4 = reinterpret_cast<const float4*>(r);
+            #pragma unroll 4
+            for (int64_t i = lane; i < (K >> 2); i += 32) {
+                const float4 v = __ldg(r4 + i);
+                m = absmax_step(absmax_step(absmax_step(absmax_step(m, v.x), v.y), v.z), v.w);
+            }
+        } else {
+            for (int64_t k = lane; k < K; k += 32) m = absmax_step(m, __ldg(r + k));
+        }
+        #pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float other = __shfl_xor_sync(0xffffffffu, m, off);
+            m = (other > m) ? other : m;
+        }
+        int e = 0;
+        if (m > 0.0f && m <= 3.402823466e38f) {
+            int p;
+            frexpf(m, &p);  // m in [2^(p-1), 2^p)
+            e = 15 - p;     // m * 2^e in [2^14, 2^15)
+            e = e < -126 ? -126 : (e > 126 ? 126 : e);
+        }
+        const float up = __int_as_float((e + 127) << 23);
+        if (lane == 0) rowscale[row] = __int_as_float((127 - e) << 23);
+        if (vec) {
+            const float4* r4 = reinterpret_cast<const float4*>(r);
+            uint4* o8 = reinterpret_cast<uint4*>(o);
+            for (int64_t c = lane; c < (K >> 3); c += 32) {
+                const float4 a = __ldg(r4 + 2 * c);
+                const float4 b = __ldg(r4 + 2 * c + 1);
+                __half2 h0 = __floats2half2_rn(a.x * up, a.y * up);
+                __half2 h1 = __floats2half2_rn(a.z * up, a.w * up);
+                __half2 h2 = __floats2half2_rn(b.x * up, b.y * up);
+                __half2 h3 = __floats2half2_rn(b.z * up, b.w * up);
+                uint4 packed;
+                packed.x = *reinterpret_cast<uint32_t*>(&h0);
+                packed.y = *reinterpret_cast<uint32_t*>(&h1);
+                packed.z = *reinterpret_cast<uint32_t*>(&h2);
+                packed.w = *reinterpret_cast<uint32_t*>(&h3);
+                o8[c] = packed;
+            }
+        } else {
+            for (int64_t k = lane; k < K; k += 32) o[k] = __float2half_rn(__ldg(r + k) * up);
+        }
+    }
+}
+
+// Four int8 codes (one word) -> two f16x2 words, exact:
+// (code ^ 0x80) in the low byte of f16 0x6400 gives 1024 + 128 + code;
+// subtracting 1152 leaves the code.
+__device__ __forceinline__ void widen4_f16(uint32_t word, uint32_t& lo, uint32_t& hi) {
+    const uint32_t b = word ^ 0x80808080u;
+    const uint32_t plo = __byte_perm(b, 0x64646464u, 0x5140);
+    const uint32_t phi = __byte_perm(b, 0x64646464u, 0x7362);
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+    __half2 l = __hsub2(*reinterpret_cast<const __half2*>(&plo), bias);
+    __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&phi), bias);
+    lo = *reinterpret_cast<uint32_t*>(&l);
+    hi = *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int BM>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+               float* __restrict__ out, const float* __restrict__ scale, const float* __restrict__ rowscale,
+               int M, int N, int K) {
+    using C = Cfg<BM>;
+    constexpr int S = C::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* xs = smem;                                  // S x [BM][64] f16, 128B swizzle
+    uint8_t* ws = smem + S * C::kXBytes;                 // S x [128][64] int8, 64B swizzle
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ws + S * C::kWBytes);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+
+    const uint32_t full0 = smem_addr(bars);
+    const uint32_t empty0 = full0 + 8 * S;
+    const uint32_t afull0 = empty0 + 8 * S;
+    const uint32_t aempty0 = afull0 + 8 * kAStages;
+    const uint32_t acc_full = aempty0 + 8 * kAStages;
+    const uint32_t drain = acc_full + 8;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * kTileN;
+    const int m0 = blockIdx.y * BM;
+    const int num_kb = (K + kBK - 1) / kBK;
+    unsigned int* err = &g_tc_error;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        for (int a = 0; a < kAStages; ++a) {
+            mbar_init(afull0 + 8 * a, 4);
+            mbar_init(aempty0 + 8 * a, 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (warp == kWarpTma && lane == 0) {
+        tma_prefetch_desc(&tmap_x);
+        tma_prefetch_desc(&tmap_w);
+    }
+    if (warp == kWarpMma) {
+        tmem_alloc(smem_addr(tmem_slot), C::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t acc_tmem = tmem;          // columns [0, BM)
+    const uint32_t a_tmem0 = tmem + BM;      // A buffers at columns BM + 32 * a
+
+    if (warp == kWarpTma) {
+        if (lane == 0) {
+            for (int kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % S;
+                if (kb >= S && !mbar_wait(empty0 + 8 * s, ((kb / S) - 1) & 1, err, 1u)) break;
+                mbar_arrive_expect_tx(full0 + 8 * s, C::kXBytes + C::kWBytes);
+                tma_load_2d(smem_addr(xs + s * C::kXBytes), &tmap_x, kb * kBK, m0, full0 + 8 * s);
+                tma_load_2d(smem_addr(ws + s * C::kWBytes), &tmap_w, kb * kBK, n0, full0 + 8 * s);
+            }
+            // Nothing of ours may still be landing in shared memory at exit:
+            // wait (bounded) for the last fill of every stage.
+            for (int kb = (num_kb > S ? num_kb - S : 0); kb < num_kb; ++kb) {
+                mbar_wait(full0 + 8 * (kb % S), (kb / S) & 1, err, 64u);
+            }
+        }
+    } else if (warp == kWarpMma) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16_f32(kTileN, BM);
+            for (int kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % S;
+                const int a = kb % kAStages;
+                if (!mbar_wait(full0 + 8 * s, (kb / S) & 1, err, 2u)) break;
+                if (!mbar_wait(afull0 + 8 * a, (kb / kAStages) & 1, err, 4u)) break;
+                tc_fence_after();
+                const uint64_t bdesc = smem_desc_sw128_kmajor(smem_addr(xs + s * C::kXBytes));
+                #pragma unroll
+                for (int j = 0; j < kBK / 16; ++j) {
+                    // K step of 16 f16 = 32 bytes inside the 128-byte swizzle row.
+                    mma_f16_ts(acc_tmem, a_tmem0 + a * 32 + j * 8, bdesc + static_cast<uint64_t>(j * 2), idesc,
+                               (kb | j) != 0 ? 1u : 0u);
+                }
+                mma_commit(empty0 + 8 * s);
+                mma_commit(aempty0 + 8 * a);
+            }
+            mma_commit(acc_full);
+            // Every MMA must be finished before tensor memory is released.
+            mma_commit(drain);
+            mbar_wait(drain, 0, err, 128u);
+        }
+    } else if (warp < kWarpEpi0) {
+        // Converters: thread owns weight row r of the tile = tensor-memory lane r.
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        for (int kb = 0; kb < num_kb; ++kb) {
+            const int s = kb % S;
+            const int a = kb % kAStages;
+            bool ok = mbar_wait(full0 + 8 * s, (kb / S) & 1, err, 8u);
+            if (ok && kb >= kAStages) ok = mbar_wait(aempty0 + 8 * a, ((kb / kAStages) - 1) & 1, err, 16u);
+            // tcgen05.st below is warp-collective: leave together or not at all.
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            const uint8_t* row = ws + s * C::kWBytes + r * kBK;
+            uint32_t w[16];
+            #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ ((r >> 1) & 3)) << 4));
+                w[4 * c + 0] = v.x;
+                w[4 * c + 1] = v.y;
+                w[4 * c + 2] = v.z;
+                w[4 * c + 3] = v.w;
+            }
+            uint32_t h[32];
+            #pragma unroll
+            for (int i = 0; i < 16; ++i) widen4_f16(w[i], h[2 * i], h[2 * i + 1]);
+            tmem_st_32x32b_x32(tmem + lane_addr + BM + a * 32, h);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(afull0 + 8 * a);
+        }
+    } else {
+        // Epilogue: lane = weight row n, 32 accumulator columns (activation rows) per load.
+        const int quarter = warp & 3;
+        const int n = n0 + quarter * 32 + lane;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        const bool ok = mbar_wait(acc_full, 0, err, 32u);
+        if (__all_sync(0xffffffffu, ok)) {
+            tc_fence_after();
+            const float sc = (n < N) ? __ldg(scale + n) : 0.0f;
+            #pragma unroll 1
+            for (int c0 = 0; c0 < BM; c0 += 32) {
+                if (m0 + c0 >= M) break;
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(acc_tmem + lane_addr + c0, v);
+                tmem_wait_ld();
+                if (n < N) {
+                    #pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int m = m0 + c0 + j;
+                        if (m < M) {
+                            out[static_cast<int64_t>(m) * N + n] = (__uint_as_float(v[j]) * __ldg(rowscale + m)) * sc;
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kWarpMma) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, C::kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+constexpr int kMaxDevices = 64;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        }
+    });
+    return fn;
+}
+
+// Stream-ordered scratch for x16 + rowscale: a private pool per device that
+// keeps its memory between calls (no trimming at synchronisation points).
+std::mutex g_pool_mu;
+cudaMemPool_t g_pool[kMaxDevices] = {};
+
+cudaError_t scratch_pool(cudaMemPool_t* out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_pool_mu);
+    if (g_pool[dev] == nullptr) {
+        cudaMemPoolProps props = {};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaMemPool_t pool;
+        e = cudaMemPoolCreate(&pool, &props);
+        if (e != cudaSuccess) return e;
+        uint64_t keep = UINT64_MAX;
+        e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        if (e != cudaSuccess) return e;
+        g_pool[dev] = pool;
+    }
+    *out = g_pool[dev];
+    return cudaSuccess;
+}
+
+bool g_attr_set[kMaxDevices][4] = {};
+
+template <int BM>
+popcornStatus_t launch_gemm(int slot, const CUtensorMap& tx, const CUtensorMap& tw, float* out, const float* scale,
+                            const float* rowscale, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+    using C = Cfg<BM>;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < kMaxDevices && !g_attr_set[dev][slot]) {
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BM>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+        if (e != cudaSuccess) return record_cuda(e);
+        g_attr_set[dev][slot] = true;
+    }
+    dim3 grid(static_cast<unsigned>(ceil_div(N, kTileN)), static_cast<unsigned>(ceil_div(M, BM)));
+    tc_gemm_kernel<BM><<<grid, kThreads, C::kSmem, stream>>>(tx, tw, out, scale, rowscale, static_cast<int>(M),
+                                                             static_cast<int>(N), static_cast<int>(K));
+    return check_launch();
+}
+
+int pick_bm(int64_t M) {
+    if (M <= 32) return 32;
+    if (M <= 64) return 64;
+    if (M <= 128) return 128;
+    return 256;
+}
+
+}  // namespace
+
+bool tc_supported(const float*, const int8_t* q, int64_t M, int64_t N, int64_t K) {
+    // TMA: 16-byte aligned weight base and row pitch; int32 tile coordinates.
+    return (K % 16 == 0) && aligned16(q) && M <= INT32_MAX && N <= INT32_MAX && K <= INT32_MAX &&
+           M * K <= (int64_t(1) << 40) && encode_fn() != nullptr;
+}
+
+int tc_launch_count(int64_t, int64_t, int64_t) { return 2; }
+
+popcornStatus_t tc_dequant_matmul(float* out, const float* x, const int8_t* q, const float* scale, int64_t M,
+                                  int64_t N, int64_t K, cudaStream_t stream) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
+    if (encode == nullptr) return POPCORN_ERROR_INVALID_VALUE;
+
+    // Scratch: x16 [M, K] f16, then rowscale [M] f32, each 256-byte aligned.
+    const size_t x16_bytes = (static_cast<size_t>(M) * K * 2 + 255) & ~size_t(255);
+    const size_t bytes = x16_bytes + ((static_cast<size_t>(M) * 4 + 255) & ~size_t(255));
+    cudaMemPool_t pool;
+    cudaError_t e = scratch_pool(&pool);
+    if (e != cudaSuccess) return record_cuda(e);
+    void* scratch = nullptr;
+    e = cudaMallocFromPoolAsync(&scratch, bytes, pool, stream);
+    if (e != cudaSuccess) return record_cuda(e);
+    __half* x16 = static_cast<__half*>(scratch);
+    float* rowscale = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + x16_bytes);
+
+    const int vec = aligned16(x) ? 1 : 0;
+    int64_t blocks = ceil_div(M, 8);
+    const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
+    if (blocks > cap) blocks = cap;
+    x_to_f16_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x16, rowscale, x, M, K, vec);
+    popcornStatus_t st = check_launch();
+
+    const int bm = pick_bm(M);
+    CUtensorMap tx, tw;
+    if (st == POPCORN_SUCCESS) {
+        const cuuint64_t xdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+        const cuuint64_t xstride[1] = {static_cast<cuuint64_t>(K) * 2};
+        const cuuint32_t xbox[2] = {kBK, static_cast<cuuint32_t>(bm)};
+        const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+        const cuuint64_t wstride[1] = {static_cast<cuuint64_t>(K)};
+        const cuuint32_t wbox[2] = {kBK, kTileN};
+        const cuuint32_t estride[2] = {1, 1};
+        CUresult r1 = encode(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, xdims, xstride, xbox, estride,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        CUresult r2 = encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q), wdims, wstride, wbox,
+                             estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS) st = POPCORN_ERROR_INVALID_VALUE;
+    }
+    if (st == POPCORN_SUCCESS) {
+        switch (bm) {
+            case 32: st = launch_gemm<32>(0, tx, tw, out, scale, rowscale, M, N, K, stream); break;
+            case 64: st = launch_gemm<64>(1, tx, tw, out, scale, rowscale, M, N, K, stream); break;
+            case 128: st = launch_gemm<128>(2, tx, tw, out, scale, rowscale, M, N, K, stream); break;
+            default: st = launch_gemm<256>(3, tx, tw, out, scale, rowscale, M, N, K, stream); break;
+        }
+    }
+    e = cudaFreeAsync(scratch, stream);
+    if (st == POPCORN_SUCCESS && e != cudaSuccess) st = record_cuda(e);
+    return st;
+}
 
 }  // namespace pcb
+
+extern "C" int popcornB200DeviceErrors(unsigned int* flags) {
+    if (flags == nullptr) return POPCORN_ERROR_INVALID_VALUE;
+    unsigned int zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(flags, pcb::g_tc_error, sizeof(unsigned int));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(pcb::g_tc_error, &zero, sizeof(unsigned int));
+    return pcb::record_cuda(e);
+}

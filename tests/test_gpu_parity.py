@@ -322,3 +322,102 @@ def test_error_record_is_per_thread(lib):
     t.join()
     assert seen == [0]
     assert isinstance(ctypes.c_int(lib.popcornGetLastCudaError()).value, int)
+
+
+# ---------------------------------------------------------------------------
+# tcgen05 tensor-core path.
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("M", [1, 5, 16, 32, 33, 64, 65, 100, 128, 129, 256, 300])
+@pytest.mark.parametrize("N,K", [(128, 64), (100, 16), (300, 80), (256, 1024), (129, 4096)])
+def test_tensor_path_shapes(cuda, M, N, K):
+    import torch
+
+    x, q, s = random_case(M, N, K, 100 + M + N + K)
+    got = abi_matmul(torch, cuda, x, q, s, path=pc.PATH_TENSOR_F16)
+    assert pc.device_errors() == 0
+    ref = oracle.dequant_matmul(x, q, s, fused=True, threads=8)
+    err = oracle.normwise_rel_err(got, ref)
+    assert err <= TOL_TENSOR, err
+    # f16 activations: expect ~1e-4, far inside the tolerance.
+    assert err <= 5e-4, err
+
+
+def test_tensor_path_row_scaling_handles_extreme_rows(cuda):
+    # Rows of wildly different magnitude, an all-zero row, a NaN row and an
+    # infinite entry: every finite row keeps f16 relative precision.
+    import torch
+
+    M, N, K = 8, 256, 512
+    x, q, s = random_case(M, N, K, 77)
+    x = x.copy()
+    x[0] *= 1e-30
+    x[1] *= 1e30
+    x[2] = 0.0
+    x[3, 5] = np.nan
+    x[4, 7] = np.inf
+    x[5] *= 3e-42 / np.abs(x[5]).max()  # denormal row
+    got = abi_matmul(torch, cuda, x, q, s, path=pc.PATH_TENSOR_F16)
+    assert pc.device_errors() == 0
+    ref = oracle.dequant_matmul(x, q, s, fused=True)
+    for m in (0, 1, 6, 7):
+        assert oracle.normwise_rel_err(got[m], ref[m]) <= 5e-4, m
+    assert np.all(got[2] == 0.0)
+    assert np.all(np.isnan(got[3]))
+    assert np.all(~np.isfinite(got[4]))
+
+
+def test_tensor_path_prefill_full_size(cuda):
+    # M=2048, K=4096, N=4096 against a float64 torch reference on the GPU.
+    import torch
+
+    g = torch.Generator(device=cuda)
+    g.manual_seed(7)
+    x = torch.randn((2048, 4096), generator=g, device=cuda)
+    w = torch.randn((4096, 4096), generator=g, device=cuda) * 0.02
+    q, s = pc.quantize(w)
+    y = pc.dequantize_matmul(x, q, s)
+    assert pc.select_path(x.data_ptr(), q.data_ptr(), 2048, 4096, 4096) == pc.PATH_TENSOR_F16
+    ref = x.double() @ (q.double() * s.double()[:, None]).T
+    torch.cuda.synchronize()
+    assert pc.device_errors() == 0
+    err = float((y.double() - ref).abs().max() / ref.abs().max())
+    assert err <= TOL_TENSOR, err
+
+
+def test_tensor_path_skinny_full_size(cuda):
+    import torch
+
+    g = torch.Generator(device=cuda)
+    g.manual_seed(8)
+    x = torch.randn((32, 4096), generator=g, device=cuda)
+    w = torch.randn((11008, 4096), generator=g, device=cuda) * 0.02
+    q, s = pc.quantize(w)
+    y = pc.dequantize_matmul(x, q, s)
+    ref = x.double() @ (q.double() * s.double()[:, None]).T
+    torch.cuda.synchronize()
+    assert pc.device_errors() == 0
+    err = float((y.double() - ref).abs().max() / ref.abs().max())
+    assert err <= TOL_TENSOR, err
+
+
+def test_decode_full_size_vs_oracle(cuda):
+    import torch
+
+    x, q, s = random_case(1, 4096, 4096, 55)
+    got = abi_matmul(torch, cuda, x, q, s)
+    assert oracle.normwise_rel_err(got, oracle.dequant_matmul(x, q, s, fused=True, threads=8)) <= TOL_F32
+
+
+def test_tensor_path_back_to_back_calls_reuse_scratch(cuda):
+    # Stream-ordered scratch: many calls in flight on one stream stay correct.
+    import torch
+
+    M, N, K = 256, 512, 1024
+    x, q, s = random_case(M, N, K, 3)
+    xd, qd, sd = dev(x, torch, cuda), dev(q, torch, cuda), dev(s, torch, cuda)
+    outs = [pc.dequantize_matmul(xd * (i + 1), qd, sd, path=pc.PATH_TENSOR_F16) for i in range(8)]
+    torch.cuda.synchronize()
+    assert pc.device_errors() == 0
+    ref = oracle.dequant_matmul(x, q, s, fused=True, threads=8)
+    for i, o in enumerate(outs):
+        assert oracle.normwise_rel_err(o.cpu().numpy() / (i + 1), ref) <= 5e-4
