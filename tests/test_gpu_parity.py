@@ -145,7 +145,10 @@ def test_config1_host_parity(golden, cuda):
     qo, so = oracle.quantize(w)
     np.testing.assert_array_equal(q.cpu().numpy(), qo)
     np.testing.assert_array_equal(s.cpu().numpy(), golden["config1/scale"])
-    got = abi_matmul(torch, cuda, x, qo, so)
+    # The golden output was made from the test loop's roundf codes; feed the
+    # same codes (they differ from rintf only on exact .5 quotients).
+    q_ref, s_ref = oracle.quantize(w, ties_away=True)
+    got = abi_matmul(torch, cuda, x, q_ref, s_ref)
     ref = golden["config1/out"]
     assert oracle.normwise_rel_err(got, ref) <= TOL_F32
     np.testing.assert_allclose(got, ref, rtol=0, atol=5e-5)
@@ -306,7 +309,8 @@ def test_quantize_full_size_roundtrip_property(cuda):
     q, s = pc.quantize(w)
     d = pc.dequantize(q, s)
     torch.cuda.synchronize()
-    assert bool(((d - w).abs() <= 0.5000001 * s[:, None]).all())
+    # |w/s - q| <= 1/2, plus the f32 roundings of w/s and q*s (|q| <= 127).
+    assert bool(((d - w).abs() <= (0.5 + 2.0 ** -15) * s[:, None]).all())
     assert int(q.abs().max()) == 127
     qo, so = oracle.quantize(w.cpu().numpy())
     assert np.array_equal(q.cpu().numpy(), qo) and np.array_equal(s.cpu().numpy(), so)
