@@ -83,6 +83,41 @@ int popcornDequantizeMatmulLaunchCount(
     popcornMatmulPath_t path
 );
 
+/*
+ * popcornDequantizeMatmul_i8f32 on the tensor-core path for callers that
+ * cannot let a library allocate device memory: processes that hand out all
+ * GPU memory through their own allocator (a cgo service accounting for every
+ * byte, a server reserving HBM for its caches) or that forbid allocation after
+ * start-up so a steady-state step can never fail or stall on it. There is no
+ * counterpart in the reference; popcorn's ABI has no scratch-free variant.
+ *
+ * It allocates nothing: its scratch is one fixed device array inside this
+ * library (16 MiB for f16 activations + 64 KiB for row scales) that every
+ * GPU loading the library holds until the process exits. Limits: K % 16 == 0,
+ * 16-byte aligned qweight, M <= 16384 and M*K*2 rounded up to 256 bytes
+ * <= 16 MiB (for example M = 2048 with K = 4096); anything larger, or a shape
+ * the tensor path cannot run, returns POPCORN_ERROR_INVALID_VALUE without
+ * launching. Results equal popcornDequantizeMatmulPath_i8f32 with
+ * POPCORN_MATMUL_PATH_TENSOR_F16.
+ *
+ * The first call on a device also looks up the array's device address and
+ * sets kernel attributes for that device; make that first call before any
+ * stream capture. Every call shares the one array and it keeps the last
+ * call's contents (nothing in it needs to start at zero): calls whose kernels
+ * overlap on the GPU -- on different streams, or from different host threads
+ * -- race on it and must be serialised by the caller.
+ */
+popcornStatus_t popcornDequantizeMatmulNoAlloc_i8f32(
+    float* out,
+    const float* x,
+    const int8_t* qweight,
+    const float* scale,
+    int64_t M,
+    int64_t N,
+    int64_t K,
+    cudaStream_t stream
+);
+
 /* Diagnostic: copies the current device's kernel error bits into *flags and
  * clears them (synchronous). Non-zero bits mean a bounded wait inside a
  * tensor-core kernel gave up (the kernel ended early instead of hanging);

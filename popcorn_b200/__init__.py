@@ -48,6 +48,7 @@ EXT_SYMBOLS = (
     "popcornDequantizeMatmulSelectPath",
     "popcornDequantizeMatmulLaunchCount",
     "popcornB200DeviceErrors",
+    "popcornDequantizeMatmulNoAlloc_i8f32",
 )
 
 _vp = ctypes.c_void_p
@@ -66,6 +67,7 @@ _SIGNATURES = {
     "popcornDequantizeMatmulSelectPath": (_int, [_vp, _vp, _i64, _i64, _i64]),
     "popcornDequantizeMatmulLaunchCount": (_int, [_vp, _vp, _i64, _i64, _i64, _int]),
     "popcornB200DeviceErrors": (_int, [ctypes.POINTER(ctypes.c_uint)]),
+    "popcornDequantizeMatmulNoAlloc_i8f32": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
 }
 
 _lib = None
@@ -134,6 +136,10 @@ def popcornDequantize_i8f32(out, qweight, scale, N, K, stream=0) -> int:
 
 def popcornDequantizeMatmulPath_i8f32(out, x, qweight, scale, M, N, K, path, stream=0) -> int:
     return load_library().popcornDequantizeMatmulPath_i8f32(out, x, qweight, scale, M, N, K, path, stream)
+
+
+def popcornDequantizeMatmulNoAlloc_i8f32(out, x, qweight, scale, M, N, K, stream=0) -> int:
+    return load_library().popcornDequantizeMatmulNoAlloc_i8f32(out, x, qweight, scale, M, N, K, stream)
 
 
 def select_path(x_ptr: int, q_ptr: int, M: int, N: int, K: int) -> int:

@@ -448,6 +448,113 @@ popcornStatus_t tc_dequant_matmul(float* out, const float* x, const int8_t* q, c
 
 }  // namespace pcb
 
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the tensor path.
+//
+// Some callers cannot let a library allocate device memory: a process whose
+// GPU memory is carved up once at start-up by its own allocator (a Go/cgo
+// service that accounts for every byte, or an inference server that reserves
+// almost all of HBM for its KV cache), or a real-time loop that forbids any
+// allocation after initialisation so it can never fail or stall mid-run. For
+// them, popcornDequantizeMatmulNoAlloc_i8f32 runs the same two kernels as the
+// tensor path with its scratch in the fixed array below instead of the pool.
+//
+// The array is a file-scope device variable: every GPU that loads this
+// library holds it (16 MiB + 64 KiB) until the process exits. In host code
+// its name is only a host-side stand-in, not a device address, so the entry
+// point looks up the real address with cudaGetSymbolAddress once per device
+// (with that device current) and passes that pointer to the kernels.
+// ---------------------------------------------------------------------------
+namespace pcb {
+namespace {
+
+constexpr size_t kNoAllocX16Bytes = size_t(16) << 20;  // f16 activations
+constexpr size_t kNoAllocRowBytes = size_t(64) << 10;  // f32 row scales
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocX16Bytes + kNoAllocRowBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device (looked up on
+// the first call per device, cached after).
+cudaError_t noalloc_scratch(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return e;
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace pcb
+
+extern "C" popcornStatus_t popcornDequantizeMatmulNoAlloc_i8f32(float* out, const float* x, const int8_t* qweight,
+                                                               const float* scale, int64_t M, int64_t N, int64_t K,
+                                                               cudaStream_t stream) {
+    using namespace pcb;
+    if (out == nullptr || x == nullptr || qweight == nullptr || scale == nullptr) {
+        return POPCORN_ERROR_INVALID_VALUE;
+    }
+    if (M <= 0 || N <= 0 || K <= 0) return POPCORN_SUCCESS;
+    if (!tc_supported(x, qweight, M, N, K)) return POPCORN_ERROR_INVALID_VALUE;
+    if (M > static_cast<int64_t>(kNoAllocRowBytes / 4) || K > static_cast<int64_t>(kNoAllocX16Bytes / 2)) {
+        return POPCORN_ERROR_INVALID_VALUE;
+    }
+    const size_t x16_bytes = (static_cast<size_t>(M) * K * 2 + 255) & ~size_t(255);
+    if (x16_bytes > kNoAllocX16Bytes) return POPCORN_ERROR_INVALID_VALUE;
+    PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
+    if (encode == nullptr) return POPCORN_ERROR_INVALID_VALUE;
+
+    void* scratch = nullptr;
+    cudaError_t e = noalloc_scratch(&scratch);
+    if (e != cudaSuccess) return record_cuda(e);
+    __half* x16 = static_cast<__half*>(scratch);
+    float* rowscale = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + kNoAllocX16Bytes);
+
+    // The prologue writes every x16 element and row scale the GEMM reads (tile
+    // edges past M or K are zero-filled by TMA, not read from the array), so
+    // nothing left in the array by an earlier call needs clearing.
+    const int vec = aligned16(x) ? 1 : 0;
+    int64_t blocks = ceil_div(M, 8);
+    const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
+    if (blocks > cap) blocks = cap;
+    x_to_f16_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x16, rowscale, x, M, K, vec);
+    popcornStatus_t st = check_launch();
+    if (st != POPCORN_SUCCESS) return st;
+
+    const int bm = pick_bm(M);
+    CUtensorMap tx, tw;
+    const cuuint64_t xdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    const cuuint64_t xstride[1] = {static_cast<cuuint64_t>(K) * 2};
+    const cuuint32_t xbox[2] = {kBK, static_cast<cuuint32_t>(bm)};
+    const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+    const cuuint64_t wstride[1] = {static_cast<cuuint64_t>(K)};
+    const cuuint32_t wbox[2] = {kBK, kTileN};
+    const cuuint32_t estride[2] = {1, 1};
+    CUresult r1 = encode(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, xdims, xstride, xbox, estride,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r2 = encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(qweight), wdims, wstride, wbox,
+                         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS) return POPCORN_ERROR_INVALID_VALUE;
+    switch (bm) {
+        case 32: return launch_gemm<32>(0, tx, tw, out, scale, rowscale, M, N, K, stream);
+        case 64: return launch_gemm<64>(1, tx, tw, out, scale, rowscale, M, N, K, stream);
+        case 128: return launch_gemm<128>(2, tx, tw, out, scale, rowscale, M, N, K, stream);
+        default: return launch_gemm<256>(3, tx, tw, out, scale, rowscale, M, N, K, stream);
+    }
+}
+
 extern "C" int popcornB200DeviceErrors(unsigned int* flags) {
     if (flags == nullptr) return POPCORN_ERROR_INVALID_VALUE;
     unsigned int zero = 0;
