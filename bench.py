@@ -239,6 +239,12 @@ def time_graph(torch, setup, steps, warmup, soak_s, sampler, dist_on):
     stream.synchronize()
     once = time.perf_counter() - t_soak0
     reps = max(1, int(soak_s / max(once, 1e-6)))
+    if dist_on:
+        # Every rank must replay the same number of graphs (each holds the
+        # same sequence of NCCL collectives), so agree on the count.
+        t = torch.tensor([reps], dtype=torch.int64, device=torch.device("cuda", torch.cuda.current_device()))
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        reps = int(t.item())
     with torch.cuda.stream(stream):
         for _ in range(reps):
             graph.replay()

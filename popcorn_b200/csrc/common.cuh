@@ -51,6 +51,10 @@ popcornStatus_t tc_dequant_matmul(float* out, const float* x, const int8_t* q,
                                   int64_t K, cudaStream_t stream);
 int tc_launch_count(int64_t M, int64_t N, int64_t K);
 
+// Read and clear the device error words of the bounded-wait kernels.
+cudaError_t tc_take_errors(unsigned int* bits);
+cudaError_t gemv_take_errors(unsigned int* bits);
+
 }  // namespace pcb
 
 #endif  // POPCORN_B200_COMMON_CUH

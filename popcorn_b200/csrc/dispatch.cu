@@ -91,3 +91,12 @@ extern "C" int popcornDequantizeMatmulLaunchCount(const float* x, const int8_t* 
     }
     return pcb::simt_launch_count(x, qweight, M, N, K);
 }
+
+extern "C" int popcornB200DeviceErrors(unsigned int* flags) {
+    if (flags == nullptr) return POPCORN_ERROR_INVALID_VALUE;
+    unsigned int a = 0, b = 0;
+    cudaError_t e = pcb::tc_take_errors(&a);
+    if (e == cudaSuccess) e = pcb::gemv_take_errors(&b);
+    *flags = a | (b << 16);
+    return pcb::record_cuda(e);
+}

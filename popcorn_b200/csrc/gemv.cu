@@ -30,6 +30,11 @@
 #include "common.cuh"
 
 namespace pcb {
+
+// Error bits of bounded waits in this file's kernels (read by
+// popcornB200DeviceErrors); none of the current kernels waits on a barrier.
+__device__ unsigned int g_gemv_error = 0;
+
 namespace {
 
 // Four int8 codes (one 32-bit word) -> four exact floats.
@@ -99,8 +104,11 @@ __device__ __forceinline__ float warp_reduce_scatter(float (&v)[V], int lane) {
 
 // MT activation rows (<= 4), U 16-element K slices per thread, R weight rows
 // per iteration. Block b owns weight rows [b*rpc, min(N, (b+1)*rpc)).
-template <int MT, int U, int R>
-__global__ void __launch_bounds__(kXsThreads, (MT * U <= 1) ? 4 : 2)
+// PIPE: blocks own several row groups and overlap the next group's loads with
+// the current group's math (more registers, two blocks per SM); without it a
+// block owns one row group and four blocks fit per SM.
+template <int MT, int U, int R, bool PIPE>
+__global__ void __launch_bounds__(kXsThreads, (MT * U <= 1 && !PIPE) ? 4 : 2)
 gemv_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* __restrict__ q,
                const float* __restrict__ scale, int64_t M, int64_t N, int64_t K, int rpc) {
     extern __shared__ float part[];  // [rpc][MT][kXsWarps]
@@ -110,6 +118,27 @@ gemv_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_
     const int64_t units = K >> 4;
     const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rpc;
     const int64_t r1 = (r0 + rpc < N) ? r0 + rpc : N;
+
+    // Programmatic dependent launch: let the next kernel in the stream start
+    // as soon as SM resources free up, and, before waiting for the previous
+    // kernel, pull this block's weight rows into L2. A prefetch is only a
+    // hint (L2 is the coherence point), so it is safe even if the previous
+    // kernel writes these rows; every real read happens after the wait.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (tid < kXsWarps && blockIdx.y == 0) {
+        // The first two row groups: enough to cover the previous kernel's tail.
+        const int64_t bytes = ((r1 - r0) < 2 * R ? (r1 - r0) : 2 * R) * K;
+        const int64_t chunk = (bytes + kXsWarps - 1) / kXsWarps;
+        const int64_t c0 = (static_cast<int64_t>(tid) * chunk) & ~int64_t(15);
+        int64_t c1 = (static_cast<int64_t>(tid + 1) * chunk) & ~int64_t(15);
+        if (tid == kXsWarps - 1 || c1 > bytes) c1 = bytes;
+        if (c1 > c0) {
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(q + r0 * K + c0),
+                         "r"(static_cast<uint32_t>(c1 - c0))
+                         : "memory");
+        }
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     for (int64_t m0 = static_cast<int64_t>(blockIdx.y) * MT; m0 < M; m0 += static_cast<int64_t>(gridDim.y) * MT) {
         // Activations of this thread's K slices, kept in registers.
@@ -134,19 +163,35 @@ gemv_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_
             }
         }
 
-        for (int64_t rb = r0; rb < r1; rb += R) {
-            uint4 w[R][U];
+        // With PIPE, row groups of R are software-pipelined: the next group's
+        // loads are in flight while the current group is multiplied and
+        // reduced. Without it each group is loaded at the top of its iteration.
+        uint4 wn[R][U];
+        auto load_group = [&](int64_t rb, uint4 (&dst)[R][U]) {
             #pragma unroll
             for (int r = 0; r < R; ++r) {
                 #pragma unroll
                 for (int u = 0; u < U; ++u) {
                     const int64_t unit = tid + static_cast<int64_t>(u) * kXsThreads;
                     if (rb + r < r1 && unit < units) {
-                        w[r][u] = __ldg(reinterpret_cast<const uint4*>(q + (rb + r) * K) + unit);
+                        dst[r][u] = __ldg(reinterpret_cast<const uint4*>(q + (rb + r) * K) + unit);
                     } else {
-                        w[r][u] = make_uint4(0u, 0u, 0u, 0u);  // code 0
+                        dst[r][u] = make_uint4(0u, 0u, 0u, 0u);  // code 0
                     }
                 }
+            }
+        };
+        if constexpr (PIPE) load_group(r0, wn);
+        for (int64_t rb = r0; rb < r1; rb += R) {
+            uint4 w[R][U];
+            if constexpr (PIPE) {
+                #pragma unroll
+                for (int r = 0; r < R; ++r)
+                    #pragma unroll
+                    for (int u = 0; u < U; ++u) w[r][u] = wn[r][u];
+                if (rb + R < r1) load_group(rb + R, wn);
+            } else {
+                load_group(rb, w);
             }
             float acc[R * MT];
             #pragma unroll
@@ -194,6 +239,7 @@ gemv_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_
         __syncthreads();
     }
 }
+
 
 // --------------------------------------------------------------- gemv_kernel
 constexpr int kGemvWarps = 4;
@@ -359,11 +405,11 @@ popcornStatus_t launch_gemv(int slot, float* out, const float* x, const int8_t* 
     return check_launch();
 }
 
-// Rows per block for the x-stationary kernel: every block of the grid is
-// resident at once (one wave), each owning an equal share of the rows.
+// Rows per block for the x-stationary kernel so that the whole grid is
+// resident at once (one wave).
 template <typename Kern>
 int xs_rows_per_block(Kern kernel, int slot, int64_t N) {
-    static int occ_cache[kMaxDevices][8] = {};
+    static int occ_cache[kMaxDevices][16] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     int occ = (dev >= 0 && dev < kMaxDevices) ? occ_cache[dev][slot] : 0;
@@ -385,17 +431,42 @@ int xs_rows_per_block(Kern kernel, int slot, int64_t N) {
 template <int MT, int U, int R>
 popcornStatus_t launch_xs(int slot, float* out, const float* x, const int8_t* q, const float* scale, int64_t M,
                           int64_t N, int64_t K, cudaStream_t stream) {
-    const int rpc = xs_rows_per_block(gemv_xs_kernel<MT, U, R>, slot, N);
+    // One row group of R rows per block while a single wave of resident
+    // blocks holds the grid (every thread has all its loads in flight at
+    // once); otherwise fewer, pipelined blocks that stream several groups.
+    int rpc = xs_rows_per_block(gemv_xs_kernel<MT, U, R, false>, 2 * slot, N);
+    const bool pipe = rpc > R;
+    if (pipe) rpc = xs_rows_per_block(gemv_xs_kernel<MT, U, R, true>, 2 * slot + 1, N);
+    if (rpc < R) rpc = R;
     const int smem = rpc * MT * kXsWarps * static_cast<int>(sizeof(float));
     const int64_t gx = ceil_div(N, rpc);
     int64_t gy = ceil_div(M, MT);
     if (gy > 65535) gy = 65535;
-    dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
-    gemv_xs_kernel<MT, U, R><<<grid, kXsThreads, smem, stream>>>(out, x, q, scale, M, N, K, rpc);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
+    cfg.blockDim = dim3(kXsThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = pipe ? cudaLaunchKernelEx(&cfg, gemv_xs_kernel<MT, U, R, true>, out, x, q, scale, M, N, K, rpc)
+                         : cudaLaunchKernelEx(&cfg, gemv_xs_kernel<MT, U, R, false>, out, x, q, scale, M, N, K, rpc);
+    if (e != cudaSuccess) return record_cuda(e);
     return check_launch();
 }
 
+
 }  // namespace
+
+cudaError_t gemv_take_errors(unsigned int* bits) {
+    unsigned int zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(bits, g_gemv_error, sizeof(unsigned int));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_gemv_error, &zero, sizeof(unsigned int));
+    return e;
+}
 
 int simt_launch_count(const float*, const int8_t*, int64_t M, int64_t N, int64_t K) {
     return (M > 0 && N > 0 && K > 0) ? 1 : 0;

@@ -44,13 +44,13 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kBK = 64;        // K elements per pipeline stage
 constexpr int kTileN = 128;    // weight rows per CTA (MMA M)
-constexpr int kAStages = 4;    // tensor-memory A buffers, 32 columns each
-constexpr int kThreads = 320;  // 10 warps
+constexpr int kThreads = 448;  // 14 warps
 constexpr int kWarpTma = 0;
 constexpr int kWarpMma = 1;
-constexpr int kWarpEpi0 = 6;
+constexpr int kWarpConv0 = 2;  // two groups of four converter warps: 2-5, 6-9
+constexpr int kConvGroups = 2;
+constexpr int kWarpEpi0 = 10;
 
 constexpr int pow2_at_least(int v) {
     int p = 32;
@@ -58,15 +58,27 @@ constexpr int pow2_at_least(int v) {
     return p;
 }
 
+// Per tile shape: K elements per stage (kBK), ring depths filling ~200 KB of
+// shared memory and the 512 tensor-memory columns left after the accumulator.
+// The weight tile of a stage is [128 rows x kBK bytes]; HBM streams such a
+// row-strided tile far better with 128-byte rows than with 64-byte rows
+// (measured with plain TMA streaming: 4.1 vs 2.7 TB/s), so every shape whose
+// activation tile leaves room uses kBK = 128.
 template <int BM>
 struct Cfg {
-    static constexpr int kStages = BM >= 256 ? 4 : (BM >= 128 ? 6 : 8);
+    static constexpr int kBK = BM >= 256 ? 64 : 128;
+    static constexpr int kSub = kBK / 64;           // 64-wide f16 swizzle atoms per stage
+    static constexpr int kACols = kBK / 2;          // tensor-memory columns per A buffer
+    static constexpr int kStages = BM >= 256 ? 5 : (BM >= 128 ? 4 : (BM >= 64 ? 6 : 8));
+    static constexpr int kAStages = BM >= 256 ? 8 : (BM >= 128 ? 6 : 7);
     static constexpr int kXBytes = BM * kBK * 2;   // f16 activation tile per stage
     static constexpr int kWBytes = kTileN * kBK;   // int8 weight tile per stage
-    static constexpr int kTmemCols = pow2_at_least(BM + kAStages * 32);
+    static constexpr int kTmemCols = pow2_at_least(BM + kAStages * kACols);
     static constexpr int kNumBars = 2 * kStages + 2 * kAStages + 2;
     static constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16;
     static_assert(kXBytes % 1024 == 0, "x16 stages must stay 1024-byte aligned");
+    static_assert(kTmemCols <= 512, "tensor memory holds 512 columns");
+    static_assert(kSmem <= 227 * 1024, "shared memory per block");
 };
 
 __device__ __forceinline__ float absmax_step(float m, float v) {
@@ -153,10 +165,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
                int M, int N, int K) {
     using C = Cfg<BM>;
     constexpr int S = C::kStages;
+    constexpr int kAStages = C::kAStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* xs = smem;                                  // S x [BM][64] f16, 128B swizzle
-    uint8_t* ws = smem + S * C::kXBytes;                 // S x [128][64] int8, 64B swizzle
+    constexpr int kBK = C::kBK;
+    uint8_t* xs = smem;                                  // S x kSub x [BM][64] f16, 128B swizzle
+    uint8_t* ws = smem + S * C::kXBytes;                 // S x [128][kBK] int8, 64B/128B swizzle
     uint64_t* bars = reinterpret_cast<uint64_t*>(ws + S * C::kWBytes);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
 
@@ -171,7 +185,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
     const int lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * kTileN;
     const int m0 = blockIdx.y * BM;
-    const int num_kb = (K + kBK - 1) / kBK;
+    const int num_kb = (K + C::kBK - 1) / C::kBK;
     unsigned int* err = &g_tc_error;
 
     if (threadIdx.x == 0) {
@@ -200,7 +214,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t acc_tmem = tmem;          // columns [0, BM)
-    const uint32_t a_tmem0 = tmem + BM;      // A buffers at columns BM + 32 * a
+    const uint32_t a_tmem0 = tmem + BM;      // A buffers at columns BM + kACols * a
 
     if (warp == kWarpTma) {
         if (lane == 0) {
@@ -208,7 +222,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
                 const int s = kb % S;
                 if (kb >= S && !mbar_wait(empty0 + 8 * s, ((kb / S) - 1) & 1, err, 1u)) break;
                 mbar_arrive_expect_tx(full0 + 8 * s, C::kXBytes + C::kWBytes);
-                tma_load_2d(smem_addr(xs + s * C::kXBytes), &tmap_x, kb * kBK, m0, full0 + 8 * s);
+                #pragma unroll
+                for (int sub = 0; sub < C::kSub; ++sub) {
+                    tma_load_2d(smem_addr(xs + s * C::kXBytes + sub * BM * 128), &tmap_x, kb * kBK + sub * 64, m0,
+                                full0 + 8 * s);
+                }
                 tma_load_2d(smem_addr(ws + s * C::kWBytes), &tmap_w, kb * kBK, n0, full0 + 8 * s);
             }
             // Nothing of ours may still be landing in shared memory at exit:
@@ -226,12 +244,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
                 if (!mbar_wait(full0 + 8 * s, (kb / S) & 1, err, 2u)) break;
                 if (!mbar_wait(afull0 + 8 * a, (kb / kAStages) & 1, err, 4u)) break;
                 tc_fence_after();
-                const uint64_t bdesc = smem_desc_sw128_kmajor(smem_addr(xs + s * C::kXBytes));
                 #pragma unroll
                 for (int j = 0; j < kBK / 16; ++j) {
-                    // K step of 16 f16 = 32 bytes inside the 128-byte swizzle row.
-                    mma_f16_ts(acc_tmem, a_tmem0 + a * 32 + j * 8, bdesc + static_cast<uint64_t>(j * 2), idesc,
-                               (kb | j) != 0 ? 1u : 0u);
+                    // K step of 16 f16 = 32 bytes inside a 128-byte swizzle row of
+                    // the (j / 4)-th 64-wide atom of the activation tile.
+                    const uint64_t bdesc =
+                        smem_desc_sw128_kmajor(smem_addr(xs + s * C::kXBytes + (j / 4) * BM * 128));
+                    mma_f16_ts(acc_tmem, a_tmem0 + a * C::kACols + j * 8, bdesc + static_cast<uint64_t>((j % 4) * 2),
+                               idesc, (kb | j) != 0 ? 1u : 0u);
                 }
                 mma_commit(empty0 + 8 * s);
                 mma_commit(aempty0 + 8 * a);
@@ -243,10 +263,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
         }
     } else if (warp < kWarpEpi0) {
         // Converters: thread owns weight row r of the tile = tensor-memory lane r.
+        // Two groups of four warps take alternate k-steps, so two conversions
+        // are always in flight.
         const int quarter = warp & 3;
+        const int group = (warp - kWarpConv0) >> 2;
         const int r = quarter * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = group; kb < num_kb; kb += kConvGroups) {
             const int s = kb % S;
             const int a = kb % kAStages;
             bool ok = mbar_wait(full0 + 8 * s, (kb / S) & 1, err, 8u);
@@ -255,19 +278,27 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
             const uint8_t* row = ws + s * C::kWBytes + r * kBK;
-            uint32_t w[16];
             #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ ((r >> 1) & 3)) << 4));
-                w[4 * c + 0] = v.x;
-                w[4 * c + 1] = v.y;
-                w[4 * c + 2] = v.z;
-                w[4 * c + 3] = v.w;
+            for (int g = 0; g < kBK / 64; ++g) {
+                // 64 codes (four 16-byte chunks) -> 32 f16x2 columns. The tile was
+                // written by TMA with a 64B swizzle (kBK = 64: chunk ^= (r >> 1) & 3)
+                // or a 128B swizzle (kBK = 128: chunk ^= r & 7).
+                uint32_t w[16];
+                #pragma unroll
+                for (int c4 = 0; c4 < 4; ++c4) {
+                    const int c = g * 4 + c4;
+                    const int phys = (kBK == 64) ? (c ^ ((r >> 1) & 3)) : (c ^ (r & 7));
+                    const uint4 v = *reinterpret_cast<const uint4*>(row + (phys << 4));
+                    w[4 * c4 + 0] = v.x;
+                    w[4 * c4 + 1] = v.y;
+                    w[4 * c4 + 2] = v.z;
+                    w[4 * c4 + 3] = v.w;
+                }
+                uint32_t h[32];
+                #pragma unroll
+                for (int i = 0; i < 16; ++i) widen4_f16(w[i], h[2 * i], h[2 * i + 1]);
+                tmem_st_32x32b_x32(tmem + lane_addr + BM + a * C::kACols + g * 32, h);
             }
-            uint32_t h[32];
-            #pragma unroll
-            for (int i = 0; i < 16; ++i) widen4_f16(w[i], h[2 * i], h[2 * i + 1]);
-            tmem_st_32x32b_x32(tmem + lane_addr + BM + a * 32, h);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -381,6 +412,29 @@ int pick_bm(int64_t M) {
     return 256;
 }
 
+// Tensor maps of one call: x16 [M, K] f16 in [bm x 64] boxes (128B swizzle),
+// qweight [N, K] int8 in [128 x bk] boxes (bk = 64: 64B swizzle, bk = 128:
+// 128B swizzle), matching Cfg<bm>.
+bool make_maps(PFN_cuTensorMapEncodeTiled_v12000 encode, __half* x16, const int8_t* q, int64_t M, int64_t N,
+               int64_t K, int bm, CUtensorMap* tx, CUtensorMap* tw) {
+    const int bk = bm >= 256 ? 64 : 128;
+    const cuuint64_t xdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    const cuuint64_t xstride[1] = {static_cast<cuuint64_t>(K) * 2};
+    const cuuint32_t xbox[2] = {64, static_cast<cuuint32_t>(bm)};
+    const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+    const cuuint64_t wstride[1] = {static_cast<cuuint64_t>(K)};
+    const cuuint32_t wbox[2] = {static_cast<cuuint32_t>(bk), kTileN};
+    const cuuint32_t estride[2] = {1, 1};
+    CUresult r1 = encode(tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, xdims, xstride, xbox, estride,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r2 = encode(tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q), wdims, wstride, wbox, estride,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         bk == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r1 == CUDA_SUCCESS && r2 == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 bool tc_supported(const float*, const int8_t* q, int64_t M, int64_t N, int64_t K) {
@@ -417,22 +471,7 @@ popcornStatus_t tc_dequant_matmul(float* out, const float* x, const int8_t* q, c
 
     const int bm = pick_bm(M);
     CUtensorMap tx, tw;
-    if (st == POPCORN_SUCCESS) {
-        const cuuint64_t xdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
-        const cuuint64_t xstride[1] = {static_cast<cuuint64_t>(K) * 2};
-        const cuuint32_t xbox[2] = {kBK, static_cast<cuuint32_t>(bm)};
-        const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
-        const cuuint64_t wstride[1] = {static_cast<cuuint64_t>(K)};
-        const cuuint32_t wbox[2] = {kBK, kTileN};
-        const cuuint32_t estride[2] = {1, 1};
-        CUresult r1 = encode(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, xdims, xstride, xbox, estride,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        CUresult r2 = encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q), wdims, wstride, wbox,
-                             estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
-                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS) st = POPCORN_ERROR_INVALID_VALUE;
-    }
+    if (st == POPCORN_SUCCESS && !make_maps(encode, x16, q, M, N, K, bm, &tx, &tw)) st = POPCORN_ERROR_INVALID_VALUE;
     if (st == POPCORN_SUCCESS) {
         switch (bm) {
             case 32: st = launch_gemm<32>(0, tx, tw, out, scale, rowscale, M, N, K, stream); break;
@@ -533,20 +572,7 @@ extern "C" popcornStatus_t popcornDequantizeMatmulNoAlloc_i8f32(float* out, cons
 
     const int bm = pick_bm(M);
     CUtensorMap tx, tw;
-    const cuuint64_t xdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
-    const cuuint64_t xstride[1] = {static_cast<cuuint64_t>(K) * 2};
-    const cuuint32_t xbox[2] = {kBK, static_cast<cuuint32_t>(bm)};
-    const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
-    const cuuint64_t wstride[1] = {static_cast<cuuint64_t>(K)};
-    const cuuint32_t wbox[2] = {kBK, kTileN};
-    const cuuint32_t estride[2] = {1, 1};
-    CUresult r1 = encode(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, xdims, xstride, xbox, estride,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    CUresult r2 = encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(qweight), wdims, wstride, wbox,
-                         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS) return POPCORN_ERROR_INVALID_VALUE;
+    if (!make_maps(encode, x16, qweight, M, N, K, bm, &tx, &tw)) return POPCORN_ERROR_INVALID_VALUE;
     switch (bm) {
         case 32: return launch_gemm<32>(0, tx, tw, out, scale, rowscale, M, N, K, stream);
         case 64: return launch_gemm<64>(1, tx, tw, out, scale, rowscale, M, N, K, stream);
@@ -555,10 +581,11 @@ extern "C" popcornStatus_t popcornDequantizeMatmulNoAlloc_i8f32(float* out, cons
     }
 }
 
-extern "C" int popcornB200DeviceErrors(unsigned int* flags) {
-    if (flags == nullptr) return POPCORN_ERROR_INVALID_VALUE;
+namespace pcb {
+cudaError_t tc_take_errors(unsigned int* bits) {
     unsigned int zero = 0;
-    cudaError_t e = cudaMemcpyFromSymbol(flags, pcb::g_tc_error, sizeof(unsigned int));
-    if (e == cudaSuccess) e = cudaMemcpyToSymbol(pcb::g_tc_error, &zero, sizeof(unsigned int));
-    return pcb::record_cuda(e);
+    cudaError_t e = cudaMemcpyFromSymbol(bits, g_tc_error, sizeof(unsigned int));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_tc_error, &zero, sizeof(unsigned int));
+    return e;
 }
+}  // namespace pcb

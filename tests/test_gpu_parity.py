@@ -425,3 +425,19 @@ def test_tensor_path_back_to_back_calls_reuse_scratch(cuda):
     ref = oracle.dequant_matmul(x, q, s, fused=True, threads=8)
     for i, o in enumerate(outs):
         assert oracle.normwise_rel_err(o.cpu().numpy() / (i + 1), ref) <= 5e-4
+
+
+@pytest.mark.parametrize("M,N,K", [
+    (1, 4096, 4096), (1, 1100, 4096), (1, 1000, 8192), (1, 777, 16384), (1, 1031, 11008),
+    (1, 5000, 1024), (2, 4096, 4096), (2, 999, 8192), (3, 2000, 4096), (4, 4097, 4096), (4, 300, 4096),
+])
+def test_bulk_gemv_variants(cuda, M, N, K):
+    # Every template variant of the bulk-staged decode GEMV (f32 path, M <= 4).
+    import torch
+
+    assert M * N * K > (1 << 22)
+    x, q, s = random_case(M, N, K, 7 * M + N)
+    got = abi_matmul(torch, cuda, x, q, s)
+    assert pc.device_errors() == 0
+    ref = oracle.dequant_matmul(x, q, s, fused=True, threads=8)
+    assert oracle.normwise_rel_err(got, ref) <= TOL_F32
