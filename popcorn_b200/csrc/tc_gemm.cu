@@ -144,6 +144,108 @@ x_to_f16_kernel(__half* __restrict__ x16, float* __restrict__ rowscale, const fl
     }
 }
 
+// Same conversion, one block per row with the row held in registers (U
+// 16-float slices per thread, K <= 16 * 256 * U): x is read from HBM once and
+// every thread has all of its loads in flight at once. Needs K % 16 == 0 and
+// a 16-byte aligned x.
+constexpr int kRowThreads = 256;
+
+template <int U>
+__global__ void __launch_bounds__(kRowThreads)
+x_to_f16_row_kernel(__half* __restrict__ x16, float* __restrict__ rowscale, const float* __restrict__ x, int64_t M,
+                    int64_t K) {
+    __shared__ float red[2][kRowThreads / 32];
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int64_t units = K >> 4;
+    int parity = 0;
+    for (int64_t row = blockIdx.x; row < M; row += gridDim.x, parity ^= 1) {
+        const float4* r4 = reinterpret_cast<const float4*>(x + row * K);
+        float4 v[U][4];
+        #pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t unit = tid + static_cast<int64_t>(u) * kRowThreads;
+            #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                v[u][c] = (unit < units) ? __ldg(r4 + unit * 4 + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+        }
+        float m = 0.0f;
+        #pragma unroll
+        for (int u = 0; u < U; ++u)
+            #pragma unroll
+            for (int c = 0; c < 4; ++c)
+                m = absmax_step(absmax_step(absmax_step(absmax_step(m, v[u][c].x), v[u][c].y), v[u][c].z), v[u][c].w);
+        #pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float other = __shfl_xor_sync(0xffffffffu, m, off);
+            m = (other > m) ? other : m;
+        }
+        if (lane == 0) red[parity][warp] = m;
+        __syncthreads();
+        m = red[parity][0];
+        #pragma unroll
+        for (int w = 1; w < kRowThreads / 32; ++w) {
+            const float other = red[parity][w];
+            m = (other > m) ? other : m;
+        }
+        int e = 0;
+        if (m > 0.0f && m <= 3.402823466e38f) {
+            int p;
+            frexpf(m, &p);
+            e = 15 - p;
+            e = e < -126 ? -126 : (e > 126 ? 126 : e);
+        }
+        const float up = __int_as_float((e + 127) << 23);
+        if (tid == 0) rowscale[row] = __int_as_float((127 - e) << 23);
+        uint4* o8 = reinterpret_cast<uint4*>(x16 + row * K);
+        #pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t unit = tid + static_cast<int64_t>(u) * kRowThreads;
+            if (unit < units) {
+                #pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const float4 a = v[u][2 * h];
+                    const float4 b = v[u][2 * h + 1];
+                    __half2 h0 = __floats2half2_rn(a.x * up, a.y * up);
+                    __half2 h1 = __floats2half2_rn(a.z * up, a.w * up);
+                    __half2 h2 = __floats2half2_rn(b.x * up, b.y * up);
+                    __half2 h3 = __floats2half2_rn(b.z * up, b.w * up);
+                    uint4 packed;
+                    packed.x = *reinterpret_cast<uint32_t*>(&h0);
+                    packed.y = *reinterpret_cast<uint32_t*>(&h1);
+                    packed.z = *reinterpret_cast<uint32_t*>(&h2);
+                    packed.w = *reinterpret_cast<uint32_t*>(&h3);
+                    o8[unit * 2 + h] = packed;
+                }
+            }
+        }
+    }
+}
+
+// Launch the x -> f16 prologue: block-per-row kernel where it applies.
+popcornStatus_t launch_x_to_f16(__half* x16, float* rowscale, const float* x, int64_t M, int64_t K,
+                                cudaStream_t stream) {
+    const bool vec = aligned16(x);
+    const int64_t slices = ceil_div(K / 16, kRowThreads);
+    if (vec && K % 16 == 0 && K >= 1024 && slices <= 4) {
+        int64_t blocks = M;
+        const int64_t cap = static_cast<int64_t>(device_sm_count()) * 8;
+        if (blocks > cap) blocks = cap;
+        const unsigned g = static_cast<unsigned>(blocks);
+        if (slices == 1) x_to_f16_row_kernel<1><<<g, kRowThreads, 0, stream>>>(x16, rowscale, x, M, K);
+        else if (slices == 2) x_to_f16_row_kernel<2><<<g, kRowThreads, 0, stream>>>(x16, rowscale, x, M, K);
+        else x_to_f16_row_kernel<4><<<g, kRowThreads, 0, stream>>>(x16, rowscale, x, M, K);
+        return check_launch();
+    }
+    int64_t blocks = ceil_div(M, 8);
+    const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
+    if (blocks > cap) blocks = cap;
+    x_to_f16_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x16, rowscale, x, M, K, vec ? 1 : 0);
+    return check_launch();
+}
+
 // Four int8 codes (one word) -> two f16x2 words, exact:
 // (code ^ 0x80) in the low byte of f16 0x6400 gives 1024 + 128 + code;
 // subtracting 1152 leaves the code.
@@ -341,6 +443,223 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
     }
 }
 
+// ------------------------------------------------------------ CTA-pair kernel
+// Large M: a cluster of two CTAs computes a 256 (weight rows) x 256
+// (activation rows) tile with tcgen05.mma.cta_group::2. CTA r of the pair
+// converts its own 128 weight rows into its own tensor memory (the A operand
+// is split by rows across the pair) and loads only its half of the
+// activation tile (the B operand is split the same way), so each CTA moves
+// half the tiles a single CTA with the same output tile would (48 KB per
+// 128-deep k-step), and the pair's MMA work per k-step doubles.
+// The leader CTA (rank 0) issues the MMAs; the pair synchronises through the
+// leader's mbarriers:
+//   full[s]   activation halves of both CTAs landed (TMA .cta_group::2 loads
+//             complete their bytes on the leader's barrier; only the leader
+//             posts the expected byte count);
+//   wfull[s]  this CTA's weight tile landed (local);
+//   afull[a]  both CTAs' converters wrote A buffer a (8 remote arrivals);
+//   empty[s], aempty[a], acc_full, drain: multicast tcgen05.commit from the
+//             leader to the same barrier in both CTAs.
+// Stages are 128 deep in K: a CTA's TMA ring costs a roughly fixed time per
+// iteration (measured on this part: ~0.4 us whether a stage carries 8 KB or
+// 40 KB), so fewer, bigger stages move the same bytes in half the iterations.
+namespace pair {
+constexpr int kBK = 128;
+constexpr int kSub = kBK / 64;                     // 64-wide f16 swizzle atoms per stage
+constexpr int kRowsX = 128;                        // activation rows per CTA (half of 256)
+constexpr int kStages = 4;
+constexpr int kAStages = 4;                        // 64 columns each
+constexpr int kACols = kBK / 2;
+constexpr int kXBytes = kRowsX * kBK * 2;          // 32 KB (two 16 KB swizzle atoms)
+constexpr int kWBytes = kTileN * kBK;              // 16 KB
+constexpr int kTmemCols = 512;                     // 256 accumulator + 4 x 64 A
+constexpr int kNumBars = 3 * kStages + 2 * kAStages + 2;
+constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16;
+static_assert(kSmem <= 227 * 1024, "shared memory per block");
+}  // namespace pair
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                    float* __restrict__ out, const float* __restrict__ scale, const float* __restrict__ rowscale,
+                    int M, int N, int K) {
+    using namespace pair;
+    constexpr int S = kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* xs = smem;                                  // S x kSub x [128][64] f16, 128B swizzle
+    uint8_t* ws = smem + S * kXBytes;                    // S x [128][128] int8, 128B swizzle
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ws + S * kWBytes);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+
+    const uint32_t full0 = smem_addr(bars);
+    const uint32_t wfull0 = full0 + 8 * S;
+    const uint32_t empty0 = wfull0 + 8 * S;
+    const uint32_t afull0 = empty0 + 8 * S;
+    const uint32_t aempty0 = afull0 + 8 * kAStages;
+    const uint32_t acc_full = aempty0 + 8 * kAStages;
+    const uint32_t drain = acc_full + 8;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int n0 = (blockIdx.x >> 1) * (2 * kTileN) + static_cast<int>(rank) * kTileN;  // this CTA's weight rows
+    const int mp = blockIdx.y * (2 * kRowsX);                                          // pair's activation rows
+    const int num_kb = (K + kBK - 1) / kBK;
+    unsigned int* err = &g_tc_error;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(wfull0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        for (int a = 0; a < kAStages; ++a) {
+            mbar_init(afull0 + 8 * a, 2 * 4);  // four converter warps in each CTA
+            mbar_init(aempty0 + 8 * a, 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (warp == kWarpTma && lane == 0) {
+        tma_prefetch_desc(&tmap_x);
+        tma_prefetch_desc(&tmap_w);
+    }
+    if (warp == kWarpMma) {
+        tmem_alloc_pair(smem_addr(tmem_slot), kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // the peer's barriers exist before anyone arrives on them
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t a_tmem0 = tmem + 2 * kRowsX;  // A buffers after the 256 accumulator columns
+
+    if (warp == kWarpTma) {
+        if (lane == 0) {
+            const uint32_t full_leader0 = mapa_shared(full0, 0);
+            for (int kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % S;
+                if (kb >= S && !mbar_wait_cluster(empty0 + 8 * s, ((kb / S) - 1) & 1, err, 1u)) break;
+                if (leader) mbar_arrive_expect_tx(full0 + 8 * s, 2 * kXBytes);
+                mbar_arrive_expect_tx(wfull0 + 8 * s, kWBytes);
+                #pragma unroll
+                for (int sub = 0; sub < kSub; ++sub) {
+                    tma_load_2d_pair(smem_addr(xs + s * kXBytes + sub * kRowsX * 128), &tmap_x, kb * kBK + sub * 64,
+                                     mp + static_cast<int>(rank) * kRowsX, full_leader0 + 8 * s);
+                }
+                tma_load_2d(smem_addr(ws + s * kWBytes), &tmap_w, kb * kBK, n0, wfull0 + 8 * s);
+            }
+            // Leave no copy of ours in flight: the weight tiles signal this CTA;
+            // the activation halves are covered by the drain below (the leader
+            // consumes every stage before it commits the drain).
+            for (int kb = (num_kb > S ? num_kb - S : 0); kb < num_kb; ++kb) {
+                mbar_wait(wfull0 + 8 * (kb % S), (kb / S) & 1, err, 64u);
+            }
+        }
+    } else if (warp == kWarpMma) {
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = idesc_f16_f32(2 * kTileN, 2 * kRowsX);
+            for (int kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % S;
+                const int a = kb % kAStages;
+                if (!mbar_wait_cluster(full0 + 8 * s, (kb / S) & 1, err, 2u)) break;
+                if (!mbar_wait_cluster(afull0 + 8 * a, (kb / kAStages) & 1, err, 4u)) break;
+                tc_fence_after();
+                #pragma unroll
+                for (int j = 0; j < kBK / 16; ++j) {
+                    const uint64_t bdesc = smem_desc_sw128_kmajor(smem_addr(xs + s * kXBytes + (j / 4) * kRowsX * 128));
+                    mma_f16_ts_pair(tmem, a_tmem0 + a * kACols + j * 8, bdesc + static_cast<uint64_t>((j % 4) * 2),
+                                    idesc, (kb | j) != 0 ? 1u : 0u);
+                }
+                mma_commit_pair(empty0 + 8 * s, 0x3);
+                mma_commit_pair(aempty0 + 8 * a, 0x3);
+            }
+            mma_commit_pair(acc_full, 0x3);
+            mma_commit_pair(drain, 0x3);
+        }
+    } else if (warp < kWarpEpi0) {
+        // Converters: thread owns weight row r of this CTA's 128 = tensor-memory lane r.
+        const int quarter = warp & 3;
+        const int group = (warp - kWarpConv0) >> 2;
+        const int r = quarter * 32 + lane;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        const uint32_t afull_leader0 = mapa_shared(afull0, 0);
+        for (int kb = group; kb < num_kb; kb += kConvGroups) {
+            const int s = kb % S;
+            const int a = kb % kAStages;
+            bool ok = mbar_wait(wfull0 + 8 * s, (kb / S) & 1, err, 8u);
+            if (ok && kb >= kAStages) ok = mbar_wait_cluster(aempty0 + 8 * a, ((kb / kAStages) - 1) & 1, err, 16u);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            const uint8_t* row = ws + s * kWBytes + r * kBK;
+            #pragma unroll
+            for (int g = 0; g < kBK / 64; ++g) {
+                // 64 codes -> 32 f16x2 columns; 128B swizzle: chunk ^= r & 7.
+                uint32_t w[16];
+                #pragma unroll
+                for (int c4 = 0; c4 < 4; ++c4) {
+                    const int c = g * 4 + c4;
+                    const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) << 4));
+                    w[4 * c4 + 0] = v.x;
+                    w[4 * c4 + 1] = v.y;
+                    w[4 * c4 + 2] = v.z;
+                    w[4 * c4 + 3] = v.w;
+                }
+                uint32_t h[32];
+                #pragma unroll
+                for (int i = 0; i < 16; ++i) widen4_f16(w[i], h[2 * i], h[2 * i + 1]);
+                tmem_st_32x32b_x32(tmem + lane_addr + 2 * kRowsX + a * kACols + g * 32, h);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(afull_leader0 + 8 * a);
+        }
+    } else {
+        // Epilogue: lane = weight row n of this CTA, 256 accumulator columns =
+        // activation rows mp .. mp + 255 of the pair.
+        const int quarter = warp & 3;
+        const int n = n0 + quarter * 32 + lane;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        const bool ok = mbar_wait_cluster(acc_full, 0, err, 32u);
+        if (__all_sync(0xffffffffu, ok)) {
+            tc_fence_after();
+            const float sc = (n < N) ? __ldg(scale + n) : 0.0f;
+            #pragma unroll 1
+            for (int c0 = 0; c0 < 2 * kRowsX; c0 += 32) {
+                if (mp + c0 >= M) break;
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem + lane_addr + c0, v);
+                tmem_wait_ld();
+                if (n < N) {
+                    #pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int m = mp + c0 + j;
+                        if (m < M) {
+                            out[static_cast<int64_t>(m) * N + n] = (__uint_as_float(v[j]) * __ldg(rowscale + m)) * sc;
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    // Every MMA of the pair must be finished before either CTA releases its
+    // tensor memory or shared memory: wait for the drain commit, then meet.
+    if (warp == kWarpMma && lane == 0) mbar_wait_cluster(drain, 0, err, 128u);
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp == kWarpMma) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, kTmemCols);
+    }
+}
+
 // ------------------------------------------------------------------ host side
 constexpr int kMaxDevices = 64;
 
@@ -386,7 +705,7 @@ cudaError_t scratch_pool(cudaMemPool_t* out) {
     return cudaSuccess;
 }
 
-bool g_attr_set[kMaxDevices][4] = {};
+bool g_attr_set[kMaxDevices][5] = {};
 
 template <int BM>
 popcornStatus_t launch_gemm(int slot, const CUtensorMap& tx, const CUtensorMap& tw, float* out, const float* scale,
@@ -412,12 +731,12 @@ int pick_bm(int64_t M) {
     return 256;
 }
 
-// Tensor maps of one call: x16 [M, K] f16 in [bm x 64] boxes (128B swizzle),
-// qweight [N, K] int8 in [128 x bk] boxes (bk = 64: 64B swizzle, bk = 128:
-// 128B swizzle), matching Cfg<bm>.
+// Tensor maps of one call: x16 [M, K] f16 in [xrows x 64] boxes (128B
+// swizzle), qweight [N, K] int8 in [128 x bk] boxes (bk = 64: 64B swizzle,
+// bk = 128: 128B swizzle).
 bool make_maps(PFN_cuTensorMapEncodeTiled_v12000 encode, __half* x16, const int8_t* q, int64_t M, int64_t N,
-               int64_t K, int bm, CUtensorMap* tx, CUtensorMap* tw) {
-    const int bk = bm >= 256 ? 64 : 128;
+               int64_t K, int xrows, int bk, CUtensorMap* tx, CUtensorMap* tw) {
+    const int bm = xrows;
     const cuuint64_t xdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
     const cuuint64_t xstride[1] = {static_cast<cuuint64_t>(K) * 2};
     const cuuint32_t xbox[2] = {64, static_cast<cuuint32_t>(bm)};
@@ -433,6 +752,44 @@ bool make_maps(PFN_cuTensorMapEncodeTiled_v12000 encode, __half* x16, const int8
                          bk == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r1 == CUDA_SUCCESS && r2 == CUDA_SUCCESS;
+}
+
+popcornStatus_t launch_pair(const CUtensorMap& tx, const CUtensorMap& tw, float* out, const float* scale,
+                            const float* rowscale, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < kMaxDevices && !g_attr_set[dev][4]) {
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             pair::kSmem);
+        if (e != cudaSuccess) return record_cuda(e);
+        g_attr_set[dev][4] = true;
+    }
+    dim3 grid(static_cast<unsigned>(2 * ceil_div(N, 2 * kTileN)), static_cast<unsigned>(ceil_div(M, 2 * pair::kRowsX)));
+    tc_gemm_pair_kernel<<<grid, kThreads, pair::kSmem, stream>>>(tx, tw, out, scale, rowscale, static_cast<int>(M),
+                                                                 static_cast<int>(N), static_cast<int>(K));
+    return check_launch();
+}
+
+// The GEMM launch of the tensor path once x16 and rowscale are in place:
+// CTA pairs (256 x 256 tiles) for M > 128, single CTAs with BM activation
+// rows otherwise.
+popcornStatus_t launch_tc_gemm(PFN_cuTensorMapEncodeTiled_v12000 encode, __half* x16, const float* rowscale,
+                               float* out, const int8_t* q, const float* scale, int64_t M, int64_t N, int64_t K,
+                               cudaStream_t stream) {
+    const int bm = pick_bm(M);
+    CUtensorMap tx, tw;
+    if (bm >= 256) {
+        if (!make_maps(encode, x16, q, M, N, K, pair::kRowsX, pair::kBK, &tx, &tw)) return POPCORN_ERROR_INVALID_VALUE;
+        static_assert(pair::kBK == 128, "make_maps: 128-deep weight boxes use the 128B swizzle");
+        return launch_pair(tx, tw, out, scale, rowscale, M, N, K, stream);
+    }
+    const int bk = (bm >= 256) ? 64 : 128;
+    if (!make_maps(encode, x16, q, M, N, K, bm, bk, &tx, &tw)) return POPCORN_ERROR_INVALID_VALUE;
+    switch (bm) {
+        case 32: return launch_gemm<32>(0, tx, tw, out, scale, rowscale, M, N, K, stream);
+        case 64: return launch_gemm<64>(1, tx, tw, out, scale, rowscale, M, N, K, stream);
+        default: return launch_gemm<128>(2, tx, tw, out, scale, rowscale, M, N, K, stream);
+    }
 }
 
 }  // namespace
@@ -462,24 +819,9 @@ popcornStatus_t tc_dequant_matmul(float* out, const float* x, const int8_t* q, c
     __half* x16 = static_cast<__half*>(scratch);
     float* rowscale = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + x16_bytes);
 
-    const int vec = aligned16(x) ? 1 : 0;
-    int64_t blocks = ceil_div(M, 8);
-    const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
-    if (blocks > cap) blocks = cap;
-    x_to_f16_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x16, rowscale, x, M, K, vec);
-    popcornStatus_t st = check_launch();
+    popcornStatus_t st = launch_x_to_f16(x16, rowscale, x, M, K, stream);
 
-    const int bm = pick_bm(M);
-    CUtensorMap tx, tw;
-    if (st == POPCORN_SUCCESS && !make_maps(encode, x16, q, M, N, K, bm, &tx, &tw)) st = POPCORN_ERROR_INVALID_VALUE;
-    if (st == POPCORN_SUCCESS) {
-        switch (bm) {
-            case 32: st = launch_gemm<32>(0, tx, tw, out, scale, rowscale, M, N, K, stream); break;
-            case 64: st = launch_gemm<64>(1, tx, tw, out, scale, rowscale, M, N, K, stream); break;
-            case 128: st = launch_gemm<128>(2, tx, tw, out, scale, rowscale, M, N, K, stream); break;
-            default: st = launch_gemm<256>(3, tx, tw, out, scale, rowscale, M, N, K, stream); break;
-        }
-    }
+    if (st == POPCORN_SUCCESS) st = launch_tc_gemm(encode, x16, rowscale, out, q, scale, M, N, K, stream);
     e = cudaFreeAsync(scratch, stream);
     if (st == POPCORN_SUCCESS && e != cudaSuccess) st = record_cuda(e);
     return st;
@@ -562,23 +904,10 @@ extern "C" popcornStatus_t popcornDequantizeMatmulNoAlloc_i8f32(float* out, cons
     // The prologue writes every x16 element and row scale the GEMM reads (tile
     // edges past M or K are zero-filled by TMA, not read from the array), so
     // nothing left in the array by an earlier call needs clearing.
-    const int vec = aligned16(x) ? 1 : 0;
-    int64_t blocks = ceil_div(M, 8);
-    const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
-    if (blocks > cap) blocks = cap;
-    x_to_f16_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x16, rowscale, x, M, K, vec);
-    popcornStatus_t st = check_launch();
+    popcornStatus_t st = launch_x_to_f16(x16, rowscale, x, M, K, stream);
     if (st != POPCORN_SUCCESS) return st;
 
-    const int bm = pick_bm(M);
-    CUtensorMap tx, tw;
-    if (!make_maps(encode, x16, qweight, M, N, K, bm, &tx, &tw)) return POPCORN_ERROR_INVALID_VALUE;
-    switch (bm) {
-        case 32: return launch_gemm<32>(0, tx, tw, out, scale, rowscale, M, N, K, stream);
-        case 64: return launch_gemm<64>(1, tx, tw, out, scale, rowscale, M, N, K, stream);
-        case 128: return launch_gemm<128>(2, tx, tw, out, scale, rowscale, M, N, K, stream);
-        default: return launch_gemm<256>(3, tx, tw, out, scale, rowscale, M, N, K, stream);
-    }
+    return launch_tc_gemm(encode, x16, rowscale, out, qweight, scale, M, N, K, stream);
 }
 
 namespace pcb {
