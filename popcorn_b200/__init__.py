@@ -49,7 +49,23 @@ EXT_SYMBOLS = (
     "popcornDequantizeMatmulLaunchCount",
     "popcornB200DeviceErrors",
     "popcornDequantizeMatmulNoAlloc_i8f32",
+    "popcornDequantizeMatmulAllGather_i8f32",
+    "popcornDequantizeMatmulAllReduce_i8f32",
 )
+
+TP_MAX_RANKS = 8
+
+
+class TpGroup(ctypes.Structure):
+    """popcornTpGroup_t (include/popcorn_tp.h)."""
+
+    _fields_ = [
+        ("recv", ctypes.c_void_p * TP_MAX_RANKS),
+        ("recv_bytes", ctypes.c_int64),
+        ("state", ctypes.c_void_p),
+        ("rank", ctypes.c_int),
+        ("world", ctypes.c_int),
+    ]
 
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -68,6 +84,8 @@ _SIGNATURES = {
     "popcornDequantizeMatmulLaunchCount": (_int, [_vp, _vp, _i64, _i64, _i64, _int]),
     "popcornB200DeviceErrors": (_int, [ctypes.POINTER(ctypes.c_uint)]),
     "popcornDequantizeMatmulNoAlloc_i8f32": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "popcornDequantizeMatmulAllGather_i8f32": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp]),
+    "popcornDequantizeMatmulAllReduce_i8f32": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
 }
 
 _lib = None

@@ -17,6 +17,23 @@ namespace pcb {
 // Number of streaming multiprocessors on a B200.
 constexpr int kB200Sms = 148;
 
+// Ranks of one tensor-parallel group (GPUs of one node).
+constexpr int kPeerMaxRanks = 8;
+
+// Collective fused into the decode GEMV.
+enum PeerMode : int { kPeerNone = 0, kPeerGather = 1, kPeerReduce = 2 };
+
+// Arguments of the fused decode GEMV + collective (passed by value to the kernel).
+struct PeerArgs {
+    unsigned long long* recv[kPeerMaxRanks];  // every rank's receive area, mapped on this GPU
+    int64_t half_words;                       // 8-byte words in each half of a receive area
+    unsigned int* state;                      // this rank's {call count, finished-block counter}
+    int64_t n_offset;                         // all-gather: first output channel of this rank's shard
+    int64_t n_total;                          // all-gather: output channels of the gathered result
+    int rank;
+    int world;
+};
+
 // Records `err` for popcornGetLastCudaError() and maps it to a status.
 popcornStatus_t record_cuda(cudaError_t err);
 
@@ -50,6 +67,12 @@ popcornStatus_t tc_dequant_matmul(float* out, const float* x, const int8_t* q,
                                   const float* scale, int64_t M, int64_t N,
                                   int64_t K, cudaStream_t stream);
 int tc_launch_count(int64_t M, int64_t N, int64_t K);
+
+// Fused decode GEMV + all-gather / all-reduce (gemv.cu). `rows` is the
+// number of weight rows of this rank's call (n_local, or N for a reduce).
+bool peer_supported(const float* x, const int8_t* q, int64_t M, int64_t K);
+popcornStatus_t peer_dequant_matmul(PeerMode mode, const PeerArgs& pa, float* out, const float* x, const int8_t* q,
+                                    const float* scale, int64_t M, int64_t rows, int64_t K, cudaStream_t stream);
 
 // Read and clear the device error words of the bounded-wait kernels.
 cudaError_t tc_take_errors(unsigned int* bits);

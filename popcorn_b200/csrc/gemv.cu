@@ -71,8 +71,111 @@ seq_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* _
 }
 
 constexpr int kMaxDevices = 64;
+constexpr int kXsSlots = 8;  // decode kernel variants (launch_xs slot numbers)
 
 // ------------------------------------------------------------ gemv_xs_kernel
+// Fused collectives (tensor-parallel decode). A call with sequence number e
+// (this rank's call count + 1, the same on every rank) sends each output
+// value as one 8-byte word {e, f32 bits} into half (e & 1) of the receiving
+// rank's area: an aligned 64-bit store is single-copy atomic, so a reader
+// that sees the tag e also sees the value, and no flag or fence has to
+// follow the data. All-gather: the value of output (m, n) goes to slot
+// m * N + n of every other rank. All-reduce: rank r's partial of (m, n) goes
+// to slot r * M * N + m * N + n of every rank, its own included. After its
+// own outputs, every block polls its share of this rank's slots until they
+// carry tag e (bounded), then writes them (all-gather) or their sum in rank
+// order (all-reduce) to `out`. A rank is at most one call ahead of another
+// (a call ends only when all of its inputs from every rank have arrived), so
+// alternating halves keep a faster rank from overwriting slots that a slower
+// one has not read yet.
+constexpr uint64_t kPeerWaitNs = 1000ull * 1000ull * 1000ull;  // 1 s
+constexpr unsigned int kPeerTimeoutBit = 0x100u;
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned int atom_add_acq_rel_gpu(unsigned int* p, unsigned int v) {
+    unsigned int old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ unsigned long long tagged(unsigned int e, float v) {
+    return (static_cast<unsigned long long>(e) << 32) | __float_as_uint(v);
+}
+
+// Waits (until deadline) for slot p to carry tag e; returns false on timeout.
+__device__ __forceinline__ bool wait_tag(const unsigned long long* p, unsigned int e, uint64_t deadline, float& v) {
+    for (;;) {
+        const unsigned long long w = ld_relaxed_sys_u64(p);
+        if (static_cast<unsigned int>(w >> 32) == e) {
+            v = __uint_as_float(static_cast<unsigned int>(w));
+            return true;
+        }
+        if (global_ns() > deadline) {
+            atomicOr(&g_gemv_error, kPeerTimeoutBit);
+            return false;
+        }
+    }
+}
+
+// Second half of a fused call, run by every block after its own outputs:
+// collect this block's share of the values other ranks send, then count the
+// block done; the last block advances the call count for the next call.
+template <int MODE>
+__device__ void peer_finish(const PeerArgs& pa, float* __restrict__ out, int64_t M, int64_t rows, unsigned int e) {
+    const int64_t blocks = static_cast<int64_t>(gridDim.x) * gridDim.y;
+    const int64_t b = static_cast<int64_t>(blockIdx.y) * gridDim.x + blockIdx.x;
+    const unsigned long long* mine = pa.recv[pa.rank] + (e & 1u) * pa.half_words;
+    const int64_t others = pa.n_total - rows;  // all-gather: columns owned by other ranks
+    const int64_t total = (MODE == kPeerGather) ? M * others : M * rows;
+    const int64_t j0 = total * b / blocks;
+    const int64_t j1 = total * (b + 1) / blocks;
+    const uint64_t deadline = global_ns() + kPeerWaitNs;
+    for (int64_t j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
+        if constexpr (MODE == kPeerGather) {
+            const int64_t m = j / others;
+            const int64_t c = j - m * others;
+            const int64_t idx = m * pa.n_total + (c < pa.n_offset ? c : c + rows);
+            float v;
+            if (!wait_tag(mine + idx, e, deadline, v)) break;
+            out[idx] = v;
+        } else {
+            float sum = 0.0f;
+            bool ok = true;
+            for (int p = 0; p < pa.world; ++p) {
+                float v;
+                if (!wait_tag(mine + static_cast<int64_t>(p) * total + j, e, deadline, v)) {
+                    ok = false;
+                    break;
+                }
+                sum = (p == 0) ? v : sum + v;
+            }
+            if (!ok) break;
+            out[j] = sum;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && atom_add_acq_rel_gpu(pa.state + 1, 1u) == static_cast<unsigned int>(blocks - 1)) {
+        volatile unsigned int* st = pa.state;
+        st[1] = 0u;  // ready for the next call
+        st[0] = e;
+    }
+}
+
 constexpr int kXsThreads = 256;
 constexpr int kXsWarps = kXsThreads / 32;
 
@@ -107,10 +210,10 @@ __device__ __forceinline__ float warp_reduce_scatter(float (&v)[V], int lane) {
 // PIPE: blocks own several row groups and overlap the next group's loads with
 // the current group's math (more registers, two blocks per SM); without it a
 // block owns one row group and four blocks fit per SM.
-template <int MT, int U, int R, bool PIPE>
+template <int MT, int U, int R, bool PIPE, int MODE = kPeerNone>
 __global__ void __launch_bounds__(kXsThreads, (MT * U <= 1 && !PIPE) ? 4 : 2)
 gemv_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* __restrict__ q,
-               const float* __restrict__ scale, int64_t M, int64_t N, int64_t K, int rpc) {
+               const float* __restrict__ scale, int64_t M, int64_t N, int64_t K, int rpc, const PeerArgs pa) {
     extern __shared__ float part[];  // [rpc][MT][kXsWarps]
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -118,7 +221,6 @@ gemv_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_
     const int64_t units = K >> 4;
     const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rpc;
     const int64_t r1 = (r0 + rpc < N) ? r0 + rpc : N;
-
     // Programmatic dependent launch: let the next kernel in the stream start
     // as soon as SM resources free up, and, before waiting for the previous
     // kernel, pull this block's weight rows into L2. A prefetch is only a
@@ -139,6 +241,16 @@ gemv_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_
         }
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    // Fused collective: this call's sequence number (the count is advanced
+    // by the previous call's last block, so it is stable for this whole grid).
+    unsigned int e = 0;
+    if constexpr (MODE != kPeerNone) {
+        __shared__ unsigned int s_e;
+        if (tid == 0) s_e = *reinterpret_cast<volatile unsigned int*>(pa.state) + 1u;
+        __syncthreads();
+        e = s_e;
+    }
 
     for (int64_t m0 = static_cast<int64_t>(blockIdx.y) * MT; m0 < M; m0 += static_cast<int64_t>(gridDim.y) * MT) {
         // Activations of this thread's K slices, kept in registers.
@@ -234,10 +346,26 @@ gemv_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_
             float s = 0.0f;
             #pragma unroll
             for (int wv = 0; wv < kXsWarps; ++wv) s += part[i * kXsWarps + wv];
-            if (m0 + m < M) out[(m0 + m) * N + r0 + r] = s * __ldg(scale + r0 + r);
+            if (m0 + m < M) {
+                const float val = s * __ldg(scale + r0 + r);
+                if constexpr (MODE == kPeerGather) {
+                    const int64_t idx = (m0 + m) * pa.n_total + pa.n_offset + r0 + r;
+                    out[idx] = val;
+                    const int64_t slot = (e & 1u) * pa.half_words + idx;
+                    for (int p = 0; p < pa.world; ++p) {
+                        if (p != pa.rank) st_relaxed_sys_u64(pa.recv[p] + slot, tagged(e, val));
+                    }
+                } else if constexpr (MODE == kPeerReduce) {
+                    const int64_t slot = (e & 1u) * pa.half_words + pa.rank * M * N + (m0 + m) * N + r0 + r;
+                    for (int p = 0; p < pa.world; ++p) st_relaxed_sys_u64(pa.recv[p] + slot, tagged(e, val));
+                } else {
+                    out[(m0 + m) * N + r0 + r] = val;
+                }
+            }
         }
         __syncthreads();
     }
+    if constexpr (MODE != kPeerNone) peer_finish<MODE>(pa, out, M, N, e);
 }
 
 
@@ -430,7 +558,8 @@ int xs_rows_per_block(Kern kernel, int slot, int64_t N) {
 
 template <int MT, int U, int R>
 popcornStatus_t launch_xs(int slot, float* out, const float* x, const int8_t* q, const float* scale, int64_t M,
-                          int64_t N, int64_t K, cudaStream_t stream) {
+                          int64_t N, int64_t K, cudaStream_t stream, PeerMode mode = kPeerNone,
+                          const PeerArgs* peer = nullptr) {
     // One row group of R rows per block while a single wave of resident
     // blocks holds the grid (every thread has all its loads in flight at
     // once); otherwise fewer, pipelined blocks that stream several groups.
@@ -452,8 +581,38 @@ popcornStatus_t launch_xs(int slot, float* out, const float* x, const int8_t* q,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = pipe ? cudaLaunchKernelEx(&cfg, gemv_xs_kernel<MT, U, R, true>, out, x, q, scale, M, N, K, rpc)
-                         : cudaLaunchKernelEx(&cfg, gemv_xs_kernel<MT, U, R, false>, out, x, q, scale, M, N, K, rpc);
+    cudaError_t e;
+    if (mode != kPeerNone) {
+        // Fused collective: plain stream order (the block counter and call
+        // count must not be shared with an overlapping launch), and every
+        // block resident at once, since blocks wait for other ranks' data.
+        using Kernel = void (*)(float*, const float*, const int8_t*, const float*, int64_t, int64_t, int64_t, int,
+                                const PeerArgs);
+        Kernel kern;
+        if (mode == kPeerGather) {
+            kern = pipe ? gemv_xs_kernel<MT, U, R, true, kPeerGather> : gemv_xs_kernel<MT, U, R, false, kPeerGather>;
+        } else {
+            kern = pipe ? gemv_xs_kernel<MT, U, R, true, kPeerReduce> : gemv_xs_kernel<MT, U, R, false, kPeerReduce>;
+        }
+        static int resident_cache[kMaxDevices][kXsSlots * 4] = {};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const int key = slot * 4 + (mode == kPeerGather ? 0 : 2) + (pipe ? 1 : 0);
+        int occ = (dev >= 0 && dev < kMaxDevices) ? resident_cache[dev][key] : 0;
+        if (occ == 0) {
+            // Partial sums take at most 256 rows x 4 x 8 floats of shared memory.
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kXsThreads, 32 * 1024);
+            if (e != cudaSuccess) return record_cuda(e);
+            if (dev >= 0 && dev < kMaxDevices) resident_cache[dev][key] = occ;
+        }
+        if (gx * gy > static_cast<int64_t>(occ) * device_sm_count()) return POPCORN_ERROR_INVALID_VALUE;
+        cfg.numAttrs = 0;
+        e = cudaLaunchKernelEx(&cfg, kern, out, x, q, scale, M, N, K, rpc, *peer);
+    } else {
+        const PeerArgs none = {};
+        e = pipe ? cudaLaunchKernelEx(&cfg, gemv_xs_kernel<MT, U, R, true>, out, x, q, scale, M, N, K, rpc, none)
+                 : cudaLaunchKernelEx(&cfg, gemv_xs_kernel<MT, U, R, false>, out, x, q, scale, M, N, K, rpc, none);
+    }
     if (e != cudaSuccess) return record_cuda(e);
     return check_launch();
 }
@@ -466,6 +625,25 @@ cudaError_t gemv_take_errors(unsigned int* bits) {
     cudaError_t e = cudaMemcpyFromSymbol(bits, g_gemv_error, sizeof(unsigned int));
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_gemv_error, &zero, sizeof(unsigned int));
     return e;
+}
+
+bool peer_supported(const float* x, const int8_t* q, int64_t M, int64_t K) {
+    return M >= 1 && M <= 4 && vector_ok(x, q, K) && ceil_div(K / 16, kXsThreads) <= (M == 1 ? 4 : (M == 2 ? 2 : 1));
+}
+
+popcornStatus_t peer_dequant_matmul(PeerMode mode, const PeerArgs& pa, float* out, const float* x, const int8_t* q,
+                                    const float* scale, int64_t M, int64_t rows, int64_t K, cudaStream_t stream) {
+    const int64_t slices = ceil_div(K / 16, kXsThreads);
+    if (M == 1) {
+        if (slices == 1) return launch_xs<1, 1, 8>(0, out, x, q, scale, M, rows, K, stream, mode, &pa);
+        if (slices == 2) return launch_xs<1, 2, 4>(1, out, x, q, scale, M, rows, K, stream, mode, &pa);
+        return launch_xs<1, 4, 2>(2, out, x, q, scale, M, rows, K, stream, mode, &pa);
+    }
+    if (M == 2) {
+        if (slices == 1) return launch_xs<2, 1, 8>(3, out, x, q, scale, M, rows, K, stream, mode, &pa);
+        return launch_xs<2, 2, 4>(4, out, x, q, scale, M, rows, K, stream, mode, &pa);
+    }
+    return launch_xs<4, 1, 4>(5, out, x, q, scale, M, rows, K, stream, mode, &pa);
 }
 
 int simt_launch_count(const float*, const int8_t*, int64_t M, int64_t N, int64_t K) {

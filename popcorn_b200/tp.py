@@ -23,12 +23,13 @@ is the library's C ABI on the current CUDA stream.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable, Optional
 
 import torch
 import torch.distributed as dist
 
-from . import dequantize_matmul
+from . import TP_MAX_RANKS, TpGroup, dequantize_matmul, load_library, PopcornError, POPCORN_SUCCESS
 
 LocalMatmul = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
 
@@ -104,3 +105,110 @@ class RowParallelLinear:
         if self.world > 1:
             dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
         return y
+
+
+class PeerGroup:
+    """Receive areas and call state of the fused decode collectives.
+
+    Allocates, on every rank of ``group``, a zero-filled receive area in torch
+    symmetric memory (peer-mapped over NVLink) large enough for an all-reduce
+    of [max_m, max_n] outputs (which also covers an all-gather of that size),
+    plus the rank's two-word call state, and fills the popcornTpGroup_t the C
+    entry points take. One group serves any number of layers; every rank must
+    make the same calls in the same order, each rank on one stream.
+    """
+
+    def __init__(self, max_m: int, max_n: int, device: torch.device, group: Optional[dist.ProcessGroup] = None):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.group = group or dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        if self.world > TP_MAX_RANKS:
+            raise ValueError(f"at most {TP_MAX_RANKS} ranks")
+        self.max_m, self.max_n = max_m, max_n
+        recv_bytes = 16 * self.world * max_m * max_n
+        self.recv = symm_mem.empty((recv_bytes // 8,), dtype=torch.int64, device=device)
+        self.recv.zero_()
+        self.state = torch.zeros((2,), dtype=torch.int32, device=device)
+        torch.cuda.synchronize(device)
+        handle = symm_mem.rendezvous(self.recv, self.group.group_name)
+        g = TpGroup()
+        for p in range(self.world):
+            g.recv[p] = handle.buffer_ptrs[p]
+        g.recv_bytes = recv_bytes
+        g.state = self.state.data_ptr()
+        g.rank, g.world = self.rank, self.world
+        self.tp_group = g
+        self._handle = handle
+        dist.barrier(group=self.group)  # every rank's receive area is zero before any call
+
+    def all_gather(self, out: torch.Tensor, x: torch.Tensor, q: torch.Tensor, s: torch.Tensor, n_offset: int,
+                   stream_handle: int) -> int:
+        """out [M, N] <- all ranks' shards; q [n_local, K] is this rank's. Returns popcornStatus_t."""
+        M, N = out.shape
+        return load_library().popcornDequantizeMatmulAllGather_i8f32(
+            ctypes.byref(self.tp_group), out.data_ptr(), x.data_ptr(), q.data_ptr(), s.data_ptr(), M, n_offset,
+            q.shape[0], N, q.shape[1], stream_handle)
+
+    def all_reduce(self, out: torch.Tensor, x: torch.Tensor, q: torch.Tensor, s: torch.Tensor,
+                   stream_handle: int) -> int:
+        """out [M, N] <- sum over ranks of x_r @ (q_r * s).T; x [M, K_r], q [N, K_r]. Returns popcornStatus_t."""
+        M, N = out.shape
+        return load_library().popcornDequantizeMatmulAllReduce_i8f32(
+            ctypes.byref(self.tp_group), out.data_ptr(), x.data_ptr(), q.data_ptr(), s.data_ptr(), M, N,
+            q.shape[1], stream_handle)
+
+
+class FusedColumnParallelLinear:
+    """Column-parallel decode layer whose all-gather is fused into the GEMV.
+
+    Each rank's kernel (popcornDequantizeMatmulAllGather_i8f32) computes its
+    output channels and sends them to every other rank over NVLink; it
+    finishes only when the other ranks' channels have arrived, so no
+    collective call follows. Decode shapes only (M <= 4). The gathered result
+    equals a single-GPU call bit for bit.
+    """
+
+    def __init__(self, qweight: torch.Tensor, scale: torch.Tensor, peer: PeerGroup):
+        self.N, self.K = qweight.shape
+        self.peer = peer
+        lo, hi = shard_bounds(self.N, peer.world, peer.rank)
+        self.lo, self.hi = lo, hi
+        self.q = qweight[lo:hi].contiguous()
+        self.s = scale[lo:hi].contiguous()
+
+    def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty((x.shape[0], self.N), dtype=torch.float32, device=x.device)
+        st = self.peer.all_gather(out, x, self.q, self.s, self.lo, torch.cuda.current_stream().cuda_stream)
+        if st != POPCORN_SUCCESS:
+            raise PopcornError(st, "popcornDequantizeMatmulAllGather_i8f32")
+        return out
+
+
+class FusedRowParallelLinear:
+    """Row-parallel decode layer whose all-reduce is fused into the GEMV.
+
+    Input channels are split across ranks as in :class:`RowParallelLinear`;
+    each rank's kernel (popcornDequantizeMatmulAllReduce_i8f32) sends its
+    partial outputs to every rank and sums all ranks' partials in rank order,
+    so every rank holds the same bits. Decode shapes only (M <= 4).
+    """
+
+    def __init__(self, qweight: torch.Tensor, scale: torch.Tensor, peer: PeerGroup):
+        self.N, self.K = qweight.shape
+        self.peer = peer
+        lo, hi = shard_bounds(self.K, peer.world, peer.rank)
+        self.lo, self.hi = lo, hi
+        self.q = qweight[:, lo:hi].contiguous()
+        self.s = scale.contiguous()
+
+    def __call__(self, x: torch.Tensor, x_is_sharded: bool = False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        xs = (x if x_is_sharded else x[:, self.lo:self.hi]).contiguous()
+        if out is None:
+            out = torch.empty((x.shape[0], self.N), dtype=torch.float32, device=x.device)
+        st = self.peer.all_reduce(out, xs, self.q, self.s, torch.cuda.current_stream().cuda_stream)
+        if st != POPCORN_SUCCESS:
+            raise PopcornError(st, "popcornDequantizeMatmulAllReduce_i8f32")
+        return out

@@ -6,6 +6,7 @@ buffer returns POPCORN_ERROR_INVALID_VALUE before sizes are looked at; any
 size <= 0 returns POPCORN_SUCCESS without work. These paths return before any
 CUDA call, so they run without a GPU.
 """
+import ctypes
 import os
 import re
 import subprocess
@@ -15,7 +16,7 @@ import pytest
 import popcorn_b200 as pc
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADERS = [os.path.join(ROOT, "include", h) for h in ("popcorn.h", "popcorn_b200.h")]
+HEADERS = [os.path.join(ROOT, "include", h) for h in ("popcorn.h", "popcorn_b200.h", "popcorn_tp.h")]
 
 
 def declared_functions():
@@ -106,6 +107,80 @@ def test_nonpositive_sizes_are_noops(lib, sizes):
         assert lib.popcornQuantize_f32i8(FAKE, FAKE, FAKE, N, K, None) == pc.POPCORN_SUCCESS
         assert lib.popcornDequantize_i8f32(FAKE, FAKE, FAKE, N, K, None) == pc.POPCORN_SUCCESS
     assert pc.launch_count(FAKE, FAKE, M, N, K) == 0
+
+
+def _group(world=2, rank=0, recv_bytes=1 << 20):
+    g = pc.TpGroup()
+    g.world, g.rank = world, rank
+    g.recv_bytes = recv_bytes
+    g.state = FAKE
+    for p in range(world):
+        g.recv[p] = FAKE
+    return g
+
+
+def test_tp_group_layout_matches_header():
+    # popcornTpGroup_t: 8 pointers, int64, pointer, int, int (include/popcorn_tp.h).
+    assert ctypes.sizeof(pc.TpGroup) == 8 * 8 + 8 + 8 + 4 + 4
+    assert pc.TpGroup.recv_bytes.offset == 64 and pc.TpGroup.state.offset == 72
+    assert pc.TpGroup.rank.offset == 80 and pc.TpGroup.world.offset == 84
+
+
+def test_allgather_argument_checks(lib):
+    fn = lib.popcornDequantizeMatmulAllGather_i8f32
+    g = _group()
+    ok = (FAKE, FAKE, FAKE, FAKE)  # out, x, qweight, scale
+    # null group or buffer -> invalid before sizes
+    assert fn(None, *ok, 1, 0, 8, 16, 64, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    for i in range(4):
+        bufs = list(ok)
+        bufs[i] = 0
+        assert fn(ctypes.byref(g), *bufs, 0, 0, 8, 16, 64, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    # non-positive sizes -> no-op
+    assert fn(ctypes.byref(g), *ok, 0, 0, 8, 16, 64, None) == pc.POPCORN_SUCCESS
+    assert fn(ctypes.byref(g), *ok, 1, 0, 0, 16, 64, None) == pc.POPCORN_SUCCESS
+    # shard outside [0, N), M beyond the decode limit
+    assert fn(ctypes.byref(g), *ok, 1, 12, 8, 16, 64, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    assert fn(ctypes.byref(g), *ok, 1, -1, 8, 16, 64, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    assert fn(ctypes.byref(g), *ok, 5, 0, 8, 16, 64, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    # K % 16 != 0 or an unaligned x cannot take the vector kernel
+    assert fn(ctypes.byref(g), *ok, 1, 0, 8, 16, 72, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    assert fn(ctypes.byref(g), FAKE, FAKE + 4, FAKE, FAKE, 1, 0, 8, 16, 64, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    # rank / world out of range
+    for world, rank in ((2, 2), (9, 0), (0, 0), (2, -1)):
+        bad = _group(world=max(1, min(world, 8)), rank=rank)
+        bad.world = world
+        assert fn(ctypes.byref(bad), *ok, 1, 0, 8, 16, 64, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    # missing or misaligned receive area, missing state, receive area too small
+    bad = _group()
+    bad.recv[1] = 0
+    assert fn(ctypes.byref(bad), *ok, 1, 0, 8, 16, 64, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    bad = _group()
+    bad.recv[1] = FAKE + 4
+    assert fn(ctypes.byref(bad), *ok, 1, 0, 8, 16, 64, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    bad = _group()
+    bad.state = 0
+    assert fn(ctypes.byref(bad), *ok, 1, 0, 8, 16, 64, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    bad = _group(recv_bytes=16 * 16 - 1)  # all-gather of M=1, N=16 needs 16 * M * N bytes
+    assert fn(ctypes.byref(bad), *ok, 1, 0, 8, 16, 64, None) == pc.POPCORN_ERROR_INVALID_VALUE
+
+
+def test_allreduce_argument_checks(lib):
+    fn = lib.popcornDequantizeMatmulAllReduce_i8f32
+    g = _group()
+    ok = (FAKE, FAKE, FAKE, FAKE)
+    assert fn(None, *ok, 1, 16, 64, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    for i in range(4):
+        bufs = list(ok)
+        bufs[i] = 0
+        assert fn(ctypes.byref(g), *bufs, 1, 16, 64, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    for sizes in ((0, 16, 64), (1, 0, 64), (1, 16, 0), (-2, 16, 64)):
+        assert fn(ctypes.byref(g), *ok, *sizes, None) == pc.POPCORN_SUCCESS
+    assert fn(ctypes.byref(g), *ok, 5, 16, 64, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    assert fn(ctypes.byref(g), *ok, 1, 16, 40, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    # an all-reduce of M=1, N=16 over 2 ranks needs 16 * 2 * M * N bytes
+    small = _group(recv_bytes=16 * 2 * 16 - 16)
+    assert fn(ctypes.byref(small), *ok, 1, 16, 64, None) == pc.POPCORN_ERROR_INVALID_VALUE
 
 
 def test_batched_size_overflow_is_rejected(lib):
