@@ -59,6 +59,9 @@ def parse_args():
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
     p.add_argument("--extras", default="skinny,prefill",
                    help="comma-separated extra single-GPU workloads reported beside the headline (N=1 only)")
+    p.add_argument("--stack", default="1,128",
+                   help="M values of the 32-layer 7B-shaped linear stack timed at every N ('none' to skip)")
+    p.add_argument("--stack-layers", type=int, default=32)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--soak-s", type=float, default=0.6)
@@ -398,6 +401,92 @@ def cpu_baseline(torch, setup, wl):
                       f"wall-clock, {threads} threads"}
 
 
+def stack_shards(torch, pc, dims, layers, rank, world, device, seed):
+    """This rank's shards of `layers` random layers, generated in place.
+
+    Each shard is drawn directly (W ~ N(0, 0.02) f32, quantized per row of the
+    shard by popcornQuantize_f32i8); the full matrices never exist.
+    """
+    from popcorn_b200.tp import STACK_PARTS, shard_bounds, stack_part_shape
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed + 7919 * rank)
+    out = []
+    for _ in range(layers):
+        layer = {}
+        for part in STACK_PARTS:
+            N, K = stack_part_shape(dims, part)
+            if part in ("o", "down"):
+                lo, hi = shard_bounds(K, world, rank)
+                shape = (N, hi - lo)
+            else:
+                lo, hi = shard_bounds(N, world, rank)
+                shape = (hi - lo, K)
+            w = torch.randn(shape, generator=g, device=device) * 0.02
+            layer[part] = pc.quantize(w)
+            del w
+        out.append(layer)
+    return out
+
+
+def time_stack(torch, pc, M, layers, rank, world, device, peaks, dist_on):
+    """One pass of the 32-layer stack = one step; K passes from one CUDA graph."""
+    from popcorn_b200.tp import STACK_7B, LinearStack, PeerGroup
+
+    shards = stack_shards(torch, pc, STACK_7B, layers, rank, world, device, 4242)
+    peer = PeerGroup(M, STACK_7B["hidden"], device) if (world > 1 and M <= 4) else None
+    stack = LinearStack(shards, M, STACK_7B, device, peer=peer)
+    x = torch.randn((M, STACK_7B["hidden"]), device=device)
+    stream = torch.cuda.Stream()
+    passes = 8
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            stack(x)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(passes):
+            stack(x)
+    with torch.cuda.stream(stream):
+        graph.replay()
+    stream.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        graph.replay()
+        end.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(torch, start.elapsed_time(end), dist_on, device) / passes
+    errs = pc.device_errors()
+    del graph
+    wbytes = stack.weight_bytes()
+    if dist_on:
+        t = torch.tensor([wbytes], dtype=torch.int64, device=device)
+        torch.distributed.all_reduce(t)
+        wbytes = int(t.item())
+    gbs = wbytes / (ms * 1e-3) / 1e9
+    res = {"value": round(gbs, 2), "unit": "GB/s", "M": M, "layers": layers, "ms_per_pass": round(ms, 4),
+           "weight_bytes_per_pass": wbytes, "passes_timed": passes,
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": round(peaks["hbm"] * world, 1),
+                        "unit": "GB/s", "frac": round(gbs / (peaks["hbm"] * world), 4),
+                        "peak_source": peaks["source"] + (f" x{world}" if world > 1 else "")},
+           "launches_per_pass": stack.launches_per_pass(),
+           "row_parallel_sum": ("single GPU" if world == 1 else
+                                "fused into the GEMV (tagged NVLink peer stores)" if stack.peer is not None
+                                else "NCCL all-reduce"),
+           "device_error_bits": errs}
+    if M > 1:
+        res["tflops"] = round(2.0 * M * wbytes / (ms * 1e-3) / 1e12, 2)
+    del stack, shards, peer
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_ours(args):
     import torch
 
@@ -487,6 +576,15 @@ def run_ours(args):
             line["extra_workloads"] = extras
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(torch, setup, wl)
+
+    if args.stack != "none":
+        stack = {}
+        for m in [int(v) for v in args.stack.split(",") if v]:
+            stack[f"m{m}"] = time_stack(torch, pc, m, args.stack_layers, rank, world, device, peaks, dist_on)
+        line["stack_7b_linear"] = dict(
+            stack, config="32 layers x (qkv 4096->12288, o 4096->4096, gate and up 4096->11008, down 11008->4096), "
+                          "column-parallel qkv/gate/up, row-parallel o/down, one pass per step from a CUDA graph, "
+                          "max over ranks" if args.stack_layers == 32 else f"{args.stack_layers} layers")
 
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -212,3 +212,145 @@ class FusedRowParallelLinear:
         if st != POPCORN_SUCCESS:
             raise PopcornError(st, "popcornDequantizeMatmulAllReduce_i8f32")
         return out
+
+
+# ---------------------------------------------------------------------------
+# 7B-shaped linear stack (tensor-parallel, Megatron-style placement)
+# ---------------------------------------------------------------------------
+STACK_7B = {"hidden": 4096, "qkv": 12288, "ffn": 11008}
+STACK_PARTS = ("qkv", "o", "gate", "up", "down")
+
+
+def stack_part_shape(dims: dict, part: str) -> tuple[int, int]:
+    """[N, K] of the full weight of one projection of a layer."""
+    h = dims["hidden"]
+    return {"qkv": (dims["qkv"], h), "o": (h, h), "gate": (dims["ffn"], h), "up": (dims["ffn"], h),
+            "down": (h, dims["ffn"])}[part]
+
+
+def shard_stack_layer(full: dict, rank: int, world: int) -> dict:
+    """This rank's shards of one layer given its full (qweight, scale) pairs.
+
+    qkv, gate and up are column-parallel (rows of qweight split); o and down
+    are row-parallel (columns of qweight split, re-packed contiguous, the
+    whole per-channel scale kept).
+    """
+    out = {}
+    for part, (q, s) in full.items():
+        if part in ("o", "down"):
+            lo, hi = shard_bounds(q.shape[1], world, rank)
+            out[part] = (q[:, lo:hi].contiguous(), s.contiguous())
+        else:
+            lo, hi = shard_bounds(q.shape[0], world, rank)
+            out[part] = (q[lo:hi].contiguous(), s[lo:hi].contiguous())
+    return out
+
+
+def peer_fusable(M: int, K: int) -> bool:
+    """Whether the fused decode collectives take these sizes (popcorn_tp.h)."""
+    limit = {1: 16384, 2: 8192, 3: 4096, 4: 4096}.get(M, 0)
+    return K % 16 == 0 and 0 < K <= limit
+
+
+class LinearStack:
+    """The linear layers of a decoder stack, tensor-parallel over `group`.
+
+    Per layer: h -> qkv (column-parallel) -> o (row-parallel, all-reduce) ->
+    gate and up (column-parallel) -> down (row-parallel, all-reduce) -> h.
+    Attention and the SiLU(gate) * up product lie outside the dequant-matmul
+    path; in their place the o projection reads the first columns of the
+    rank's qkv output and the down projection reads the rank's gate output,
+    so every weight byte of every layer is streamed once per pass and every
+    collective of a Megatron-style stack happens, with nothing else between
+    the calls. Column-parallel outputs stay sharded (no all-gather).
+
+    Row-parallel sums use the fused popcornDequantizeMatmulAllReduce_i8f32
+    when a PeerGroup is given and M <= 4, else the library call followed by an
+    NCCL all-reduce. All buffers are allocated here, so a pass can be captured
+    in a CUDA graph. ``local_matmul`` (x, q, s) -> y replaces the library call
+    (for host-side tests on CPU ranks, with torch.distributed all-reduce).
+    """
+
+    def __init__(self, layers: list, M: int, dims: dict, device, group: Optional[dist.ProcessGroup] = None,
+                 peer: Optional[PeerGroup] = None, local_matmul: Optional[LocalMatmul] = None):
+        self.layers = layers
+        self.M = M
+        self.dims = dims
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.local_matmul = local_matmul
+        h = dims["hidden"]
+        ko = shard_bounds(h, self.world, self.rank)
+        self.k_o = ko[1] - ko[0]
+        k_down = layers[0]["down"][0].shape[1]
+        fusable = self.world > 1 and peer_fusable(M, self.k_o) and peer_fusable(M, k_down)
+        self.peer = peer if (peer is not None and fusable) else None
+        n_qkv = layers[0]["qkv"][0].shape[0]
+        n_ffn = layers[0]["gate"][0].shape[0]
+        if n_qkv < self.k_o:
+            raise ValueError("qkv shard narrower than the o projection's input slice")
+        f32 = torch.float32
+        self.a = torch.empty((M, n_qkv), dtype=f32, device=device)
+        self.xo = torch.empty((M, self.k_o), dtype=f32, device=device)
+        self.h1 = torch.empty((M, h), dtype=f32, device=device)
+        self.g = torch.empty((M, n_ffn), dtype=f32, device=device)
+        self.u = torch.empty((M, n_ffn), dtype=f32, device=device)
+        self.h2 = torch.empty((M, h), dtype=f32, device=device)
+        self._lib = None if local_matmul is not None else load_library()
+
+    def _mm(self, out: torch.Tensor, x: torch.Tensor, q: torch.Tensor, s: torch.Tensor) -> None:
+        if self.local_matmul is not None:
+            out.copy_(self.local_matmul(x, q, s))
+            return
+        st = self._lib.popcornDequantizeMatmul_i8f32(out.data_ptr(), x.data_ptr(), q.data_ptr(), s.data_ptr(),
+                                                     out.shape[0], q.shape[0], q.shape[1],
+                                                     torch.cuda.current_stream().cuda_stream)
+        if st != POPCORN_SUCCESS:
+            raise PopcornError(st, "popcornDequantizeMatmul_i8f32")
+
+    def _row(self, out: torch.Tensor, x: torch.Tensor, q: torch.Tensor, s: torch.Tensor) -> None:
+        if self.peer is not None:
+            st = self.peer.all_reduce(out, x, q, s, torch.cuda.current_stream().cuda_stream)
+            if st != POPCORN_SUCCESS:
+                raise PopcornError(st, "popcornDequantizeMatmulAllReduce_i8f32")
+            return
+        self._mm(out, x, q, s)
+        if self.world > 1:
+            dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.group)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """One pass over every layer; returns the last layer's output buffer."""
+        h = x
+        for i, w in enumerate(self.layers):
+            self._mm(self.a, h, *w["qkv"])
+            if self.M == 1:
+                xo = self.a[:, : self.k_o]                 # contiguous for a single row
+            else:
+                self.xo.copy_(self.a[:, : self.k_o])
+                xo = self.xo
+            self._row(self.h1, xo, *w["o"])
+            self._mm(self.g, self.h1, *w["gate"])
+            self._mm(self.u, self.h1, *w["up"])
+            self._row(self.h2, self.g, *w["down"])
+            h = self.h2
+        return h
+
+    __call__ = forward
+
+    def weight_bytes(self) -> int:
+        """int8 weight bytes this rank streams per pass."""
+        return sum(q.numel() for w in self.layers for (q, _) in w.values())
+
+    def launches_per_pass(self) -> int:
+        """Library kernel launches per pass (NCCL and copies not counted)."""
+        if self._lib is None:
+            return 0
+        n = 0
+        M = self.M
+        for w in self.layers:
+            for part in STACK_PARTS:
+                q = w[part][0]
+                n += self._lib.popcornDequantizeMatmulLaunchCount(0x10000, q.data_ptr(), M, q.shape[0],
+                                                                  q.shape[1], 0)
+        return n

@@ -15,7 +15,8 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle
-from popcorn_b200.tp import ColumnParallelLinear, RowParallelLinear, shard_bounds
+from popcorn_b200.tp import (STACK_PARTS, ColumnParallelLinear, LinearStack, RowParallelLinear, shard_bounds,
+                             shard_stack_layer, stack_part_shape)
 
 
 def oracle_matmul(x, q, s):
@@ -89,3 +90,80 @@ def test_column_and_row_parallel_gloo_world2(case):
         # Row-parallel: two partial k-sums added; f32 rounding only.
         assert oracle.normwise_rel_err(y_row, ref) <= 1e-5
     np.testing.assert_array_equal(ret[0][1], ret[1][1])  # all ranks agree
+
+
+SMALL_STACK = {"hidden": 64, "qkv": 192, "ffn": 176}
+
+
+def small_stack_weights(layers):
+    full = []
+    for i in range(layers):
+        layer = {}
+        for j, part in enumerate(STACK_PARTS):
+            N, K = stack_part_shape(SMALL_STACK, part)
+            w = oracle.fill_normal(N * K, 100 + 10 * i + j, 0.02).reshape(N, K)
+            q, s = oracle.quantize(w)
+            layer[part] = (torch.from_numpy(q), torch.from_numpy(s))
+        full.append(layer)
+    return full
+
+
+def stack_reference(full, x, world):
+    """The stack computed whole on one device, with the o projection reading
+    the same qkv columns that the ranks' shards feed it."""
+    h = x
+    hid = SMALL_STACK["hidden"]
+    for layer in full:
+        a = oracle.dequant_matmul(h, layer["qkv"][0].numpy(), layer["qkv"][1].numpy())
+        cols = []
+        for r in range(world):
+            lo, _ = shard_bounds(SMALL_STACK["qkv"], world, r)
+            klo, khi = shard_bounds(hid, world, r)
+            cols.append(a[:, lo:lo + (khi - klo)])
+        xo = np.ascontiguousarray(np.concatenate(cols, axis=1))
+        h1 = oracle.dequant_matmul(xo, layer["o"][0].numpy(), layer["o"][1].numpy())
+        g = oracle.dequant_matmul(h1, layer["gate"][0].numpy(), layer["gate"][1].numpy())
+        h = oracle.dequant_matmul(g, layer["down"][0].numpy(), layer["down"][1].numpy())
+    return h
+
+
+def _stack_worker(rank, world, port, M, layers, ret):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        full = small_stack_weights(layers)
+        shards = [shard_stack_layer(layer, rank, world) for layer in full]
+        stack = LinearStack(shards, M, SMALL_STACK, torch.device("cpu"), local_matmul=oracle_matmul)
+        x = torch.from_numpy(oracle.fill_normal(M * SMALL_STACK["hidden"], 7, 1.0).reshape(M, -1))
+        ret[rank] = stack(x).numpy().copy()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("M", [1, 3])
+def test_linear_stack_gloo_world2(M):
+    world, layers = 2, 2
+    ctx = mp.get_context("spawn")
+    ret = ctx.Manager().dict()
+    port = free_port()
+    procs = [ctx.Process(target=_stack_worker, args=(r, world, port, M, layers, ret)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    x = oracle.fill_normal(M * SMALL_STACK["hidden"], 7, 1.0).reshape(M, -1)
+    ref = stack_reference(small_stack_weights(layers), x, world)
+    np.testing.assert_array_equal(ret[0], ret[1])  # all ranks agree
+    assert oracle.normwise_rel_err(ret[0], ref) <= 1e-5
+
+
+def test_linear_stack_single_rank_is_the_plain_chain():
+    # world 1 (no process group): every projection is one plain call.
+    M = 2
+    full = small_stack_weights(1)
+    stack = LinearStack([shard_stack_layer(full[0], 0, 1)], M, SMALL_STACK, torch.device("cpu"),
+                        local_matmul=oracle_matmul)
+    x = oracle.fill_normal(M * SMALL_STACK["hidden"], 7, 1.0).reshape(M, -1)
+    np.testing.assert_array_equal(stack(torch.from_numpy(x)).numpy(), stack_reference(full, x, 1))
