@@ -52,33 +52,28 @@ constexpr int kWarpConv0 = 2;  // two groups of four converter warps: 2-5, 6-9
 constexpr int kConvGroups = 2;
 constexpr int kWarpEpi0 = 10;
 
-constexpr int pow2_at_least(int v) {
-    int p = 32;
-    while (p < v) p <<= 1;
-    return p;
-}
-
-// Per tile shape: K elements per stage (kBK), ring depths filling ~200 KB of
-// shared memory and the 512 tensor-memory columns left after the accumulator.
-// The weight tile of a stage is [128 rows x kBK bytes]; HBM streams such a
-// row-strided tile far better with 128-byte rows than with 64-byte rows
-// (measured with plain TMA streaming: 4.1 vs 2.7 TB/s), so every shape whose
-// activation tile leaves room uses kBK = 128.
+// Per activation-tile height BM: k-blocks of 128 (one [128 x 128] int8 weight
+// box, 128-byte swizzle, and a [BM x 128] f16 activation box per stage) in a
+// ring of kStages stages; ring slot s is also tensor-memory A buffer s, so
+// one barrier per slot says "its tiles and its A buffer are free again".
+// Tensor memory: accumulator (BM columns) + kStages A buffers of 64 columns.
 template <int BM>
 struct Cfg {
-    static constexpr int kBK = BM >= 256 ? 64 : 128;
+    static constexpr int kBK = 128;
     static constexpr int kSub = kBK / 64;           // 64-wide f16 swizzle atoms per stage
     static constexpr int kACols = kBK / 2;          // tensor-memory columns per A buffer
-    static constexpr int kStages = BM >= 256 ? 5 : (BM >= 128 ? 4 : (BM >= 64 ? 6 : 8));
-    static constexpr int kAStages = BM >= 256 ? 8 : (BM >= 128 ? 6 : 7);
+    static constexpr int kStages = BM >= 128 ? 4 : (BM >= 64 ? 6 : 7);
     static constexpr int kXBytes = BM * kBK * 2;   // f16 activation tile per stage
     static constexpr int kWBytes = kTileN * kBK;   // int8 weight tile per stage
-    static constexpr int kTmemCols = pow2_at_least(BM + kAStages * kACols);
-    static constexpr int kNumBars = 2 * kStages + 2 * kAStages + 2;
+    static constexpr int kTmemCols = 512;
+    static constexpr int kNumBars = 3 * kStages + 2;
     static constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16;
+    // Split-K reduction buffer: [128 weight rows][BM + 4] f32 in the idle ring.
+    static constexpr int kRedStride = BM + 4;
     static_assert(kXBytes % 1024 == 0, "x16 stages must stay 1024-byte aligned");
-    static_assert(kTmemCols <= 512, "tensor memory holds 512 columns");
+    static_assert(BM + kStages * kACols <= kTmemCols, "tensor memory holds 512 columns");
     static_assert(kSmem <= 227 * 1024, "shared memory per block");
+    static_assert(kTileN * kRedStride * 4 <= kStages * (kXBytes + kWBytes), "reduction buffer fits the ring");
 };
 
 __device__ __forceinline__ float absmax_step(float m, float v) {
@@ -260,44 +255,50 @@ __device__ __forceinline__ void widen4_f16(uint32_t word, uint32_t& lo, uint32_t
     hi = *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Split-K over a cluster: with `splits` = C > 1 the C CTAs of a cluster
+// (consecutive blockIdx.x) share one 128-row tile, rank r taking k-blocks
+// [num_kb * r / C, num_kb * (r + 1) / C). Each rank copies its accumulator
+// into its idle ring, and after a cluster barrier rank r adds the C partials
+// of weight rows [128 r / C, 128 (r + 1) / C) in rank order 0..C-1 through
+// distributed shared memory, so results do not depend on timing.
 template <int BM>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                float* __restrict__ out, const float* __restrict__ scale, const float* __restrict__ rowscale,
-               int M, int N, int K) {
+               int M, int N, int K, int splits) {
     using C = Cfg<BM>;
     constexpr int S = C::kStages;
-    constexpr int kAStages = C::kAStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr int kBK = C::kBK;
     uint8_t* xs = smem;                                  // S x kSub x [BM][64] f16, 128B swizzle
-    uint8_t* ws = smem + S * C::kXBytes;                 // S x [128][kBK] int8, 64B/128B swizzle
+    uint8_t* ws = smem + S * C::kXBytes;                 // S x [128][128] int8, 128B swizzle
     uint64_t* bars = reinterpret_cast<uint64_t*>(ws + S * C::kWBytes);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+    float* red = reinterpret_cast<float*>(smem);         // split-K partial, reuses the ring
 
+    // full[s]: stage s landed (TMA). afull[s]: A buffer s written (4 converter
+    // warps). release[s]: the MMAs reading stage s and A buffer s finished.
     const uint32_t full0 = smem_addr(bars);
-    const uint32_t empty0 = full0 + 8 * S;
-    const uint32_t afull0 = empty0 + 8 * S;
-    const uint32_t aempty0 = afull0 + 8 * kAStages;
-    const uint32_t acc_full = aempty0 + 8 * kAStages;
+    const uint32_t afull0 = full0 + 8 * S;
+    const uint32_t release0 = afull0 + 8 * S;
+    const uint32_t acc_full = release0 + 8 * S;
     const uint32_t drain = acc_full + 8;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * kTileN;
-    const int m0 = blockIdx.y * BM;
-    const int num_kb = (K + C::kBK - 1) / C::kBK;
+    const int rank = static_cast<int>(blockIdx.x) % splits;
+    const int n0 = (static_cast<int>(blockIdx.x) / splits) * kTileN;
+    const int num_kb = (K + kBK - 1) / kBK;
+    const int kb0 = num_kb * rank / splits;
+    const int n_kb = num_kb * (rank + 1) / splits - kb0;
     unsigned int* err = &g_tc_error;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(full0 + 8 * s, 1);
-            mbar_init(empty0 + 8 * s, 1);
-        }
-        for (int a = 0; a < kAStages; ++a) {
-            mbar_init(afull0 + 8 * a, 4);
-            mbar_init(aempty0 + 8 * a, 1);
+            mbar_init(afull0 + 8 * s, 4);
+            mbar_init(release0 + 8 * s, 1);
         }
         mbar_init(acc_full, 1);
         mbar_init(drain, 1);
@@ -316,35 +317,35 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t acc_tmem = tmem;          // columns [0, BM)
-    const uint32_t a_tmem0 = tmem + BM;      // A buffers at columns BM + kACols * a
+    const uint32_t a_tmem0 = tmem + BM;      // A buffer s at columns BM + kACols * s
 
     if (warp == kWarpTma) {
         if (lane == 0) {
-            for (int kb = 0; kb < num_kb; ++kb) {
-                const int s = kb % S;
-                if (kb >= S && !mbar_wait(empty0 + 8 * s, ((kb / S) - 1) & 1, err, 1u)) break;
+            for (int i = 0; i < n_kb; ++i) {
+                const int s = i % S;
+                if (i >= S && !mbar_wait(release0 + 8 * s, ((i / S) - 1) & 1, err, 1u)) break;
+                const int kb = kb0 + i;
                 mbar_arrive_expect_tx(full0 + 8 * s, C::kXBytes + C::kWBytes);
                 #pragma unroll
                 for (int sub = 0; sub < C::kSub; ++sub) {
-                    tma_load_2d(smem_addr(xs + s * C::kXBytes + sub * BM * 128), &tmap_x, kb * kBK + sub * 64, m0,
+                    tma_load_2d(smem_addr(xs + s * C::kXBytes + sub * BM * 128), &tmap_x, kb * kBK + sub * 64, 0,
                                 full0 + 8 * s);
                 }
                 tma_load_2d(smem_addr(ws + s * C::kWBytes), &tmap_w, kb * kBK, n0, full0 + 8 * s);
             }
             // Nothing of ours may still be landing in shared memory at exit:
             // wait (bounded) for the last fill of every stage.
-            for (int kb = (num_kb > S ? num_kb - S : 0); kb < num_kb; ++kb) {
-                mbar_wait(full0 + 8 * (kb % S), (kb / S) & 1, err, 64u);
+            for (int i = (n_kb > S ? n_kb - S : 0); i < n_kb; ++i) {
+                mbar_wait(full0 + 8 * (i % S), (i / S) & 1, err, 64u);
             }
         }
     } else if (warp == kWarpMma) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16_f32(kTileN, BM);
-            for (int kb = 0; kb < num_kb; ++kb) {
-                const int s = kb % S;
-                const int a = kb % kAStages;
-                if (!mbar_wait(full0 + 8 * s, (kb / S) & 1, err, 2u)) break;
-                if (!mbar_wait(afull0 + 8 * a, (kb / kAStages) & 1, err, 4u)) break;
+            for (int i = 0; i < n_kb; ++i) {
+                const int s = i % S;
+                if (!mbar_wait(full0 + 8 * s, (i / S) & 1, err, 2u)) break;
+                if (!mbar_wait(afull0 + 8 * s, (i / S) & 1, err, 4u)) break;
                 tc_fence_after();
                 #pragma unroll
                 for (int j = 0; j < kBK / 16; ++j) {
@@ -352,11 +353,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
                     // the (j / 4)-th 64-wide atom of the activation tile.
                     const uint64_t bdesc =
                         smem_desc_sw128_kmajor(smem_addr(xs + s * C::kXBytes + (j / 4) * BM * 128));
-                    mma_f16_ts(acc_tmem, a_tmem0 + a * C::kACols + j * 8, bdesc + static_cast<uint64_t>((j % 4) * 2),
-                               idesc, (kb | j) != 0 ? 1u : 0u);
+                    mma_f16_ts(acc_tmem, a_tmem0 + s * C::kACols + j * 8, bdesc + static_cast<uint64_t>((j % 4) * 2),
+                               idesc, (i | j) != 0 ? 1u : 0u);
                 }
-                mma_commit(empty0 + 8 * s);
-                mma_commit(aempty0 + 8 * a);
+                mma_commit(release0 + 8 * s);
             }
             mma_commit(acc_full);
             // Every MMA must be finished before tensor memory is released.
@@ -365,32 +365,29 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
         }
     } else if (warp < kWarpEpi0) {
         // Converters: thread owns weight row r of the tile = tensor-memory lane r.
-        // Two groups of four warps take alternate k-steps, so two conversions
+        // Two groups of four warps take alternate k-blocks, so two conversions
         // are always in flight.
         const int quarter = warp & 3;
         const int group = (warp - kWarpConv0) >> 2;
         const int r = quarter * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-        for (int kb = group; kb < num_kb; kb += kConvGroups) {
-            const int s = kb % S;
-            const int a = kb % kAStages;
-            bool ok = mbar_wait(full0 + 8 * s, (kb / S) & 1, err, 8u);
-            if (ok && kb >= kAStages) ok = mbar_wait(aempty0 + 8 * a, ((kb / kAStages) - 1) & 1, err, 16u);
+        for (int i = group; i < n_kb; i += kConvGroups) {
+            const int s = i % S;
+            bool ok = mbar_wait(full0 + 8 * s, (i / S) & 1, err, 8u);
+            if (ok && i >= S) ok = mbar_wait(release0 + 8 * s, ((i / S) - 1) & 1, err, 16u);
             // tcgen05.st below is warp-collective: leave together or not at all.
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
             const uint8_t* row = ws + s * C::kWBytes + r * kBK;
             #pragma unroll
             for (int g = 0; g < kBK / 64; ++g) {
-                // 64 codes (four 16-byte chunks) -> 32 f16x2 columns. The tile was
-                // written by TMA with a 64B swizzle (kBK = 64: chunk ^= (r >> 1) & 3)
-                // or a 128B swizzle (kBK = 128: chunk ^= r & 7).
+                // 64 codes (four 16-byte chunks, 128B swizzle: chunk ^= r & 7)
+                // -> 32 f16x2 columns.
                 uint32_t w[16];
                 #pragma unroll
                 for (int c4 = 0; c4 < 4; ++c4) {
                     const int c = g * 4 + c4;
-                    const int phys = (kBK == 64) ? (c ^ ((r >> 1) & 3)) : (c ^ (r & 7));
-                    const uint4 v = *reinterpret_cast<const uint4*>(row + (phys << 4));
+                    const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) << 4));
                     w[4 * c4 + 0] = v.x;
                     w[4 * c4 + 1] = v.y;
                     w[4 * c4 + 2] = v.z;
@@ -398,36 +395,46 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
                 }
                 uint32_t h[32];
                 #pragma unroll
-                for (int i = 0; i < 16; ++i) widen4_f16(w[i], h[2 * i], h[2 * i + 1]);
-                tmem_st_32x32b_x32(tmem + lane_addr + BM + a * C::kACols + g * 32, h);
+                for (int k = 0; k < 16; ++k) widen4_f16(w[k], h[2 * k], h[2 * k + 1]);
+                tmem_st_32x32b_x32(tmem + lane_addr + BM + s * C::kACols + g * 32, h);
             }
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(afull0 + 8 * a);
+            if (lane == 0) mbar_arrive(afull0 + 8 * s);
         }
     } else {
         // Epilogue: lane = weight row n, 32 accumulator columns (activation rows) per load.
         const int quarter = warp & 3;
-        const int n = n0 + quarter * 32 + lane;
+        const int row = quarter * 32 + lane;
+        const int n = n0 + row;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
         const bool ok = mbar_wait(acc_full, 0, err, 32u);
         if (__all_sync(0xffffffffu, ok)) {
             tc_fence_after();
+            // The ring's last asynchronous (TMA, MMA) accesses are complete;
+            // order them before this thread's generic stores into it.
+            if (splits > 1) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             const float sc = (n < N) ? __ldg(scale + n) : 0.0f;
             #pragma unroll 1
             for (int c0 = 0; c0 < BM; c0 += 32) {
-                if (m0 + c0 >= M) break;
+                if (c0 >= M) break;
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(acc_tmem + lane_addr + c0, v);
                 tmem_wait_ld();
-                if (n < N) {
+                if (splits > 1) {
+                    // The ring is idle: every MMA has finished reading it.
+                    float4* dst = reinterpret_cast<float4*>(red + row * C::kRedStride + c0);
+                    #pragma unroll
+                    for (int q4 = 0; q4 < 8; ++q4) {
+                        dst[q4] = make_float4(__uint_as_float(v[4 * q4]), __uint_as_float(v[4 * q4 + 1]),
+                                              __uint_as_float(v[4 * q4 + 2]), __uint_as_float(v[4 * q4 + 3]));
+                    }
+                } else if (n < N) {
                     #pragma unroll
                     for (int j = 0; j < 32; ++j) {
-                        const int m = m0 + c0 + j;
-                        if (m < M) {
-                            out[static_cast<int64_t>(m) * N + n] = (__uint_as_float(v[j]) * __ldg(rowscale + m)) * sc;
-                        }
+                        const int m = c0 + j;
+                        if (m < M) out[static_cast<int64_t>(m) * N + n] = (__uint_as_float(v[j]) * __ldg(rowscale + m)) * sc;
                     }
                 }
             }
@@ -436,6 +443,47 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
 
     tc_fence_before();
     __syncthreads();
+    if (splits > 1) {
+        // Every rank's partial is in its shared memory.
+        cluster_sync();
+        if (warp >= kWarpEpi0) {
+            const int et = threadIdx.x - kWarpEpi0 * 32;  // 0..127
+            const int rows = kTileN / splits;
+            const int mq = ((M < BM ? M : BM) + 3) / 4;  // 4-column groups the epilogue wrote
+            const uint32_t red_base = smem_addr(red);
+            for (int unit = et; unit < rows * mq; unit += 128) {
+                const int rl = rank * rows + unit % rows;  // weight row within the tile
+                const int m = 4 * (unit / rows);
+                const uint32_t off = static_cast<uint32_t>((rl * C::kRedStride + m) * 4);
+                float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                for (int p = 0; p < splits; ++p) {
+                    float4 v;
+                    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                                 : "r"(mapa_shared(red_base + off, static_cast<uint32_t>(p))));
+                    if (p == 0) {
+                        acc = v;
+                    } else {
+                        acc.x += v.x;
+                        acc.y += v.y;
+                        acc.z += v.z;
+                        acc.w += v.w;
+                    }
+                }
+                const int nn = n0 + rl;
+                if (nn < N) {
+                    const float sc = __ldg(scale + nn);
+                    const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+                    #pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        if (m + k < M) out[static_cast<int64_t>(m + k) * N + nn] = (a4[k] * __ldg(rowscale + m + k)) * sc;
+                    }
+                }
+            }
+        }
+        // No rank may leave while another still reads its shared memory.
+        cluster_sync();
+    }
     if (warp == kWarpMma) {
         __syncwarp();
         tc_fence_after();
@@ -707,6 +755,48 @@ cudaError_t scratch_pool(cudaMemPool_t* out) {
 
 bool g_attr_set[kMaxDevices][5] = {};
 
+// Cluster size for the split-K launch of a tile grid: the largest C in
+// {8, 4, 2} that keeps every CTA resident at once (tiles * C clusters' worth
+// of SMs, checked with the occupancy API) and leaves each rank >= 4 k-blocks;
+// 1 when the tiles alone already fill half the GPU.
+template <int BM>
+int pick_splits(int slot, int64_t tiles, int64_t num_kb) {
+    using C = Cfg<BM>;
+    static int cache[kMaxDevices][3][4] = {};  // [dev][slot][log2 C - 1]: 0 unknown, 1 no, 2 yes
+    const int64_t sms = device_sm_count();
+    if (tiles * 2 > sms) return 1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    for (int c = 8; c >= 2; c >>= 1) {
+        if (tiles * c > sms || num_kb < 4 * c) continue;
+        const int li = c == 8 ? 2 : (c == 4 ? 1 : 0);
+        int* known = (dev >= 0 && dev < kMaxDevices) ? &cache[dev][slot][li] : nullptr;
+        int clusters = 0;
+        if (known == nullptr || *known == 0) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(static_cast<unsigned>(c));
+            cfg.blockDim = dim3(kThreads);
+            cfg.dynamicSmemBytes = C::kSmem;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = static_cast<unsigned>(c);
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            if (cudaOccupancyMaxActiveClusters(&clusters, tc_gemm_kernel<BM>, &cfg) != cudaSuccess) {
+                cudaGetLastError();
+                clusters = 0;
+            }
+            if (known != nullptr) *known = clusters > 0 ? 2 + clusters : 1;
+        } else {
+            clusters = *known >= 2 ? *known - 2 : 0;
+        }
+        if (clusters >= tiles) return c;
+    }
+    return 1;
+}
+
 template <int BM>
 popcornStatus_t launch_gemm(int slot, const CUtensorMap& tx, const CUtensorMap& tw, float* out, const float* scale,
                             const float* rowscale, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
@@ -718,9 +808,23 @@ popcornStatus_t launch_gemm(int slot, const CUtensorMap& tx, const CUtensorMap& 
         if (e != cudaSuccess) return record_cuda(e);
         g_attr_set[dev][slot] = true;
     }
-    dim3 grid(static_cast<unsigned>(ceil_div(N, kTileN)), static_cast<unsigned>(ceil_div(M, BM)));
-    tc_gemm_kernel<BM><<<grid, kThreads, C::kSmem, stream>>>(tx, tw, out, scale, rowscale, static_cast<int>(M),
-                                                             static_cast<int>(N), static_cast<int>(K));
+    const int64_t tiles = ceil_div(N, kTileN);
+    const int splits = pick_splits<BM>(slot, tiles, ceil_div(K, C::kBK));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(tiles * splits));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = splits > 1 ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BM>, tx, tw, out, scale, rowscale,
+                                             static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), splits);
+    if (e != cudaSuccess) return record_cuda(e);
     return check_launch();
 }
 
@@ -783,8 +887,7 @@ popcornStatus_t launch_tc_gemm(PFN_cuTensorMapEncodeTiled_v12000 encode, __half*
         static_assert(pair::kBK == 128, "make_maps: 128-deep weight boxes use the 128B swizzle");
         return launch_pair(tx, tw, out, scale, rowscale, M, N, K, stream);
     }
-    const int bk = (bm >= 256) ? 64 : 128;
-    if (!make_maps(encode, x16, q, M, N, K, bm, bk, &tx, &tw)) return POPCORN_ERROR_INVALID_VALUE;
+    if (!make_maps(encode, x16, q, M, N, K, bm, 128, &tx, &tw)) return POPCORN_ERROR_INVALID_VALUE;
     switch (bm) {
         case 32: return launch_gemm<32>(0, tx, tw, out, scale, rowscale, M, N, K, stream);
         case 64: return launch_gemm<64>(1, tx, tw, out, scale, rowscale, M, N, K, stream);
