@@ -47,7 +47,11 @@ WORKLOADS = {
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of
 # the dominant kernel from one ncu capture of that workload; the command that
 # produced each figure is in the profiles/ summary named beside it.
-NCU_TRAFFIC = {}
+NCU_TRAFFIC = {
+    "decode": 16826112,    # profiles/gemv_xs_decode_m1_k4096_n4096.md
+    "skinny": 45422848,    # profiles/tc_gemm_skinny_m32_k4096_n11008.md
+    "prefill": 36620032,   # profiles/tc_gemm_pair_prefill_m2048_k4096_n4096.md
+}
 
 
 def parse_args():
