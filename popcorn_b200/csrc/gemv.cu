@@ -132,6 +132,18 @@ __device__ __forceinline__ bool wait_tag(const unsigned long long* p, unsigned i
     }
 }
 
+// dp2a with unsigned 16-bit halves in a and signed bytes in b.
+__device__ __forceinline__ int dp2a_lo_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp2a.lo.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp2a_hi_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp2a.hi.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
 // Second half of a fused call, run by every block after its own outputs:
 // collect this block's share of the values other ranks send, then count the
 // block done; the last block advances the call count for the next call.
@@ -280,6 +292,16 @@ gemv_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_
         // reduced. Without it each group is loaded at the top of its iteration.
         uint4 wn[R][U];
         auto load_group = [&](int64_t rb, uint4 (&dst)[R][U]) {
+            if (U == 1 && rb + R <= r1 && units == kXsThreads) {
+                // Whole group, every slice in range: no predicates, no zero fill.
+                const uint4* p = reinterpret_cast<const uint4*>(q + rb * K) + tid;
+                const int64_t row16 = K >> 4;
+                #pragma unroll
+                for (int r = 0; r < R; ++r)
+                    #pragma unroll
+                    for (int u = 0; u < U; ++u) dst[r][u] = __ldg(p + r * row16 + u * kXsThreads);
+                return;
+            }
             #pragma unroll
             for (int r = 0; r < R; ++r) {
                 #pragma unroll
@@ -293,19 +315,39 @@ gemv_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_
                 }
             }
         };
-        if constexpr (PIPE) load_group(r0, wn);
-        for (int64_t rb = r0; rb < r1; rb += R) {
-            uint4 w[R][U];
-            if constexpr (PIPE) {
-                #pragma unroll
-                for (int r = 0; r < R; ++r)
+        // The first row group is requested before anything else is computed
+        // (this launch is latency-bound), then the row-group loop runs with
+        // the per-group arithmetic as a parameter, so the fixed-point and the
+        // float path each keep only their own copy of x live.
+        load_group(r0, wn);
+        // Without PIPE a block owns exactly one row group (rpc == R).
+        auto run_groups = [&](auto&& dot) {
+            for (int64_t rb = r0; rb < r1; rb += R) {
+                float acc[R * MT];
+                if constexpr (PIPE) {
+                    uint4 w[R][U];
                     #pragma unroll
-                    for (int u = 0; u < U; ++u) w[r][u] = wn[r][u];
-                if (rb + R < r1) load_group(rb + R, wn);
-            } else {
-                load_group(rb, w);
+                    for (int r = 0; r < R; ++r)
+                        #pragma unroll
+                        for (int u = 0; u < U; ++u) w[r][u] = wn[r][u];
+                    if (rb + R < r1) load_group(rb + R, wn);
+                    dot(w, acc);
+                } else {
+                    if (rb != r0) load_group(rb, wn);
+                    dot(wn, acc);
+                }
+                constexpr int V = R * MT;
+                const float total = warp_reduce_scatter<V>(acc, lane);
+                constexpr int span = 32 / V;
+                if ((lane % span) == 0) {
+                    const int idx = lane / span;  // = r * MT + m
+                    const int r = idx / MT;
+                    const int m = idx % MT;
+                    if (rb + r < r1) part[((rb + r - r0) * MT + m) * kXsWarps + warp] = total;
+                }
             }
-            float acc[R * MT];
+        };
+        auto dot_float = [&](const uint4 (&w)[R][U], float (&acc)[R * MT]) {
             #pragma unroll
             for (int r = 0; r < R; ++r) {
                 float2 a[MT];
@@ -328,15 +370,74 @@ gemv_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_
                 #pragma unroll
                 for (int m = 0; m < MT; ++m) acc[r * MT + m] = a[m].x + a[m].y;
             }
-            constexpr int V = R * MT;
-            const float total = warp_reduce_scatter<V>(acc, lane);
-            constexpr int span = 32 / V;
-            if ((lane % span) == 0) {
-                const int idx = lane / span;  // = r * MT + m
-                const int r = idx / MT;
-                const int m = idx % MT;
-                if (rb + r < r1) part[((rb + r - r0) * MT + m) * kXsWarps + warp] = total;
+        };
+
+        // M = 1: each thread turns its slice of x into 30-bit fixed point
+        // X (scaled by a power of two from the slice's max |x|), written as
+        // X = hi * 2^16 + lo with hi signed and lo unsigned 16-bit, so one
+        // dp2a multiplies two codes by two halves exactly and four dp2a
+        // finish a 4-byte weight word: no widening, no float multiply-adds.
+        // The thread's int32 sums over its <= 64 columns cannot overflow
+        // (|hi| <= 2^14, lo < 2^16, |code| <= 128); they are combined in f32
+        // as hi_sum * 2^16 + lo_sum (one rounding) and scaled back by the
+        // power of two (exact) before the float reduction across threads. A
+        // warp that holds a non-finite x or a slice max outside
+        // [2^-90, 2^100] keeps the float path (same NaN/inf behaviour as
+        // popcorn's f32 kernel).
+        bool fixed = false;
+        float up = 1.0f, down = 1.0f;
+        if constexpr (MT == 1) {
+            // Max of the |x| bit patterns: NaN and inf have the largest.
+            uint32_t mb = 0;
+            #pragma unroll
+            for (int u = 0; u < U; ++u) {
+                #pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    mb = max(mb, __float_as_uint(xv[0][u][c].x) & 0x7FFFFFFFu);
+                    mb = max(mb, __float_as_uint(xv[0][u][c].y) & 0x7FFFFFFFu);
+                }
             }
+            const bool bad = mb != 0u && (mb < 0x12800000u || mb > 0x71800000u);  // outside [2^-90, 2^100]
+            fixed = !__any_sync(0xffffffffu, bad);
+            if (fixed && mb != 0u) {
+                const int ex = 156 - static_cast<int>(mb >> 23);  // max |x| * 2^ex in [2^29, 2^30)
+                up = __int_as_float((ex + 127) << 23);
+                down = __int_as_float((127 - ex) << 23);
+            }
+        }
+        if (MT == 1 && fixed) {
+            uint32_t xh[U][8], xl[U][8];
+            #pragma unroll
+            for (int u = 0; u < U; ++u) {
+                #pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const uint32_t a = static_cast<uint32_t>(__float2int_rn(xv[0][u][c].x * up));
+                    const uint32_t b = static_cast<uint32_t>(__float2int_rn(xv[0][u][c].y * up));
+                    xl[u][c] = __byte_perm(a, b, 0x5410);  // low halves (unsigned)
+                    xh[u][c] = __byte_perm(a, b, 0x7632);  // high halves (signed)
+                }
+            }
+            run_groups([&](const uint4 (&w)[R][U], float (&acc)[R * MT]) {
+                #pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    int sh = 0, sl = 0;
+                    #pragma unroll
+                    for (int u = 0; u < U; ++u) {
+                        const int words[4] = {static_cast<int>(w[r][u].x), static_cast<int>(w[r][u].y),
+                                              static_cast<int>(w[r][u].z), static_cast<int>(w[r][u].w)};
+                        #pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            sh = __dp2a_lo(static_cast<int>(xh[u][2 * c]), words[c], sh);
+                            sh = __dp2a_hi(static_cast<int>(xh[u][2 * c + 1]), words[c], sh);
+                            sl = dp2a_lo_us(xl[u][2 * c], words[c], sl);
+                            sl = dp2a_hi_us(xl[u][2 * c + 1], words[c], sl);
+                        }
+                    }
+                    acc[r] = fmaf(static_cast<float>(sh), 65536.0f, static_cast<float>(sl)) * down;
+                }
+            });
+        } else {
+            run_groups(dot_float);
         }
         __syncthreads();
         const int nvals = static_cast<int>(r1 - r0) * MT;
