@@ -85,6 +85,9 @@ __device__ __forceinline__ float absmax_step(float m, float v) {
 __global__ void __launch_bounds__(256)
 x_to_f16_kernel(__half* __restrict__ x16, float* __restrict__ rowscale, const float* __restrict__ x,
                 int64_t M, int64_t K, int vec) {
+    // The GEMM that follows is launched as a programmatic dependent: let it
+    // start its set-up now; it waits for this grid before reading x16.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M;
@@ -149,6 +152,7 @@ template <int U>
 __global__ void __launch_bounds__(kRowThreads)
 x_to_f16_row_kernel(__half* __restrict__ x16, float* __restrict__ rowscale, const float* __restrict__ x, int64_t M,
                     int64_t K) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // see x_to_f16_kernel
     __shared__ float red[2][kRowThreads / 32];
     const int tid = threadIdx.x;
     const int lane = tid & 31;
@@ -312,6 +316,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
         tmem_alloc(smem_addr(tmem_slot), C::kTmemCols);
         tmem_relinquish();
     }
+    // Launched as a programmatic dependent of the x -> f16 prologue: warm L2
+    // with this CTA's first weight tiles (written before the prologue ran,
+    // so already complete), then wait for x16 and rowscale.
+    if (warp == kWarpTma && lane == 0) {
+        for (int i = 0; i < S && i < n_kb; ++i) tma_prefetch_l2_2d(&tmap_w, (kb0 + i) * kBK, n0);
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -511,30 +522,46 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
 // Stages are 128 deep in K: a CTA's TMA ring costs a roughly fixed time per
 // iteration (measured on this part: ~0.4 us whether a stage carries 8 KB or
 // 40 KB), so fewer, bigger stages move the same bytes in half the iterations.
-namespace pair {
-constexpr int kBK = 128;
-constexpr int kSub = kBK / 64;                     // 64-wide f16 swizzle atoms per stage
-constexpr int kRowsX = 128;                        // activation rows per CTA (half of 256)
-constexpr int kStages = 4;
-constexpr int kAStages = 4;                        // 64 columns each
-constexpr int kACols = kBK / 2;
-constexpr int kXBytes = kRowsX * kBK * 2;          // 32 KB (two 16 KB swizzle atoms)
-constexpr int kWBytes = kTileN * kBK;              // 16 KB
-constexpr int kTmemCols = 512;                     // 256 accumulator + 4 x 64 A
-constexpr int kNumBars = 3 * kStages + 2 * kAStages + 2;
-constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16;
-static_assert(kSmem <= 227 * 1024, "shared memory per block");
-}  // namespace pair
+// RX activation rows per CTA (the pair's MMA is 256 x 2*RX): 128 for
+// prefill, 16/32/64 for skinny shapes with many weight tiles, where one MMA
+// instruction now covers both CTAs' 128 weight rows.
+template <int RX>
+struct PairCfg {
+    static constexpr int kBK = 128;
+    static constexpr int kSub = kBK / 64;                  // 64-wide f16 swizzle atoms per stage
+    static constexpr int kRowsX = RX;
+    static constexpr int kXBytes = RX * kBK * 2;           // f16 activation half-tile per stage
+    static constexpr int kWBytes = kTileN * kBK;           // 16 KB int8 weight tile per stage
+    static constexpr int kStages = (RX >= 128) ? 4 : (RX >= 64 ? 6 : 8);
+    static constexpr int kACols = kBK / 2;
+    static constexpr int kAStages = (512 - 2 * RX) / kACols < 8 ? (512 - 2 * RX) / kACols : 7;
+    static constexpr int kTmemCols = 512;                  // 2*RX accumulator + A buffers
+    static constexpr int kNumBars = 3 * kStages + 2 * kAStages + 2;
+    static constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16;
+    static_assert(kSmem <= 227 * 1024, "shared memory per block");
+    static_assert(2 * RX + kAStages * kACols <= kTmemCols, "tensor memory holds 512 columns");
+    static_assert(kXBytes % 1024 == 0, "x16 stages must stay 1024-byte aligned");
+};
 
+template <int RX>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                     float* __restrict__ out, const float* __restrict__ scale, const float* __restrict__ rowscale,
                     int M, int N, int K) {
-    using namespace pair;
-    constexpr int S = kStages;
+    using P = PairCfg<RX>;
+    constexpr int kBK = P::kBK;
+    constexpr int kSub = P::kSub;
+    constexpr int kRowsX = P::kRowsX;
+    constexpr int kXBytes = P::kXBytes;
+    constexpr int kWBytes = P::kWBytes;
+    constexpr int kAStages = P::kAStages;
+    constexpr int kACols = P::kACols;
+    constexpr int kTmemCols = P::kTmemCols;
+    constexpr int kNumBars = P::kNumBars;
+    constexpr int S = P::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* xs = smem;                                  // S x kSub x [128][64] f16, 128B swizzle
+    uint8_t* xs = smem;                                  // S x kSub x [RX][64] f16, 128B swizzle
     uint8_t* ws = smem + S * kXBytes;                    // S x [128][128] int8, 128B swizzle
     uint64_t* bars = reinterpret_cast<uint64_t*>(ws + S * kWBytes);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
@@ -578,12 +605,17 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
         tmem_alloc_pair(smem_addr(tmem_slot), kTmemCols);
         tmem_relinquish_pair();
     }
+    // Programmatic dependent of the prologue (see tc_gemm_kernel).
+    if (warp == kWarpTma && lane == 0) {
+        for (int i = 0; i < S && i < num_kb; ++i) tma_prefetch_l2_2d(&tmap_w, i * kBK, n0);
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     tc_fence_before();
     __syncthreads();
     cluster_sync();  // the peer's barriers exist before anyone arrives on them
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t a_tmem0 = tmem + 2 * kRowsX;  // A buffers after the 256 accumulator columns
+    const uint32_t a_tmem0 = tmem + 2 * kRowsX;  // A buffers after the 2*RX accumulator columns
 
     if (warp == kWarpTma) {
         if (lane == 0) {
@@ -667,8 +699,8 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
             if (lane == 0) mbar_arrive_cluster(afull_leader0 + 8 * a);
         }
     } else {
-        // Epilogue: lane = weight row n of this CTA, 256 accumulator columns =
-        // activation rows mp .. mp + 255 of the pair.
+        // Epilogue: lane = weight row n of this CTA, 2*RX accumulator columns =
+        // activation rows mp .. mp + 2*RX - 1 of the pair.
         const int quarter = warp & 3;
         const int n = n0 + quarter * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
@@ -753,7 +785,7 @@ cudaError_t scratch_pool(cudaMemPool_t* out) {
     return cudaSuccess;
 }
 
-bool g_attr_set[kMaxDevices][5] = {};
+bool g_attr_set[kMaxDevices][8] = {};
 
 // Cluster size for the split-K launch of a tile grid: the largest C in
 // {8, 4, 2} that keeps every CTA resident at once (tiles * C clusters' worth
@@ -815,13 +847,15 @@ popcornStatus_t launch_gemm(int slot, const CUtensorMap& tx, const CUtensorMap& 
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = C::kSmem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(splits);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = splits > 1 ? 1 : 0;
+    cfg.numAttrs = splits > 1 ? 2 : 1;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BM>, tx, tw, out, scale, rowscale,
                                              static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), splits);
     if (e != cudaSuccess) return record_cuda(e);
@@ -858,19 +892,31 @@ bool make_maps(PFN_cuTensorMapEncodeTiled_v12000 encode, __half* x16, const int8
     return r1 == CUDA_SUCCESS && r2 == CUDA_SUCCESS;
 }
 
-popcornStatus_t launch_pair(const CUtensorMap& tx, const CUtensorMap& tw, float* out, const float* scale,
+template <int RX>
+popcornStatus_t launch_pair(int slot, const CUtensorMap& tx, const CUtensorMap& tw, float* out, const float* scale,
                             const float* rowscale, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+    using P = PairCfg<RX>;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < kMaxDevices && !g_attr_set[dev][4]) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             pair::kSmem);
+    if (dev >= 0 && dev < kMaxDevices && !g_attr_set[dev][slot]) {
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_pair_kernel<RX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             P::kSmem);
         if (e != cudaSuccess) return record_cuda(e);
-        g_attr_set[dev][4] = true;
+        g_attr_set[dev][slot] = true;
     }
-    dim3 grid(static_cast<unsigned>(2 * ceil_div(N, 2 * kTileN)), static_cast<unsigned>(ceil_div(M, 2 * pair::kRowsX)));
-    tc_gemm_pair_kernel<<<grid, kThreads, pair::kSmem, stream>>>(tx, tw, out, scale, rowscale, static_cast<int>(M),
-                                                                 static_cast<int>(N), static_cast<int>(K));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * ceil_div(N, 2 * kTileN)), static_cast<unsigned>(ceil_div(M, 2 * RX)));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = P::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<RX>, tx, tw, out, scale, rowscale,
+                                             static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
+    if (e != cudaSuccess) return record_cuda(e);
     return check_launch();
 }
 
@@ -882,10 +928,18 @@ popcornStatus_t launch_tc_gemm(PFN_cuTensorMapEncodeTiled_v12000 encode, __half*
                                cudaStream_t stream) {
     const int bm = pick_bm(M);
     CUtensorMap tx, tw;
-    if (bm >= 256) {
-        if (!make_maps(encode, x16, q, M, N, K, pair::kRowsX, pair::kBK, &tx, &tw)) return POPCORN_ERROR_INVALID_VALUE;
-        static_assert(pair::kBK == 128, "make_maps: 128-deep weight boxes use the 128B swizzle");
-        return launch_pair(tx, tw, out, scale, rowscale, M, N, K, stream);
+    // CTA pairs: always for M > 128; for smaller M when there are more
+    // 128-row weight tiles than half the SMs (the single-CTA kernel with
+    // cluster split-K serves the rest).
+    if (bm >= 256 || ceil_div(N, kTileN) * 2 > device_sm_count()) {
+        const int rx = bm / 2;
+        if (!make_maps(encode, x16, q, M, N, K, rx, 128, &tx, &tw)) return POPCORN_ERROR_INVALID_VALUE;
+        switch (rx) {
+            case 16: return launch_pair<16>(4, tx, tw, out, scale, rowscale, M, N, K, stream);
+            case 32: return launch_pair<32>(5, tx, tw, out, scale, rowscale, M, N, K, stream);
+            case 64: return launch_pair<64>(6, tx, tw, out, scale, rowscale, M, N, K, stream);
+            default: return launch_pair<128>(7, tx, tw, out, scale, rowscale, M, N, K, stream);
+        }
     }
     if (!make_maps(encode, x16, q, M, N, K, bm, 128, &tx, &tw)) return POPCORN_ERROR_INVALID_VALUE;
     switch (bm) {

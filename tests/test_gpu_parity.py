@@ -346,6 +346,55 @@ def test_tensor_path_shapes(cuda, M, N, K):
     assert err <= 5e-4, err
 
 
+@pytest.mark.parametrize("M,N,K", [(5, 9600, 512), (16, 9601, 256), (33, 9500, 1024), (64, 9728, 2048),
+                                   (100, 10000, 1024), (128, 12288, 4096), (130, 9600, 512)])
+def test_tensor_path_pairs_for_many_weight_tiles(cuda, M, N, K):
+    # More 128-row weight tiles than half the SMs: CTA pairs (cta_group::2)
+    # with 16/32/64/128 activation rows per CTA, odd M and N tails included.
+    import torch
+
+    x, q, s = random_case(M, N, K, 7 + M + N + K)
+    got = abi_matmul(torch, cuda, x, q, s, path=pc.PATH_TENSOR_F16)
+    assert pc.device_errors() == 0
+    ref = oracle.dequant_matmul(x, q, s, fused=True, threads=8)
+    err = oracle.normwise_rel_err(got, ref)
+    assert err <= 5e-4, err
+
+
+def test_f32_path_fixed_point_edges(cuda):
+    # The M = 1 decode kernel computes in fixed point per thread slice; warps
+    # whose slice holds a non-finite or extreme |x| take the float path.
+    # Check both, and rows mixing them, against the oracle.
+    import torch
+
+    N, K = 1024, 4096
+    x, q, s = random_case(1, N, K, 31)
+    ref = oracle.dequant_matmul(x, q, s, fused=True, threads=8)
+    for scale in (1.0, 2.0 ** -80, 2.0 ** -95, 2.0 ** 95, 2.0 ** 105):
+        got = abi_matmul(torch, cuda, (x * scale).astype(np.float32), q, s)
+        want = oracle.dequant_matmul((x * scale).astype(np.float32), q, s, fused=True, threads=8)
+        assert oracle.normwise_rel_err(got, want) <= TOL_F32, scale
+    # one slice far below the others (its warp falls back), zero slices
+    xm = x.copy()
+    xm[0, :64] *= 2.0 ** -120
+    xm[0, 2048:2560] = 0.0
+    got = abi_matmul(torch, cuda, xm, q, s)
+    assert oracle.normwise_rel_err(got, oracle.dequant_matmul(xm, q, s, fused=True, threads=8)) <= TOL_F32
+    # a single inf: every output is +-inf (or NaN where the code is 0)
+    xi = x.copy()
+    xi[0, 100] = np.inf
+    got = abi_matmul(torch, cuda, xi, q, s)
+    want = oracle.dequant_matmul(xi, q, s, fused=True, threads=8)
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    assert np.array_equal(got[np.isinf(want)], want[np.isinf(want)])
+    # a NaN poisons every output
+    xn = x.copy()
+    xn[0, 4000] = np.nan
+    assert np.all(np.isnan(abi_matmul(torch, cuda, xn, q, s)))
+    assert pc.device_errors() == 0
+    assert oracle.normwise_rel_err(abi_matmul(torch, cuda, x, q, s), ref) <= TOL_F32
+
+
 def test_tensor_path_row_scaling_handles_extreme_rows(cuda):
     # Rows of wildly different magnitude, an all-zero row, a NaN row and an
     # infinite entry: every finite row keeps f16 relative precision.
