@@ -516,9 +516,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
 //             complete their bytes on the leader's barrier; only the leader
 //             posts the expected byte count);
 //   wfull[s]  this CTA's weight tile landed (local);
-//   afull[a]  both CTAs' converters wrote A buffer a (8 remote arrivals);
-//   empty[s], aempty[a], acc_full, drain: multicast tcgen05.commit from the
-//             leader to the same barrier in both CTAs.
+//   afull[s]  both CTAs' converters wrote A buffer s (8 remote arrivals);
+//   release[s], acc_full, drain: multicast tcgen05.commit from the leader to
+//             the same barrier in both CTAs (release[s] frees ring slot s:
+//             its shared-memory tiles and A buffer s).
 // Stages are 128 deep in K: a CTA's TMA ring costs a roughly fixed time per
 // iteration (measured on this part: ~0.4 us whether a stage carries 8 KB or
 // 40 KB), so fewer, bigger stages move the same bytes in half the iterations.
@@ -532,11 +533,15 @@ struct PairCfg {
     static constexpr int kRowsX = RX;
     static constexpr int kXBytes = RX * kBK * 2;           // f16 activation half-tile per stage
     static constexpr int kWBytes = kTileN * kBK;           // 16 KB int8 weight tile per stage
-    static constexpr int kStages = (RX >= 128) ? 4 : (RX >= 64 ? 6 : 8);
     static constexpr int kACols = kBK / 2;
-    static constexpr int kAStages = (512 - 2 * RX) / kACols < 8 ? (512 - 2 * RX) / kACols : 7;
     static constexpr int kTmemCols = 512;                  // 2*RX accumulator + A buffers
-    static constexpr int kNumBars = 3 * kStages + 2 * kAStages + 2;
+    // Ring slot s is also A buffer s (one release barrier frees both):
+    // as many stages as both shared and tensor memory hold.
+    static constexpr int kSmemStages = (RX >= 128) ? 4 : (RX >= 64 ? 6 : 8);
+    static constexpr int kTmemStages = (kTmemCols - 2 * RX) / kACols;
+    static constexpr int kStages = kSmemStages < kTmemStages ? kSmemStages : kTmemStages;
+    static constexpr int kAStages = kStages;
+    static constexpr int kNumBars = 4 * kStages + 2;
     static constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16;
     static_assert(kSmem <= 227 * 1024, "shared memory per block");
     static_assert(2 * RX + kAStages * kACols <= kTmemCols, "tensor memory holds 512 columns");
@@ -554,7 +559,6 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
     constexpr int kRowsX = P::kRowsX;
     constexpr int kXBytes = P::kXBytes;
     constexpr int kWBytes = P::kWBytes;
-    constexpr int kAStages = P::kAStages;
     constexpr int kACols = P::kACols;
     constexpr int kTmemCols = P::kTmemCols;
     constexpr int kNumBars = P::kNumBars;
@@ -566,12 +570,15 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
     uint64_t* bars = reinterpret_cast<uint64_t*>(ws + S * kWBytes);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
 
+    // full[s]: both activation halves landed (leader). wfull[s]: this CTA's
+    // weight tile landed. afull[s]: both CTAs' converters wrote A buffer s.
+    // release[s]: the MMAs of slot s finished (multicast commit to both
+    // CTAs): its tiles and A buffer may be refilled.
     const uint32_t full0 = smem_addr(bars);
     const uint32_t wfull0 = full0 + 8 * S;
-    const uint32_t empty0 = wfull0 + 8 * S;
-    const uint32_t afull0 = empty0 + 8 * S;
-    const uint32_t aempty0 = afull0 + 8 * kAStages;
-    const uint32_t acc_full = aempty0 + 8 * kAStages;
+    const uint32_t release0 = wfull0 + 8 * S;
+    const uint32_t afull0 = release0 + 8 * S;
+    const uint32_t acc_full = afull0 + 8 * S;
     const uint32_t drain = acc_full + 8;
 
     const int warp = threadIdx.x >> 5;
@@ -587,11 +594,8 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
         for (int s = 0; s < S; ++s) {
             mbar_init(full0 + 8 * s, 1);
             mbar_init(wfull0 + 8 * s, 1);
-            mbar_init(empty0 + 8 * s, 1);
-        }
-        for (int a = 0; a < kAStages; ++a) {
-            mbar_init(afull0 + 8 * a, 2 * 4);  // four converter warps in each CTA
-            mbar_init(aempty0 + 8 * a, 1);
+            mbar_init(release0 + 8 * s, 1);
+            mbar_init(afull0 + 8 * s, 2 * 4);  // four converter warps in each CTA
         }
         mbar_init(acc_full, 1);
         mbar_init(drain, 1);
@@ -622,7 +626,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
             const uint32_t full_leader0 = mapa_shared(full0, 0);
             for (int kb = 0; kb < num_kb; ++kb) {
                 const int s = kb % S;
-                if (kb >= S && !mbar_wait_cluster(empty0 + 8 * s, ((kb / S) - 1) & 1, err, 1u)) break;
+                if (kb >= S && !mbar_wait_cluster(release0 + 8 * s, ((kb / S) - 1) & 1, err, 1u)) break;
                 if (leader) mbar_arrive_expect_tx(full0 + 8 * s, 2 * kXBytes);
                 mbar_arrive_expect_tx(wfull0 + 8 * s, kWBytes);
                 #pragma unroll
@@ -644,9 +648,9 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
             constexpr uint32_t idesc = idesc_f16_f32(2 * kTileN, 2 * kRowsX);
             for (int kb = 0; kb < num_kb; ++kb) {
                 const int s = kb % S;
-                const int a = kb % kAStages;
+                const int a = s;
                 if (!mbar_wait_cluster(full0 + 8 * s, (kb / S) & 1, err, 2u)) break;
-                if (!mbar_wait_cluster(afull0 + 8 * a, (kb / kAStages) & 1, err, 4u)) break;
+                if (!mbar_wait_cluster(afull0 + 8 * a, (kb / S) & 1, err, 4u)) break;
                 tc_fence_after();
                 #pragma unroll
                 for (int j = 0; j < kBK / 16; ++j) {
@@ -654,8 +658,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
                     mma_f16_ts_pair(tmem, a_tmem0 + a * kACols + j * 8, bdesc + static_cast<uint64_t>((j % 4) * 2),
                                     idesc, (kb | j) != 0 ? 1u : 0u);
                 }
-                mma_commit_pair(empty0 + 8 * s, 0x3);
-                mma_commit_pair(aempty0 + 8 * a, 0x3);
+                mma_commit_pair(release0 + 8 * s, 0x3);
             }
             mma_commit_pair(acc_full, 0x3);
             mma_commit_pair(drain, 0x3);
@@ -669,9 +672,9 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
         const uint32_t afull_leader0 = mapa_shared(afull0, 0);
         for (int kb = group; kb < num_kb; kb += kConvGroups) {
             const int s = kb % S;
-            const int a = kb % kAStages;
+            const int a = s;
             bool ok = mbar_wait(wfull0 + 8 * s, (kb / S) & 1, err, 8u);
-            if (ok && kb >= kAStages) ok = mbar_wait_cluster(aempty0 + 8 * a, ((kb / kAStages) - 1) & 1, err, 16u);
+            if (ok && kb >= S) ok = mbar_wait_cluster(release0 + 8 * s, ((kb / S) - 1) & 1, err, 16u);
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
             const uint8_t* row = ws + s * kWBytes + r * kBK;
