@@ -609,11 +609,6 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
         tmem_alloc_pair(smem_addr(tmem_slot), kTmemCols);
         tmem_relinquish_pair();
     }
-    // Programmatic dependent of the prologue (see tc_gemm_kernel).
-    if (warp == kWarpTma && lane == 0) {
-        for (int i = 0; i < S && i < num_kb; ++i) tma_prefetch_l2_2d(&tmap_w, i * kBK, n0);
-    }
-    asm volatile("griddepcontrol.wait;" ::: "memory");
     tc_fence_before();
     __syncthreads();
     cluster_sync();  // the peer's barriers exist before anyone arrives on them
@@ -621,20 +616,33 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
     const uint32_t tmem = *tmem_slot;
     const uint32_t a_tmem0 = tmem + 2 * kRowsX;  // A buffers after the 2*RX accumulator columns
 
+    // Launched as a programmatic dependent of the x -> f16 prologue. The
+    // weights were written before the prologue ran, so the first ring of
+    // weight tiles is requested (and converted) while the prologue still
+    // runs; only the activation loads and the epilogue's row scales wait
+    // for it (griddepcontrol.wait in those threads).
     if (warp == kWarpTma) {
         if (lane == 0) {
             const uint32_t full_leader0 = mapa_shared(full0, 0);
+            const int first = num_kb < S ? num_kb : S;
+            for (int kb = 0; kb < first; ++kb) {
+                mbar_arrive_expect_tx(wfull0 + 8 * kb, kWBytes);
+                tma_load_2d(smem_addr(ws + kb * kWBytes), &tmap_w, kb * kBK, n0, wfull0 + 8 * kb);
+            }
+            asm volatile("griddepcontrol.wait;" ::: "memory");
             for (int kb = 0; kb < num_kb; ++kb) {
                 const int s = kb % S;
                 if (kb >= S && !mbar_wait_cluster(release0 + 8 * s, ((kb / S) - 1) & 1, err, 1u)) break;
                 if (leader) mbar_arrive_expect_tx(full0 + 8 * s, 2 * kXBytes);
-                mbar_arrive_expect_tx(wfull0 + 8 * s, kWBytes);
                 #pragma unroll
                 for (int sub = 0; sub < kSub; ++sub) {
                     tma_load_2d_pair(smem_addr(xs + s * kXBytes + sub * kRowsX * 128), &tmap_x, kb * kBK + sub * 64,
                                      mp + static_cast<int>(rank) * kRowsX, full_leader0 + 8 * s);
                 }
-                tma_load_2d(smem_addr(ws + s * kWBytes), &tmap_w, kb * kBK, n0, wfull0 + 8 * s);
+                if (kb >= first) {
+                    mbar_arrive_expect_tx(wfull0 + 8 * s, kWBytes);
+                    tma_load_2d(smem_addr(ws + s * kWBytes), &tmap_w, kb * kBK, n0, wfull0 + 8 * s);
+                }
             }
             // Leave no copy of ours in flight: the weight tiles signal this CTA;
             // the activation halves are covered by the drain below (the leader
@@ -707,6 +715,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
         const int quarter = warp & 3;
         const int n = n0 + quarter * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        asm volatile("griddepcontrol.wait;" ::: "memory");  // row scales come from the prologue
         const bool ok = mbar_wait_cluster(acc_full, 0, err, 32u);
         if (__all_sync(0xffffffffu, ok)) {
             tc_fence_after();
