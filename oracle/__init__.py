@@ -45,8 +45,11 @@ def _load():
         lib.oracle_quantize_i8.argtypes = [_vp, _vp, _vp, _i64, _i64, _int]
         lib.oracle_dequantize_i8.argtypes = [_vp, _vp, _vp, _i64, _i64]
         lib.oracle_fill_normal.argtypes = [_vp, _i64, ctypes.c_uint64, ctypes.c_float]
+        lib.oracle_dequant_matmul_grouped_i8.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int]
+        lib.oracle_quantize_grouped_i8.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _int]
         for f in (lib.oracle_dequant_matmul_i8, lib.oracle_dequant_matmul_i8_mt, lib.oracle_quantize_i8,
-                  lib.oracle_dequantize_i8, lib.oracle_fill_normal):
+                  lib.oracle_dequantize_i8, lib.oracle_fill_normal, lib.oracle_dequant_matmul_grouped_i8,
+                  lib.oracle_quantize_grouped_i8):
             f.restype = None
         _lib = lib
     return _lib
@@ -89,6 +92,31 @@ def quantize(w, ties_away: bool = False):
     return q, s
 
 
+def dequant_matmul_grouped(x, q, scale, group_size: int, fused: bool = False, threads: int = 1) -> np.ndarray:
+    """out[M,N] = sum_k x[m,k] * (q[n,k] * scale[n, k // group_size]) with popcorn's k order."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    scale = np.ascontiguousarray(scale, dtype=np.float32)
+    M, K = x.shape
+    N = q.shape[0]
+    assert K % group_size == 0 and scale.size == N * (K // group_size)
+    out = np.empty((M, N), dtype=np.float32)
+    _load().oracle_dequant_matmul_grouped_i8(_ptr(out), _ptr(x), _ptr(q), _ptr(scale), M, N, K, group_size,
+                                             int(fused), threads)
+    return out
+
+
+def quantize_grouped(w, group_size: int, ties_away: bool = False):
+    """(codes int8 [N,K], scales f32 [N, K/group_size]); rintf unless ties_away."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    N, K = w.shape
+    assert K % group_size == 0
+    q = np.empty((N, K), dtype=np.int8)
+    s = np.empty((N, K // group_size), dtype=np.float32)
+    _load().oracle_quantize_grouped_i8(_ptr(q), _ptr(s), _ptr(w), N, K, group_size, int(ties_away))
+    return q, s
+
+
 def dequantize(q, scale) -> np.ndarray:
     q = np.ascontiguousarray(q, dtype=np.int8)
     scale = np.ascontiguousarray(scale, dtype=np.float32)
@@ -124,7 +152,10 @@ def ref_loops():
         lib.ref_loops_dequant_matmul_i8.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64]
         lib.ref_loops_dequant_matmul_i8_mt.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int]
         lib.ref_loops_quantize_i8.argtypes = [_vp, _vp, _vp, _i64, _i64]
-        for f in (lib.ref_loops_dequant_matmul_i8, lib.ref_loops_dequant_matmul_i8_mt, lib.ref_loops_quantize_i8):
+        lib.ref_loops_dequant_matmul_grouped_i8.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64]
+        lib.ref_loops_quantize_grouped_i8.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64]
+        for f in (lib.ref_loops_dequant_matmul_i8, lib.ref_loops_dequant_matmul_i8_mt, lib.ref_loops_quantize_i8,
+                  lib.ref_loops_dequant_matmul_grouped_i8, lib.ref_loops_quantize_grouped_i8):
             f.restype = None
         _ref_loops = lib
     return _ref_loops
@@ -153,6 +184,26 @@ def ref_quantize(w):
     return q, s
 
 
+def ref_dequant_matmul_grouped(x, q, scale, group_size: int) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    scale = np.ascontiguousarray(scale, dtype=np.float32)
+    M, K = x.shape
+    N = q.shape[0]
+    out = np.empty((M, N), dtype=np.float32)
+    ref_loops().ref_loops_dequant_matmul_grouped_i8(_ptr(out), _ptr(x), _ptr(q), _ptr(scale), M, N, K, group_size)
+    return out
+
+
+def ref_quantize_grouped(w, group_size: int):
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    N, K = w.shape
+    q = np.empty((N, K), dtype=np.int8)
+    s = np.empty((N, K // group_size), dtype=np.float32)
+    ref_loops().ref_loops_quantize_grouped_i8(_ptr(q), _ptr(s), _ptr(w), N, K, group_size)
+    return q, s
+
+
 def have_popcorn_ref_gpu() -> bool:
     return os.path.exists(REF_GPU_LIB)
 
@@ -168,5 +219,9 @@ def popcorn_ref_gpu():
         lib.popcornDequantizeMatmulBatched_i8f32.restype = _int
         lib.popcornQuantize_f32i8.argtypes = [_vp, _vp, _vp, _i64, _i64, _vp]
         lib.popcornQuantize_f32i8.restype = _int
+        lib.popcornDequantizeMatmulGrouped_i8f32.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]
+        lib.popcornDequantizeMatmulGrouped_i8f32.restype = _int
+        lib.popcornQuantizeGrouped_f32i8.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _vp]
+        lib.popcornQuantizeGrouped_f32i8.restype = _int
         _ref_gpu = lib
     return _ref_gpu

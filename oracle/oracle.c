@@ -129,6 +129,90 @@ void oracle_quantize_i8(int8_t* out, float* scale, const float* in, int64_t N, i
     }
 }
 
+typedef struct {
+    float* out;
+    const float* x;
+    const int8_t* q;
+    const float* scale;
+    int64_t M, N, K, gs, n0, n1;
+    int fused;
+} gmm_job;
+
+static void* gmm_worker(void* arg) {
+    /* popcorn test/test_quantize.cu:51-58 and src/quantize.cu:168-177: for
+     * each output, walk k upward; the code times its group's scale, then the
+     * multiply-add with the activation. */
+    const gmm_job* j = (const gmm_job*)arg;
+    const int64_t groups = j->K / j->gs;
+    for (int64_t m = 0; m < j->M; m++) {
+        const float* xr = j->x + m * j->K;
+        for (int64_t n = j->n0; n < j->n1; n++) {
+            const int8_t* qr = j->q + n * j->K;
+            const float* sr = j->scale + n * groups;
+            float acc = 0.0f;
+            for (int64_t k = 0; k < j->K; k++) {
+                const float w = (float)qr[k] * sr[k / j->gs];
+                if (j->fused) {
+                    acc = fmaf(xr[k], w, acc);
+                } else {
+                    const float p = xr[k] * w;
+                    acc = acc + p;
+                }
+            }
+            j->out[m * j->N + n] = acc;
+        }
+    }
+    return NULL;
+}
+
+void oracle_dequant_matmul_grouped_i8(float* out, const float* x, const int8_t* q, const float* scale, int64_t M,
+                                      int64_t N, int64_t K, int64_t gs, int fused, int threads) {
+    if (threads < 1) threads = 1;
+    if (threads > N) threads = (int)N;
+    if (threads < 1) return;
+    pthread_t* tid = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)threads);
+    gmm_job* jobs = (gmm_job*)malloc(sizeof(gmm_job) * (size_t)threads);
+    for (int t = 0; t < threads; t++) {
+        gmm_job j = {out, x, q, scale, M, N, K, gs, N * t / threads, N * (t + 1) / threads, fused};
+        jobs[t] = j;
+        if (threads > 1) pthread_create(&tid[t], NULL, gmm_worker, &jobs[t]);
+    }
+    if (threads > 1) {
+        for (int t = 0; t < threads; t++) pthread_join(tid[t], NULL);
+    } else {
+        gmm_worker(&jobs[0]);
+    }
+    free(jobs);
+    free(tid);
+}
+
+void oracle_quantize_grouped_i8(int8_t* out, float* scale, const float* in, int64_t N, int64_t K, int64_t gs,
+                                int ties) {
+    const int64_t groups = K / gs;
+    for (int64_t n = 0; n < N; n++) {
+        for (int64_t g = 0; g < groups; g++) {
+            const float* r = in + n * K + g * gs;
+            /* Group max of |v|, NaN skipped by the compare (src/quantize.cu:585-592). */
+            float max_abs = 0.0f;
+            for (int64_t i = 0; i < gs; i++) {
+                const float v = r[i];
+                const float a = v < 0 ? -v : v;
+                if (a > max_abs) max_abs = a;
+            }
+            float sc = max_abs / 127.0f;
+            if (sc == 0.0f) sc = 1.0f;
+            scale[n * groups + g] = sc;
+            for (int64_t i = 0; i < gs; i++) {
+                const float d = r[i] / sc;
+                float qv = ties ? roundf(d) : rintf(d);
+                if (qv > 127.0f) qv = 127.0f;
+                if (qv < -128.0f) qv = -128.0f;
+                out[n * K + g * gs + i] = (qv != qv) ? (int8_t)0 : (int8_t)qv;  /* NaN -> 0 as on the GPU */
+            }
+        }
+    }
+}
+
 void oracle_dequantize_i8(float* out, const int8_t* q, const float* scale, int64_t N, int64_t K) {
     for (int64_t n = 0; n < N; n++) {
         const float sc = scale[n];

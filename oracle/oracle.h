@@ -36,6 +36,19 @@ void oracle_dequant_matmul_i8_mt(float* out, const float* x, const int8_t* q, co
  *           (test/test_quantize.cu:700). */
 void oracle_quantize_i8(int8_t* out, float* scale, const float* in, int64_t N, int64_t K, int ties);
 
+/* Per-group variant (src/quantize.cu:114-218, test/test_quantize.cu:42-61):
+ * out[m,n] = sum_k x[m,k] * ((float)q[n,k] * scale[n, k / gs]), k ascending,
+ * scale [N, K/gs]; `fused` as above; split over `threads` by channel. */
+void oracle_dequant_matmul_grouped_i8(float* out, const float* x, const int8_t* q, const float* scale, int64_t M,
+                                      int64_t N, int64_t K, int64_t gs, int fused, int threads);
+
+/* Per-group symmetric int8 quantization (src/quantize.cu:571-640,
+ * test/test_quantize.cu:709-742): every group of gs consecutive values of a
+ * row gets its own scale = max|v| / 127 (1 if 0), NaN skipped; `ties` as in
+ * oracle_quantize_i8. scale is [N, K/gs]. */
+void oracle_quantize_grouped_i8(int8_t* out, float* scale, const float* in, int64_t N, int64_t K, int64_t gs,
+                                int ties);
+
 /* out[n,k] = (float)q[n,k] * scale[n]. */
 void oracle_dequantize_i8(float* out, const int8_t* q, const float* scale, int64_t N, int64_t K);
 

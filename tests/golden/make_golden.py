@@ -9,8 +9,10 @@ Inputs are the reference test suite's own in-test fixtures, rebuilt here with
 the same formulas (each case cites popcorn test/test_quantize.cu), plus the
 seeded host-parity configuration (M=16, K=1024, N=1024; X ~ N(0,1), W ~
 N(0,0.02), per-row int8). Expected outputs come from the reference loops
-``ref_dequant_matmul_i8`` (:24-41) and ``ref_quantize_i8`` (:677-706), compiled
-from the reference sources, never from this repository's code. Cases whose
+``ref_dequant_matmul_i8`` (:24-41), ``ref_quantize_i8`` (:677-706) and their
+per-group forms ``ref_dequant_matmul_grouped_i8`` (:42-61) and
+``ref_quantize_grouped_i8`` (:709-742), compiled from the reference sources,
+never from this repository's code. Cases whose
 values the test spells out (the identity test) also store those values.
 """
 import hashlib
@@ -95,6 +97,23 @@ def quantize_cases():
     return cases
 
 
+def grouped_cases():
+    cases = {}
+    # dequant_matmul_grouped_i8_basic, test_quantize.cu:283-327 (M2 N3 K8, group 4)
+    x = f32([[1, 2, 3, 4, 5, 6, 7, 8], [-1, -2, -3, -4, -5, -6, -7, -8]])
+    q = np.array([[1, 2, 3, 4, 5, 6, 7, 8], [-1, -2, -3, -4, -5, -6, -7, -8], [1, 1, 1, 1, 2, 2, 2, 2]],
+                 dtype=np.int8)
+    s = f32([[0.5, 0.25], [1.0, 0.5], [0.1, 0.2]])
+    cases["g_basic"] = (x, q, s, 4)
+    # dequant_matmul_grouped_i8_large, :329-379 (M32 N64 K128, group 32, patterned data)
+    M, N, K, gs = 32, 64, 128, 32
+    x = ((np.arange(M * K) % 50).astype(np.float32) - np.float32(25.0)) * np.float32(0.02)
+    q = ((np.arange(N * K) % 200) - 100).astype(np.int8)
+    s = np.float32(0.005) + (np.arange(N * (K // gs)) % 20).astype(np.float32) * np.float32(0.001)
+    cases["g_large"] = (x.reshape(M, K), q.reshape(N, K), s.reshape(N, K // gs), gs)
+    return cases
+
+
 def config1_inputs():
     c = CONFIG1
     x = oracle.fill_normal(c["M"] * c["K"], c["x_seed"], c["x_sigma"]).reshape(c["M"], c["K"])
@@ -121,6 +140,16 @@ def main():
     for name, w in quantize_cases().items():
         qr, sr = oracle.ref_quantize(w)
         data[f"{name}/w"], data[f"{name}/codes_test_loop"], data[f"{name}/scale"] = w, qr, sr
+
+    for name, (x, q, s, gs) in grouped_cases().items():
+        data[f"{name}/x"], data[f"{name}/q"], data[f"{name}/scale"] = x, q, s
+        data[f"{name}/group_size"] = np.array(gs, dtype=np.int64)
+        data[f"{name}/out"] = oracle.ref_dequant_matmul_grouped(x, q, s, gs)
+    # quantize_grouped_i8_basic, :875-917 (N2 K8, group 4)
+    w = f32([[1, 2, 3, 4, -8, -6, -4, -2], [0.1, 0.2, 0.3, 0.4, 12.7, 0, -12.7, 6.35]])
+    qr, sr = oracle.ref_quantize_grouped(w, 4)
+    data["qg_basic/w"], data["qg_basic/codes_test_loop"], data["qg_basic/scale"] = w, qr, sr
+    data["qg_basic/group_size"] = np.array(4, dtype=np.int64)
 
     x, w = config1_inputs()
     q, s = oracle.ref_quantize(w)

@@ -136,3 +136,47 @@ def test_planted_oracle_mistake_is_caught():
     q, s = oracle.ref_quantize(w)
     wrong = oracle.dequant_matmul(x, q, s * s)
     assert not np.array_equal(wrong, oracle.ref_dequant_matmul(x, q, s))
+
+
+# ---------------------------------------------------------------------------
+# Per-group int8 (popcorn src/quantize.cu:114-218, :571-640; its CPU loops
+# test/test_quantize.cu:42-61, :709-742).
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("case", ["g_basic", "g_large"])
+def test_grouped_matmul_matches_reference_loop_bitwise(golden, case):
+    gs = int(golden[f"{case}/group_size"])
+    out = oracle.dequant_matmul_grouped(golden[f"{case}/x"], golden[f"{case}/q"], golden[f"{case}/scale"], gs)
+    np.testing.assert_array_equal(out, golden[f"{case}/out"])
+    out3 = oracle.dequant_matmul_grouped(golden[f"{case}/x"], golden[f"{case}/q"], golden[f"{case}/scale"], gs,
+                                         threads=3)
+    np.testing.assert_array_equal(out3, golden[f"{case}/out"])
+
+
+def test_grouped_quantize_roundf_matches_reference_loop(golden):
+    q, s = oracle.quantize_grouped(golden["qg_basic/w"], int(golden["qg_basic/group_size"]), ties_away=True)
+    np.testing.assert_array_equal(q, golden["qg_basic/codes_test_loop"])
+    np.testing.assert_array_equal(s, golden["qg_basic/scale"])
+
+
+def test_grouped_with_one_group_is_the_per_channel_path():
+    x = oracle.fill_normal(3 * 64, 5, 1.0).reshape(3, 64)
+    w = oracle.fill_normal(9 * 64, 6, 0.02).reshape(9, 64)
+    q, s = oracle.quantize(w)
+    qg, sg = oracle.quantize_grouped(w, 64)
+    np.testing.assert_array_equal(q, qg)
+    np.testing.assert_array_equal(s, sg[:, 0])
+    np.testing.assert_array_equal(oracle.dequant_matmul(x, q, s), oracle.dequant_matmul_grouped(x, qg, sg, 64))
+
+
+@pytest.mark.skipif(not oracle.have_ref_loops(), reason="reference loops not built (oracle/_ref)")
+@pytest.mark.parametrize("shape", [(1, 7, 8, 4), (3, 17, 64, 16), (5, 33, 96, 32), (4, 40, 256, 128), (2, 9, 48, 48)])
+def test_grouped_oracle_equals_reference_loops_random(shape):
+    M, N, K, gs = shape
+    x = oracle.fill_normal(M * K, M + N, 1.0).reshape(M, K)
+    w = oracle.fill_normal(N * K, K, 0.02).reshape(N, K)
+    qr, sr = oracle.ref_quantize_grouped(w, gs)
+    qo, so = oracle.quantize_grouped(w, gs, ties_away=True)
+    np.testing.assert_array_equal(qr, qo)
+    np.testing.assert_array_equal(sr, so)
+    np.testing.assert_array_equal(oracle.ref_dequant_matmul_grouped(x, qr, sr, gs),
+                                  oracle.dequant_matmul_grouped(x, qr, sr, gs, threads=2))
