@@ -113,6 +113,52 @@ popcornStatus_t popcornQuantize_f32i8(
     cudaStream_t stream
 );
 
+/*
+ * Per-group int8 dequant-matmul:
+ *   out[m, n] = sum_k x[m, k] * (qweight[n, k] * scale[n, k / group_size])
+ * with scale row-major [N, K / group_size]. group_size must be positive and
+ * divide K (else POPCORN_ERROR_INVALID_VALUE, checked after the null
+ * pointers and the size <= 0 no-op, as popcorn does).
+ *
+ * Replaces popcorn's popcornDequantizeMatmulGrouped_i8f32
+ * (include/popcorn.h:475-487, src/quantize.cu:114-218). f32 arithmetic:
+ * small problems and group sizes that are not a multiple of 16 follow
+ * popcorn's own operation order (bit-identical to its kernel); otherwise the
+ * group scale multiplies each 16-column partial sum, within f32 rounding of
+ * popcorn's result.
+ */
+popcornStatus_t popcornDequantizeMatmulGrouped_i8f32(
+    float* out,
+    const float* x,
+    const int8_t* qweight,
+    const float* scale,
+    int64_t M,
+    int64_t N,
+    int64_t K,
+    int64_t group_size,
+    cudaStream_t stream
+);
+
+/*
+ * Per-group symmetric int8 quantization: every group of group_size
+ * consecutive values of a row gets its own scale
+ *   scale[n, g] = max |input[n, g*gs .. (g+1)*gs)| / 127   (1.0 when 0)
+ *   out[n, k]   = rint(input[n, k] / scale[n, k / gs]) clamped to [-128, 127]
+ *
+ * Replaces popcorn's popcornQuantizeGrouped_f32i8 (include/popcorn.h:536-546,
+ * src/quantize.cu:567-697): codes and scales bit-identical to its kernels,
+ * no temporary allocation, no device synchronization.
+ */
+popcornStatus_t popcornQuantizeGrouped_f32i8(
+    int8_t* out,
+    float* scale,
+    const float* input,
+    int64_t N,
+    int64_t K,
+    int64_t group_size,
+    cudaStream_t stream
+);
+
 #ifdef __cplusplus
 }
 #endif

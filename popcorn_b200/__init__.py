@@ -41,6 +41,8 @@ ABI_SYMBOLS = (
     "popcornDequantizeMatmul_i8f32",
     "popcornDequantizeMatmulBatched_i8f32",
     "popcornQuantize_f32i8",
+    "popcornDequantizeMatmulGrouped_i8f32",
+    "popcornQuantizeGrouped_f32i8",
 )
 EXT_SYMBOLS = (
     "popcornDequantize_i8f32",
@@ -78,6 +80,8 @@ _SIGNATURES = {
     "popcornDequantizeMatmul_i8f32": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "popcornDequantizeMatmulBatched_i8f32": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "popcornQuantize_f32i8": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
+    "popcornDequantizeMatmulGrouped_i8f32": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "popcornQuantizeGrouped_f32i8": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "popcornDequantize_i8f32": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "popcornDequantizeMatmulPath_i8f32": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "popcornDequantizeMatmulSelectPath": (_int, [_vp, _vp, _i64, _i64, _i64]),
@@ -146,6 +150,14 @@ def popcornDequantizeMatmulBatched_i8f32(out, x, qweight, scale, B, M, N, K, str
 
 def popcornQuantize_f32i8(out, scale, inp, N, K, stream=0) -> int:
     return load_library().popcornQuantize_f32i8(out, scale, inp, N, K, stream)
+
+
+def popcornDequantizeMatmulGrouped_i8f32(out, x, qweight, scale, M, N, K, group_size, stream=0) -> int:
+    return load_library().popcornDequantizeMatmulGrouped_i8f32(out, x, qweight, scale, M, N, K, group_size, stream)
+
+
+def popcornQuantizeGrouped_f32i8(out, scale, inp, N, K, group_size, stream=0) -> int:
+    return load_library().popcornQuantizeGrouped_f32i8(out, scale, inp, N, K, group_size, stream)
 
 
 def popcornDequantize_i8f32(out, qweight, scale, N, K, stream=0) -> int:
@@ -233,6 +245,35 @@ def quantize(w, out=None, scale=None, stream=None):
     st = _stream_handle(stream)
     _check(popcornQuantize_f32i8(out.data_ptr(), scale.data_ptr(), w.data_ptr(), N, K, st), "popcornQuantize_f32i8")
     return out, scale
+
+
+def quantize_grouped(w, group_size: int, out=None, scale=None, stream=None):
+    """Per-group symmetric int8 quantization of f32 [N, K] -> (codes [N, K], scales [N, K / group_size])."""
+    import torch
+
+    N, K = w.shape
+    if out is None:
+        out = torch.empty((N, K), dtype=torch.int8, device=w.device)
+    if scale is None:
+        scale = torch.empty((N, K // group_size), dtype=torch.float32, device=w.device)
+    st = _stream_handle(stream)
+    _check(popcornQuantizeGrouped_f32i8(out.data_ptr(), scale.data_ptr(), w.data_ptr(), N, K, group_size, st),
+           "popcornQuantizeGrouped_f32i8")
+    return out, scale
+
+
+def dequantize_matmul_grouped(x, qweight, scale, group_size: int, out=None, stream=None):
+    """out[M, N] = x[M, K] @ (qweight[N, K] * scale[N, k // group_size]).T on the device."""
+    import torch
+
+    M, K = x.shape
+    N = qweight.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    st = _stream_handle(stream)
+    _check(popcornDequantizeMatmulGrouped_i8f32(out.data_ptr(), x.data_ptr(), qweight.data_ptr(), scale.data_ptr(),
+                                                M, N, K, group_size, st), "popcornDequantizeMatmulGrouped_i8f32")
+    return out
 
 
 def dequantize(qweight, scale, out=None, stream=None):

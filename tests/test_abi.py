@@ -48,6 +48,11 @@ def test_popcorn_h_keeps_the_reference_signatures():
         "const float* scale, int64_t B, int64_t M, int64_t N, int64_t K, cudaStream_t stream );",
         "popcornStatus_t popcornQuantize_f32i8( int8_t* out, float* scale, const float* input, int64_t N, "
         "int64_t K, cudaStream_t stream );",
+        # include/popcorn.h:477-487, :538-546
+        "popcornStatus_t popcornDequantizeMatmulGrouped_i8f32( float* out, const float* x, const int8_t* qweight, "
+        "const float* scale, int64_t M, int64_t N, int64_t K, int64_t group_size, cudaStream_t stream );",
+        "popcornStatus_t popcornQuantizeGrouped_f32i8( int8_t* out, float* scale, const float* input, int64_t N, "
+        "int64_t K, int64_t group_size, cudaStream_t stream );",
     ]:
         assert proto in norm, proto
 
@@ -181,6 +186,25 @@ def test_allreduce_argument_checks(lib):
     # an all-reduce of M=1, N=16 over 2 ranks needs 16 * 2 * M * N bytes
     small = _group(recv_bytes=16 * 2 * 16 - 16)
     assert fn(ctypes.byref(small), *ok, 1, 16, 64, None) == pc.POPCORN_ERROR_INVALID_VALUE
+
+
+def test_grouped_conventions(lib):
+    # popcorn src/quantize.cu:190-202, :652-663: null -> invalid, sizes <= 0 ->
+    # success, then group_size <= 0 or not dividing K -> invalid.
+    mm = lib.popcornDequantizeMatmulGrouped_i8f32
+    qg = lib.popcornQuantizeGrouped_f32i8
+    for args in [(0, FAKE, FAKE, FAKE), (FAKE, 0, FAKE, FAKE), (FAKE, FAKE, 0, FAKE), (FAKE, FAKE, FAKE, 0)]:
+        assert mm(*args, 1, 1, 8, 4, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    for args in [(0, FAKE, FAKE), (FAKE, 0, FAKE), (FAKE, FAKE, 0)]:
+        assert qg(*args, 1, 8, 4, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    for (M, N, K) in [(0, 2, 8), (2, 0, 8), (2, 2, 0), (-1, 2, 8)]:
+        assert mm(FAKE, FAKE, FAKE, FAKE, M, N, K, 3, None) == pc.POPCORN_SUCCESS  # sizes first, as popcorn
+    assert qg(FAKE, FAKE, FAKE, 0, 8, 3, None) == pc.POPCORN_SUCCESS
+    assert qg(FAKE, FAKE, FAKE, 2, 0, 3, None) == pc.POPCORN_SUCCESS
+    for gs in (0, -4, 3, 16):  # K = 10: popcorn's invalid-group test uses K=10, group 4
+        assert mm(FAKE, FAKE, FAKE, FAKE, 2, 2, 10, gs, None) == pc.POPCORN_ERROR_INVALID_VALUE, gs
+        assert qg(FAKE, FAKE, FAKE, 2, 10, gs, None) == pc.POPCORN_ERROR_INVALID_VALUE, gs
+    assert mm(FAKE, FAKE, FAKE, FAKE, 2, 2, 10, 4, None) == pc.POPCORN_ERROR_INVALID_VALUE
 
 
 def test_batched_size_overflow_is_rejected(lib):
