@@ -42,6 +42,9 @@ WORKLOADS = {
     "decode": dict(M=1, K=4096, N=4096, unit="GB/s", bound="hbm"),
     "skinny": dict(M=32, K=4096, N=11008, unit="GB/s", bound="hbm"),
     "prefill": dict(M=2048, K=4096, N=4096, unit="TFLOP/s", bound="tensor"),
+    # Per-group int8 (popcornDequantizeMatmulGrouped_i8f32), decode size, group 128:
+    # algorithmic bytes = codes + group scales.
+    "grouped_decode": dict(M=1, K=4096, N=4096, unit="GB/s", bound="hbm", group_size=128),
 }
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of
@@ -61,7 +64,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
-    p.add_argument("--extras", default="skinny,prefill",
+    p.add_argument("--extras", default="skinny,prefill,grouped_decode",
                    help="comma-separated extra single-GPU workloads reported beside the headline (N=1 only)")
     p.add_argument("--stack", default="1,128",
                    help="M values of the 32-layer 7B-shaped linear stack timed at every N ('none' to skip)")
@@ -182,6 +185,7 @@ class Setup:
         self.M, self.K, self.N = M, K, N
         self.Nl = N // world
         self.world = world
+        self.gs = wl.get("group_size")
         per_set = self.Nl * K + (M * K * 4 if wl["bound"] == "tensor" else 0)
         self.sets = max(2, math.ceil(pool_bytes / per_set))
         if wl["bound"] == "tensor":
@@ -192,7 +196,7 @@ class Setup:
         for i in range(self.sets):
             # W ~ N(0, 0.02) f32 quantized per row by this library's quantizer.
             w = torch.randn((self.Nl, K), generator=g, device=device) * 0.02
-            q, s = pc.quantize(w)
+            q, s = pc.quantize_grouped(w, self.gs) if self.gs else pc.quantize(w)
             del w
             self.q.append(q)
             self.s.append(s)
@@ -223,20 +227,27 @@ class Setup:
             if st != 0:
                 raise RuntimeError(f"popcornDequantizeMatmulAllGather_i8f32 failed: {st}")
             return
-        st = self.lib.popcornDequantizeMatmul_i8f32(self.out[j].data_ptr(), x.data_ptr(), self.q[j].data_ptr(),
-                                                    self.s[j].data_ptr(), self.M, self.Nl, self.K, stream_handle)
+        if self.gs:
+            st = self.lib.popcornDequantizeMatmulGrouped_i8f32(self.out[j].data_ptr(), x.data_ptr(),
+                                                               self.q[j].data_ptr(), self.s[j].data_ptr(), self.M,
+                                                               self.Nl, self.K, self.gs, stream_handle)
+        else:
+            st = self.lib.popcornDequantizeMatmul_i8f32(self.out[j].data_ptr(), x.data_ptr(), self.q[j].data_ptr(),
+                                                        self.s[j].data_ptr(), self.M, self.Nl, self.K, stream_handle)
         if st != 0:
-            raise RuntimeError(f"popcornDequantizeMatmul_i8f32 failed: {st} "
+            raise RuntimeError(f"dequant-matmul call failed: {st} "
                                f"{self.lib.popcornGetLastCudaErrorString().decode()}")
         if self.world > 1:
             self.torch.distributed.all_gather_into_tensor(self.gathered, self.out[j].view(-1), group=group)
 
     def launches_per_step(self):
-        if self.fused is not None:
+        if self.fused is not None or self.gs:
             return 1
         return self.pc.launch_count(self.x[0].data_ptr(), self.q[0].data_ptr(), self.M, self.Nl, self.K)
 
     def path(self):
+        if self.gs:
+            return f"grouped_f32 (group {self.gs})"
         return self.pc.PATH_NAMES[self.pc.select_path(self.x[0].data_ptr(), self.q[0].data_ptr(),
                                                       self.M, self.Nl, self.K)]
 
@@ -350,15 +361,21 @@ def max_over_ranks(torch, value, dist_on, device):
     return float(t.item())
 
 
+def weight_bytes(wl):
+    """Algorithmic bytes of one call: int8 codes, plus the scales of a grouped layout."""
+    gs = wl.get("group_size")
+    return wl["N"] * wl["K"] + (4 * wl["N"] * (wl["K"] // gs) if gs else 0)
+
+
 def throughput(wl, ms_per_step):
     if wl["unit"] == "GB/s":
-        return wl["N"] * wl["K"] / (ms_per_step * 1e-3) / 1e9
+        return weight_bytes(wl) / (ms_per_step * 1e-3) / 1e9
     return 2.0 * wl["M"] * wl["N"] * wl["K"] / (ms_per_step * 1e-3) / 1e12
 
 
 def roofline(wl, ms_per_launch, peaks, workload_name):
     if wl["bound"] == "hbm":
-        achieved = wl["N"] * wl["K"] / (ms_per_launch * 1e-3) / 1e9
+        achieved = weight_bytes(wl) / (ms_per_launch * 1e-3) / 1e9
         peak, unit = peaks["hbm"], "GB/s"
     else:
         achieved = 2.0 * wl["M"] * wl["N"] * wl["K"] / (ms_per_launch * 1e-3) / 1e12

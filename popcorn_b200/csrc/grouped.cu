@@ -101,8 +101,10 @@ grouped_seq_kernel(float* __restrict__ out, const float* __restrict__ x, const i
 
 // MT activation rows (<= 4), U 16-element K slices per thread, R weight rows
 // per block (one group of rows per block).
+// M = 1 with one slice per thread fits 64 registers: four blocks per SM, so a
+// decode-sized grid (N / 8 blocks) is resident in one wave.
 template <int MT, int U, int R>
-__global__ void __launch_bounds__(kGThreads, 2)
+__global__ void __launch_bounds__(kGThreads, (MT == 1 && U == 1) ? 4 : 2)
 grouped_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* __restrict__ q,
                   const float* __restrict__ scale, int64_t M, int64_t N, int64_t K, int64_t gs) {
     __shared__ float part[R * MT][kGWarps];
