@@ -45,6 +45,9 @@ WORKLOADS = {
     # Per-group int8 (popcornDequantizeMatmulGrouped_i8f32), decode size, group 128:
     # algorithmic bytes = codes + group scales.
     "grouped_decode": dict(M=1, K=4096, N=4096, unit="GB/s", bound="hbm", group_size=128),
+    # Int4 packed asymmetric (popcornDequantizeMatmulGrouped_i4f32), decode size,
+    # group 128: algorithmic bytes = packed codes + group scales and zero points.
+    "int4_decode": dict(M=1, K=4096, N=4096, unit="GB/s", bound="hbm", group_size=128, bits=4),
 }
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of
@@ -64,7 +67,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
-    p.add_argument("--extras", default="skinny,prefill,grouped_decode",
+    p.add_argument("--extras", default="skinny,prefill,grouped_decode,int4_decode",
                    help="comma-separated extra single-GPU workloads reported beside the headline (N=1 only)")
     p.add_argument("--stack", default="1,128",
                    help="M values of the 32-layer 7B-shaped linear stack timed at every N ('none' to skip)")
@@ -186,17 +189,23 @@ class Setup:
         self.Nl = N // world
         self.world = world
         self.gs = wl.get("group_size")
-        per_set = self.Nl * K + (M * K * 4 if wl["bound"] == "tensor" else 0)
+        self.bits = wl.get("bits", 8)
+        per_set = self.Nl * K * self.bits // 8 + (M * K * 4 if wl["bound"] == "tensor" else 0)
         self.sets = max(2, math.ceil(pool_bytes / per_set))
         if wl["bound"] == "tensor":
             self.sets = min(self.sets, 4)
         g = torch.Generator(device=device)
         g.manual_seed(1234 + rank)
-        self.q, self.s, self.x, self.out = [], [], [], []
+        self.q, self.s, self.z, self.x, self.out = [], [], [], [], []
         for i in range(self.sets):
-            # W ~ N(0, 0.02) f32 quantized per row by this library's quantizer.
+            # W ~ N(0, 0.02) f32 quantized (per row, per group or int4 per
+            # group) by this library's quantizer.
             w = torch.randn((self.Nl, K), generator=g, device=device) * 0.02
-            q, s = pc.quantize_grouped(w, self.gs) if self.gs else pc.quantize(w)
+            if self.bits == 4:
+                q, s, z = pc.quantize_grouped_i4(w, self.gs)
+                self.z.append(z)
+            else:
+                q, s = pc.quantize_grouped(w, self.gs) if self.gs else pc.quantize(w)
             del w
             self.q.append(q)
             self.s.append(s)
@@ -227,7 +236,12 @@ class Setup:
             if st != 0:
                 raise RuntimeError(f"popcornDequantizeMatmulAllGather_i8f32 failed: {st}")
             return
-        if self.gs:
+        if self.bits == 4:
+            st = self.lib.popcornDequantizeMatmulGrouped_i4f32(self.out[j].data_ptr(), x.data_ptr(),
+                                                               self.q[j].data_ptr(), self.s[j].data_ptr(),
+                                                               self.z[j].data_ptr(), self.M, self.Nl, self.K, self.gs,
+                                                               stream_handle)
+        elif self.gs:
             st = self.lib.popcornDequantizeMatmulGrouped_i8f32(self.out[j].data_ptr(), x.data_ptr(),
                                                                self.q[j].data_ptr(), self.s[j].data_ptr(), self.M,
                                                                self.Nl, self.K, self.gs, stream_handle)
@@ -246,6 +260,8 @@ class Setup:
         return self.pc.launch_count(self.x[0].data_ptr(), self.q[0].data_ptr(), self.M, self.Nl, self.K)
 
     def path(self):
+        if self.bits == 4:
+            return f"int4_f32 (group {self.gs})"
         if self.gs:
             return f"grouped_f32 (group {self.gs})"
         return self.pc.PATH_NAMES[self.pc.select_path(self.x[0].data_ptr(), self.q[0].data_ptr(),
@@ -362,9 +378,12 @@ def max_over_ranks(torch, value, dist_on, device):
 
 
 def weight_bytes(wl):
-    """Algorithmic bytes of one call: int8 codes, plus the scales of a grouped layout."""
+    """Algorithmic bytes of one call: the codes (int8, or int4 packed two per
+    byte), plus the scales (and int4 zero points) of a grouped layout."""
     gs = wl.get("group_size")
-    return wl["N"] * wl["K"] + (4 * wl["N"] * (wl["K"] // gs) if gs else 0)
+    bits = wl.get("bits", 8)
+    params = (4 if bits == 8 else 8) * wl["N"] * (wl["K"] // gs) if gs else 0
+    return wl["N"] * wl["K"] * bits // 8 + params
 
 
 def throughput(wl, ms_per_step):

@@ -159,6 +159,62 @@ popcornStatus_t popcornQuantizeGrouped_f32i8(
     cudaStream_t stream
 );
 
+/*
+ * Int4 per-group asymmetric dequant-matmul:
+ *   out[m, n] = sum_k x[m, k] * ((c(n, k) - zero[n, g]) * scale[n, g]),
+ *   g = k / group_size,
+ * where qweight is row-major [N, K/2] bytes holding two 4-bit codes each, the
+ * even k in the low nibble: c(n, k) = qweight[n, k/2] & 0xF for even k and
+ * qweight[n, k/2] >> 4 for odd k. scale and zero are row-major
+ * [N, K / group_size]. group_size must be positive and divide K, and K must
+ * be even (else POPCORN_ERROR_INVALID_VALUE, checked in that order after the
+ * null pointers and the size <= 0 no-op, as popcorn does).
+ *
+ * Replaces popcorn's popcornDequantizeMatmulGrouped_i4f32
+ * (include/popcorn.h:503-517, src/quantize.cu:329-446). f32 arithmetic:
+ * small problems, group sizes that are not a multiple of 16 and unaligned
+ * operands follow popcorn's own operation order (bit-identical to its
+ * kernel); otherwise each 16-column slice applies its group's zero point and
+ * scale once, within f32 rounding of popcorn's result.
+ */
+popcornStatus_t popcornDequantizeMatmulGrouped_i4f32(
+    float* out,
+    const float* x,
+    const uint8_t* qweight,
+    const float* scale,
+    const float* zero,
+    int64_t M,
+    int64_t N,
+    int64_t K,
+    int64_t group_size,
+    cudaStream_t stream
+);
+
+/*
+ * Int4 per-group asymmetric quantization of a row-major [N, K] f32 matrix:
+ *   scale[n, g] = (max - min) / 15 over the group (1.0 when that is 0)
+ *   zero[n, g]  = -min / scale[n, g]
+ *   code        = rint(input / scale + zero) clamped to [0, 15]
+ * with min and max skipping NaN; codes are packed two per byte into out
+ * [N, K/2], the even k in the low nibble. Argument checks as for the int4
+ * matmul above.
+ *
+ * Replaces popcorn's popcornQuantizeGrouped_f32i4 (include/popcorn.h:548-562,
+ * src/quantize.cu:699-888): packed codes, scales and zero points
+ * bit-identical to its kernels, no temporary allocation, no device
+ * synchronization.
+ */
+popcornStatus_t popcornQuantizeGrouped_f32i4(
+    uint8_t* out,
+    float* scale,
+    float* zero,
+    const float* input,
+    int64_t N,
+    int64_t K,
+    int64_t group_size,
+    cudaStream_t stream
+);
+
 #ifdef __cplusplus
 }
 #endif

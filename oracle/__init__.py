@@ -4,8 +4,9 @@ Only the tests, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
 ``bench.py`` import this package, and only as the checker or the timed CPU
 baseline. The product path (``popcorn_b200``) never imports it.
 
-* :func:`dequant_matmul`, :func:`quantize`, :func:`dequantize` and
-  :func:`fill_normal` wrap ``liboracle.so`` (oracle.c, the C restatement).
+* :func:`dequant_matmul`, :func:`quantize`, their per-group int8 and int4
+  forms, :func:`dequantize` and :func:`fill_normal` wrap ``liboracle.so``
+  (oracle.c, the C restatement).
 * :func:`ref_loops` loads ``_ref/libref_loops.so``: popcorn's own test-side
   CPU loops (test/test_quantize.cu:24-41, :677-706) compiled from the
   reference sources; it pins the restatement and is the "reference" CPU
@@ -47,9 +48,12 @@ def _load():
         lib.oracle_fill_normal.argtypes = [_vp, _i64, ctypes.c_uint64, ctypes.c_float]
         lib.oracle_dequant_matmul_grouped_i8.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int]
         lib.oracle_quantize_grouped_i8.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _int]
+        lib.oracle_dequant_matmul_grouped_i4.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int]
+        lib.oracle_quantize_grouped_i4.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int]
         for f in (lib.oracle_dequant_matmul_i8, lib.oracle_dequant_matmul_i8_mt, lib.oracle_quantize_i8,
                   lib.oracle_dequantize_i8, lib.oracle_fill_normal, lib.oracle_dequant_matmul_grouped_i8,
-                  lib.oracle_quantize_grouped_i8):
+                  lib.oracle_quantize_grouped_i8, lib.oracle_dequant_matmul_grouped_i4,
+                  lib.oracle_quantize_grouped_i4):
             f.restype = None
         _lib = lib
     return _lib
@@ -117,6 +121,41 @@ def quantize_grouped(w, group_size: int, ties_away: bool = False):
     return q, s
 
 
+def dequant_matmul_grouped_i4(x, q, scale, zero, group_size: int, fused: bool = False,
+                              threads: int = 1) -> np.ndarray:
+    """out[M,N] = sum_k x[m,k] * ((nibble(q, n, k) - zero[n,g]) * scale[n,g]), g = k // group_size,
+    popcorn's k order; q is [N, K/2] uint8, low nibble first."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    q = np.ascontiguousarray(q, dtype=np.uint8)
+    scale = np.ascontiguousarray(scale, dtype=np.float32)
+    zero = np.ascontiguousarray(zero, dtype=np.float32)
+    M, K = x.shape
+    N = q.shape[0]
+    assert K % 2 == 0 and K % group_size == 0 and q.shape == (N, K // 2)
+    assert scale.size == N * (K // group_size) and zero.size == scale.size
+    out = np.empty((M, N), dtype=np.float32)
+    _load().oracle_dequant_matmul_grouped_i4(_ptr(out), _ptr(x), _ptr(q), _ptr(scale), _ptr(zero), M, N, K,
+                                             group_size, int(fused), threads)
+    return out
+
+
+def quantize_grouped_i4(w, group_size: int, test_loop: bool = False):
+    """(packed uint8 [N, K/2], scale f32 [N, K/gs], zero f32 [N, K/gs]).
+
+    Default: popcorn's GPU kernels (rintf, NaN-skipping min/max in its block
+    order); ``test_loop``: popcorn's CPU test loop (roundf, first-value start,
+    even group sizes only)."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    N, K = w.shape
+    assert K % 2 == 0 and K % group_size == 0
+    assert not test_loop or group_size % 2 == 0
+    q = np.empty((N, K // 2), dtype=np.uint8)
+    s = np.empty((N, K // group_size), dtype=np.float32)
+    z = np.empty((N, K // group_size), dtype=np.float32)
+    _load().oracle_quantize_grouped_i4(_ptr(q), _ptr(s), _ptr(z), _ptr(w), N, K, group_size, int(test_loop))
+    return q, s, z
+
+
 def dequantize(q, scale) -> np.ndarray:
     q = np.ascontiguousarray(q, dtype=np.int8)
     scale = np.ascontiguousarray(scale, dtype=np.float32)
@@ -154,8 +193,11 @@ def ref_loops():
         lib.ref_loops_quantize_i8.argtypes = [_vp, _vp, _vp, _i64, _i64]
         lib.ref_loops_dequant_matmul_grouped_i8.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64]
         lib.ref_loops_quantize_grouped_i8.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64]
+        lib.ref_loops_dequant_matmul_grouped_i4.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64]
+        lib.ref_loops_quantize_grouped_i4.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64]
         for f in (lib.ref_loops_dequant_matmul_i8, lib.ref_loops_dequant_matmul_i8_mt, lib.ref_loops_quantize_i8,
-                  lib.ref_loops_dequant_matmul_grouped_i8, lib.ref_loops_quantize_grouped_i8):
+                  lib.ref_loops_dequant_matmul_grouped_i8, lib.ref_loops_quantize_grouped_i8,
+                  lib.ref_loops_dequant_matmul_grouped_i4, lib.ref_loops_quantize_grouped_i4):
             f.restype = None
         _ref_loops = lib
     return _ref_loops
@@ -204,6 +246,29 @@ def ref_quantize_grouped(w, group_size: int):
     return q, s
 
 
+def ref_dequant_matmul_grouped_i4(x, q, scale, zero, group_size: int) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    q = np.ascontiguousarray(q, dtype=np.uint8)
+    scale = np.ascontiguousarray(scale, dtype=np.float32)
+    zero = np.ascontiguousarray(zero, dtype=np.float32)
+    M, K = x.shape
+    N = q.shape[0]
+    out = np.empty((M, N), dtype=np.float32)
+    ref_loops().ref_loops_dequant_matmul_grouped_i4(_ptr(out), _ptr(x), _ptr(q), _ptr(scale), _ptr(zero), M, N, K,
+                                                    group_size)
+    return out
+
+
+def ref_quantize_grouped_i4(w, group_size: int):
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    N, K = w.shape
+    q = np.empty((N, K // 2), dtype=np.uint8)
+    s = np.empty((N, K // group_size), dtype=np.float32)
+    z = np.empty((N, K // group_size), dtype=np.float32)
+    ref_loops().ref_loops_quantize_grouped_i4(_ptr(q), _ptr(s), _ptr(z), _ptr(w), N, K, group_size)
+    return q, s, z
+
+
 def have_popcorn_ref_gpu() -> bool:
     return os.path.exists(REF_GPU_LIB)
 
@@ -223,5 +288,9 @@ def popcorn_ref_gpu():
         lib.popcornDequantizeMatmulGrouped_i8f32.restype = _int
         lib.popcornQuantizeGrouped_f32i8.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _vp]
         lib.popcornQuantizeGrouped_f32i8.restype = _int
+        lib.popcornDequantizeMatmulGrouped_i4f32.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]
+        lib.popcornDequantizeMatmulGrouped_i4f32.restype = _int
+        lib.popcornQuantizeGrouped_f32i4.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]
+        lib.popcornQuantizeGrouped_f32i4.restype = _int
         _ref_gpu = lib
     return _ref_gpu

@@ -213,6 +213,144 @@ void oracle_quantize_grouped_i8(int8_t* out, float* scale, const float* in, int6
     }
 }
 
+typedef struct {
+    float* out;
+    const float* x;
+    const uint8_t* q;
+    const float* scale;
+    const float* zero;
+    int64_t M, N, K, gs, n0, n1;
+    int fused;
+} i4mm_job;
+
+static void* i4mm_worker(void* arg) {
+    /* popcorn test/test_quantize.cu:80-96 and src/quantize.cu:374-395: for
+     * each output, walk k upward; take the nibble of byte k/2 (low for even
+     * k), subtract the group's zero point, multiply by its scale, then the
+     * multiply-add with the activation. */
+    const i4mm_job* j = (const i4mm_job*)arg;
+    const int64_t groups = j->K / j->gs;
+    const int64_t row_bytes = j->K / 2;
+    for (int64_t m = 0; m < j->M; m++) {
+        const float* xr = j->x + m * j->K;
+        for (int64_t n = j->n0; n < j->n1; n++) {
+            const uint8_t* qr = j->q + n * row_bytes;
+            const float* sr = j->scale + n * groups;
+            const float* zr = j->zero + n * groups;
+            float acc = 0.0f;
+            for (int64_t k = 0; k < j->K; k++) {
+                const uint8_t b = qr[k / 2];
+                const int nib = (k % 2 == 0) ? (b & 0x0F) : (b >> 4);
+                const int64_t g = k / j->gs;
+                const float d = (float)nib - zr[g];
+                const float w = d * sr[g];
+                if (j->fused) {
+                    acc = fmaf(xr[k], w, acc);
+                } else {
+                    const float p = xr[k] * w;
+                    acc = acc + p;
+                }
+            }
+            j->out[m * j->N + n] = acc;
+        }
+    }
+    return NULL;
+}
+
+void oracle_dequant_matmul_grouped_i4(float* out, const float* x, const uint8_t* q, const float* scale,
+                                      const float* zero, int64_t M, int64_t N, int64_t K, int64_t gs, int fused,
+                                      int threads) {
+    if (threads < 1) threads = 1;
+    if (threads > N) threads = (int)N;
+    if (threads < 1) return;
+    pthread_t* tid = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)threads);
+    i4mm_job* jobs = (i4mm_job*)malloc(sizeof(i4mm_job) * (size_t)threads);
+    for (int t = 0; t < threads; t++) {
+        i4mm_job j = {out, x, q, scale, zero, M, N, K, gs, N * t / threads, N * (t + 1) / threads, fused};
+        jobs[t] = j;
+        if (threads > 1) pthread_create(&tid[t], NULL, i4mm_worker, &jobs[t]);
+    }
+    if (threads > 1) {
+        for (int t = 0; t < threads; t++) pthread_join(tid[t], NULL);
+    } else {
+        i4mm_worker(&jobs[0]);
+    }
+    free(jobs);
+    free(tid);
+}
+
+/* Group min and max as popcorn's min/max kernel forms them
+ * (src/quantize.cu:705-750): a block of 256 threads, thread t scanning
+ * elements t, t + 256, ... from +inf / -inf with strict compares (NaN never
+ * wins), then a halving tree in which the lower-numbered partner is kept on
+ * a tie. Values that compare equal have the same bits except +0 and -0, so
+ * the order only decides the sign of a zero min or max. */
+static void i4_group_minmax_kernel_order(const float* r, int64_t gs, float* mn_out, float* mx_out) {
+    float mn[256], mx[256];
+    for (int t = 0; t < 256; t++) {
+        float a = INFINITY, b = -INFINITY;
+        for (int64_t i = t; i < gs; i += 256) {
+            const float v = r[i];
+            if (v < a) a = v;
+            if (v > b) b = v;
+        }
+        mn[t] = a;
+        mx[t] = b;
+    }
+    for (int s = 128; s > 0; s >>= 1) {
+        for (int t = 0; t < s; t++) {
+            if (mn[t + s] < mn[t]) mn[t] = mn[t + s];
+            if (mx[t + s] > mx[t]) mx[t] = mx[t + s];
+        }
+    }
+    *mn_out = mn[0];
+    *mx_out = mx[0];
+}
+
+static uint8_t i4_code(float v, float sc, float zp, int ties) {
+    const float d = v / sc + zp;
+    float qv = ties ? roundf(d) : rintf(d);
+    if (qv < 0.0f) qv = 0.0f;
+    if (qv > 15.0f) qv = 15.0f;
+    return (qv != qv) ? (uint8_t)0 : (uint8_t)qv;  /* NaN -> 0 as the GPU converts it */
+}
+
+void oracle_quantize_grouped_i4(uint8_t* out, float* scale, float* zero, const float* in, int64_t N, int64_t K,
+                                int64_t gs, int variant) {
+    const int64_t groups = K / gs;
+    for (int64_t n = 0; n < N; n++) {
+        for (int64_t g = 0; g < groups; g++) {
+            const float* r = in + n * K + g * gs;
+            float mn, mx;
+            if (variant == 0) {
+                i4_group_minmax_kernel_order(r, gs, &mn, &mx);
+            } else {
+                /* test/test_quantize.cu:761-767: start at the first value. */
+                mn = r[0];
+                mx = r[0];
+                for (int64_t i = 1; i < gs; i++) {
+                    if (r[i] < mn) mn = r[i];
+                    if (r[i] > mx) mx = r[i];
+                }
+            }
+            const float range = mx - mn;
+            float sc = range / 15.0f;
+            if (sc == 0.0f) sc = 1.0f;
+            scale[n * groups + g] = sc;
+            zero[n * groups + g] = -mn / sc;
+        }
+        /* Codes: element k uses the parameters of its own group (a byte of an
+         * odd group size straddles two groups; popcorn's apply kernel,
+         * src/quantize.cu:772-823, computes each nibble with its own group). */
+        for (int64_t k = 0; k < K; k += 2) {
+            const int64_t glo = n * groups + k / gs, ghi = n * groups + (k + 1) / gs;
+            const uint8_t lo = i4_code(in[n * K + k], scale[glo], zero[glo], variant);
+            const uint8_t hi = i4_code(in[n * K + k + 1], scale[ghi], zero[ghi], variant);
+            out[n * (K / 2) + k / 2] = (uint8_t)((hi << 4) | lo);
+        }
+    }
+}
+
 void oracle_dequantize_i8(float* out, const int8_t* q, const float* scale, int64_t N, int64_t K) {
     for (int64_t n = 0; n < N; n++) {
         const float sc = scale[n];

@@ -49,6 +49,29 @@ void oracle_dequant_matmul_grouped_i8(float* out, const float* x, const int8_t* 
 void oracle_quantize_grouped_i8(int8_t* out, float* scale, const float* in, int64_t N, int64_t K, int64_t gs,
                                 int ties);
 
+/* Int4 packed asymmetric per-group dequant-matmul (src/quantize.cu:335-405,
+ * test/test_quantize.cu:67-99): q is [N, K/2] bytes; element k of row n is
+ * the low nibble of byte k/2 for even k, the high nibble for odd k; its
+ * weight is ((float)nibble - zero[n, k/gs]) * scale[n, k/gs] (subtract, then
+ * multiply, each rounded); k ascending; `fused` as above; split over
+ * `threads` by channel. scale and zero are [N, K/gs]. */
+void oracle_dequant_matmul_grouped_i4(float* out, const float* x, const uint8_t* q, const float* scale,
+                                      const float* zero, int64_t M, int64_t N, int64_t K, int64_t gs, int fused,
+                                      int threads);
+
+/* Int4 asymmetric per-group quantization: per group min and max, then
+ * scale = (max - min) / 15 (1 if 0), zero = -min / scale, and codes
+ * clamp(round(v / scale + zero), 0, 15) packed two per byte, low nibble first.
+ * variant 0: popcorn's GPU kernels (src/quantize.cu:705-827): min/max start
+ *            at +inf/-inf and skip NaN, reduced the way its 256-thread block
+ *            does (which fixes the sign of a zero min or max), codes by rintf
+ *            (half to even), a NaN code packs as 0; any even K and any gs;
+ * variant 1: popcorn's test loop (test/test_quantize.cu:747-789): min/max
+ *            start at the group's first value, scanned in order, codes by
+ *            roundf (half away from zero); even gs only. */
+void oracle_quantize_grouped_i4(uint8_t* out, float* scale, float* zero, const float* in, int64_t N, int64_t K,
+                                int64_t gs, int variant);
+
 /* out[n,k] = (float)q[n,k] * scale[n]. */
 void oracle_dequantize_i8(float* out, const int8_t* q, const float* scale, int64_t N, int64_t K);
 

@@ -43,6 +43,8 @@ ABI_SYMBOLS = (
     "popcornQuantize_f32i8",
     "popcornDequantizeMatmulGrouped_i8f32",
     "popcornQuantizeGrouped_f32i8",
+    "popcornDequantizeMatmulGrouped_i4f32",
+    "popcornQuantizeGrouped_f32i4",
 )
 EXT_SYMBOLS = (
     "popcornDequantize_i8f32",
@@ -82,6 +84,8 @@ _SIGNATURES = {
     "popcornQuantize_f32i8": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "popcornDequantizeMatmulGrouped_i8f32": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "popcornQuantizeGrouped_f32i8": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "popcornDequantizeMatmulGrouped_i4f32": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "popcornQuantizeGrouped_f32i4": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "popcornDequantize_i8f32": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "popcornDequantizeMatmulPath_i8f32": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "popcornDequantizeMatmulSelectPath": (_int, [_vp, _vp, _i64, _i64, _i64]),
@@ -158,6 +162,15 @@ def popcornDequantizeMatmulGrouped_i8f32(out, x, qweight, scale, M, N, K, group_
 
 def popcornQuantizeGrouped_f32i8(out, scale, inp, N, K, group_size, stream=0) -> int:
     return load_library().popcornQuantizeGrouped_f32i8(out, scale, inp, N, K, group_size, stream)
+
+
+def popcornDequantizeMatmulGrouped_i4f32(out, x, qweight, scale, zero, M, N, K, group_size, stream=0) -> int:
+    return load_library().popcornDequantizeMatmulGrouped_i4f32(out, x, qweight, scale, zero, M, N, K, group_size,
+                                                               stream)
+
+
+def popcornQuantizeGrouped_f32i4(out, scale, zero, inp, N, K, group_size, stream=0) -> int:
+    return load_library().popcornQuantizeGrouped_f32i4(out, scale, zero, inp, N, K, group_size, stream)
 
 
 def popcornDequantize_i8f32(out, qweight, scale, N, K, stream=0) -> int:
@@ -273,6 +286,40 @@ def dequantize_matmul_grouped(x, qweight, scale, group_size: int, out=None, stre
     st = _stream_handle(stream)
     _check(popcornDequantizeMatmulGrouped_i8f32(out.data_ptr(), x.data_ptr(), qweight.data_ptr(), scale.data_ptr(),
                                                 M, N, K, group_size, st), "popcornDequantizeMatmulGrouped_i8f32")
+    return out
+
+
+def quantize_grouped_i4(w, group_size: int, out=None, scale=None, zero=None, stream=None):
+    """Per-group asymmetric int4 quantization of f32 [N, K] ->
+    (packed codes uint8 [N, K / 2] low nibble first, scales and zero points [N, K / group_size])."""
+    import torch
+
+    N, K = w.shape
+    G = K // group_size if group_size > 0 else 0
+    if out is None:
+        out = torch.empty((N, K // 2), dtype=torch.uint8, device=w.device)
+    if scale is None:
+        scale = torch.empty((N, G), dtype=torch.float32, device=w.device)
+    if zero is None:
+        zero = torch.empty((N, G), dtype=torch.float32, device=w.device)
+    st = _stream_handle(stream)
+    _check(popcornQuantizeGrouped_f32i4(out.data_ptr(), scale.data_ptr(), zero.data_ptr(), w.data_ptr(), N, K,
+                                        group_size, st), "popcornQuantizeGrouped_f32i4")
+    return out, scale, zero
+
+
+def dequantize_matmul_grouped_i4(x, qweight, scale, zero, group_size: int, out=None, stream=None):
+    """out[M, N] = x[M, K] @ ((codes(qweight)[N, K] - zero[N, g]) * scale[N, g]).T, g = k // group_size."""
+    import torch
+
+    M, K = x.shape
+    N = qweight.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    st = _stream_handle(stream)
+    _check(popcornDequantizeMatmulGrouped_i4f32(out.data_ptr(), x.data_ptr(), qweight.data_ptr(), scale.data_ptr(),
+                                                zero.data_ptr(), M, N, K, group_size, st),
+           "popcornDequantizeMatmulGrouped_i4f32")
     return out
 
 

@@ -50,6 +50,48 @@ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // Streaming-multiprocessor count of the current device (cached per device).
 int device_sm_count();
 
+#ifdef __CUDACC__
+// L2 prefetch hint for [p, p + bytes): the range is shrunk to 16-byte
+// boundaries (the bulk prefetch's alignment; nothing outside the range is
+// named) and split into `parts` pieces, of which the caller issues `part`.
+__device__ __forceinline__ void prefetch_l2_range(const void* p, int64_t bytes, int part, int parts) {
+    const uint64_t a = reinterpret_cast<uint64_t>(p);
+    const uint64_t lo = (a + 15u) & ~uint64_t{15};
+    const uint64_t hi = (a + static_cast<uint64_t>(bytes)) & ~uint64_t{15};
+    if (hi <= lo) return;
+    const uint64_t n = hi - lo;
+    const uint64_t chunk = ((n + parts - 1) / parts + 15u) & ~uint64_t{15};
+    const uint64_t c0 = static_cast<uint64_t>(part) * chunk;
+    if (c0 >= n) return;
+    const uint64_t c1 = (c0 + chunk < n) ? c0 + chunk : n;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(lo + c0), "r"(static_cast<uint32_t>(c1 - c0))
+                 : "memory");
+}
+
+// Programmatic dependent launch, kernel side: let the next kernel of the
+// stream begin launching now, and wait for the previous kernel's writes.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+#endif
+
+// Host side: a launch configuration that allows programmatic dependent
+// launch on `stream` (attr must outlive the launch call).
+inline cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                     cudaLaunchAttribute* attr) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cfg;
+}
+
 // ---------------------------------------------------------------------------
 // Kernel-path entry points (implemented in gemv.cu / tc_gemm.cu).
 // Each takes already validated arguments (non-null, all sizes > 0).

@@ -115,6 +115,20 @@ grouped_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const in
     const int64_t groups = K / gs;
     const int64_t r0 = static_cast<int64_t>(blockIdx.x) * R;
 
+    // Programmatic dependent launch: release the next kernel of the stream,
+    // pull this block's weight rows and scales into L2 while the previous
+    // kernel finishes (a hint; every real read follows the wait).
+    pdl_launch_dependents();
+    if (tid < kGWarps + 1 && blockIdx.y == 0) {
+        const int64_t rows = (r0 + R <= N) ? R : N - r0;
+        if (tid < kGWarps) {
+            prefetch_l2_range(q + r0 * K, rows * K, tid, kGWarps);
+        } else {
+            prefetch_l2_range(scale + r0 * groups, rows * groups * 4, 0, 1);
+        }
+    }
+    pdl_wait();
+
     // Weight rows of this block (independent of x: requested first), and the
     // group of each of this thread's slices (group_size is a multiple of 16).
     uint4 w[R][U];
@@ -232,8 +246,11 @@ popcornStatus_t launch_grouped_xs(float* out, const float* x, const int8_t* q, c
                                   int64_t N, int64_t K, int64_t gs, cudaStream_t stream) {
     const int64_t gx = ceil_div(N, R);
     const int64_t gy = ceil_div(M, MT);
-    grouped_xs_kernel<MT, U, R><<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)), kGThreads, 0, stream>>>(
-        out, x, q, scale, M, N, K, gs);
+    cudaLaunchAttribute attr[1];
+    const cudaLaunchConfig_t cfg = pdl_config(dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)),
+                                              dim3(kGThreads), 0, stream, attr);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, grouped_xs_kernel<MT, U, R>, out, x, q, scale, M, N, K, gs);
+    if (e != cudaSuccess) return record_cuda(e);
     return check_launch();
 }
 

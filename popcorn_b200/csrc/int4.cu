@@ -1,0 +1,501 @@
+// Int4 packed asymmetric per-group: popcornDequantizeMatmulGrouped_i4f32 and
+// popcornQuantizeGrouped_f32i4 (popcorn src/quantize.cu:329-446, :699-888).
+//
+// Format (popcorn): qweight is [N, K/2] bytes, two 4-bit codes per byte, the
+// even k in the low nibble; scale and zero are [N, K/group_size] f32; the
+// weight of (n, k) is (code - zero[n, g]) * scale[n, g], g = k / group_size.
+// Quantization: per group min and max (NaN skipped), scale = (max - min) / 15
+// (1 when 0), zero = -min / scale, code = clamp(rint(v / scale + zero), 0, 15).
+//
+// Kernels:
+//  * i4_seq_kernel -- one thread per output walking k upward with
+//    w = (code - zero) * scale and acc = fma(x, w, acc): popcorn's operation
+//    sequence, bit-identical to its kernel. Used for small problems, group
+//    sizes that are not a multiple of 16 and unaligned operands.
+//  * i4_xs_kernel<MT, U, R> -- x-stationary decode layout: each thread keeps
+//    U 16-element slices of x in registers and reads the matching 8 bytes of
+//    R weight rows per slice. A slice lies inside one group, so the zero
+//    point leaves the inner loop:
+//        sum_k x_k (c_k - z) s = s * (sum_k x_k (c_k - 8) - (z - 8) sum_k x_k)
+//    with c_k - 8 exact in f32 (centred codes keep the two terms small). The
+//    codes become floats without a conversion instruction: a nibble placed in
+//    the low mantissa bits of 2^23 reads as 2^23 + c; the high nibble is taken
+//    in place (2^23 + 16 c) and its activation pre-scaled by 1/16, exactly.
+//  * i4_quantize_kernel -- one warp per (row, group): min and max by shuffles,
+//    ties between +0 and -0 broken the way popcorn's 256-thread block breaks
+//    them, then (even group sizes) the packed codes of the group;
+//    i4_pack_kernel packs bytes that straddle two groups (odd group sizes)
+//    from the stored parameters. Codes, scales and zero points are
+//    bit-identical to popcorn's kernels; no temporary buffer.
+#include "common.cuh"
+
+namespace pcb {
+namespace {
+
+constexpr int kI4Threads = 256;
+constexpr int kI4Warps = kI4Threads / 32;
+
+// Butterfly reduce-scatter of V values over a warp: afterwards the lanes with
+// (lane % (32 / V)) == 0 hold the warp total of value lane / (32 / V).
+template <int V>
+__device__ __forceinline__ float i4_reduce_scatter(float (&v)[V], int lane) {
+    int cnt = V;
+    #pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        if (cnt > 1) {
+            const int half = cnt >> 1;
+            const bool up = (lane & off) != 0;
+            #pragma unroll
+            for (int i = 0; i < V / 2; ++i) {
+                if (i < half) {
+                    const float send = up ? v[i] : v[i + half];
+                    const float keep = up ? v[i + half] : v[i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+                }
+            }
+            cnt = half;
+        } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+        }
+    }
+    return v[0];
+}
+
+__global__ void __launch_bounds__(256)
+i4_seq_kernel(float* __restrict__ out, const float* __restrict__ x, const uint8_t* __restrict__ q,
+              const float* __restrict__ scale, const float* __restrict__ zero, int64_t M, int64_t N, int64_t K,
+              int64_t gs) {
+    const int64_t groups = K / gs;
+    const int64_t row_bytes = K >> 1;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < M * N; t += stride) {
+        const int64_t n = t % N;
+        const int64_t m = t / N;
+        const float* xr = x + m * K;
+        const uint8_t* qr = q + n * row_bytes;
+        const float* sr = scale + n * groups;
+        const float* zr = zero + n * groups;
+        float acc = 0.0f;
+        int64_t k = 0;
+        for (int64_t g = 0; g < groups; ++g) {  // group by group: k / gs without a division
+            const float sc = __ldg(sr + g);
+            const float zp = __ldg(zr + g);
+            for (const int64_t end = k + gs; k < end; ++k) {
+                const uint32_t b = __ldg(qr + (k >> 1));
+                const uint32_t code = (k & 1) ? (b >> 4) : (b & 0x0Fu);
+                const float w = __fmul_rn(__fsub_rn(static_cast<float>(code), zp), sc);
+                acc = __fmaf_rn(__ldg(xr + k), w, acc);
+            }
+        }
+        out[t] = acc;
+    }
+}
+
+// Eight codes (one word, k = 0..7) -> four float2 pairs (c_2j - 8, 16 (c_2j+1 - 8)).
+__device__ __forceinline__ void widen8(uint32_t word, float2 (&c)[4]) {
+    const uint32_t lo = word & 0x0F0F0F0Fu;  // even k, in place
+    const uint32_t hi = word & 0xF0F0F0F0u;  // odd k, times 16
+    const float2 bias = make_float2(-8388616.0f, -8388736.0f);  // -(2^23 + 8), -(2^23 + 128)
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float2 f = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440 + j)),
+                                     __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440 + j)));
+        c[j] = __fadd2_rn(f, bias);
+    }
+}
+
+// MT activation rows (<= 4), U 16-element K slices per thread, R weight rows
+// per block; gridDim.y = ceil(M / MT).
+template <int MT, int U, int R>
+__global__ void __launch_bounds__(kI4Threads, (MT == 1 && U == 1) ? 4 : 2)
+i4_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const uint8_t* __restrict__ q,
+             const float* __restrict__ scale, const float* __restrict__ zero, int64_t M, int64_t N, int64_t K,
+             int64_t gs) {
+    __shared__ float part[R * MT][kI4Warps];
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int64_t units = K >> 4;
+    const int64_t groups = K / gs;
+    const int64_t row_bytes = K >> 1;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * R;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * MT;
+
+    // Programmatic dependent launch: release the next kernel of the stream,
+    // pull this block's weight rows and group parameters into L2 while the
+    // previous kernel finishes (a hint; every real read follows the wait).
+    pdl_launch_dependents();
+    if (tid < kI4Warps + 2 && blockIdx.y == 0) {
+        const int64_t rows = (r0 + R <= N) ? R : N - r0;
+        if (tid < kI4Warps) {
+            prefetch_l2_range(q + r0 * row_bytes, rows * row_bytes, tid, kI4Warps);
+        } else {
+            prefetch_l2_range((tid == kI4Warps ? scale : zero) + r0 * groups, rows * groups * 4, 0, 1);
+        }
+    }
+    pdl_wait();
+
+    // Weight bytes of this block first (independent of x), then the group
+    // parameters, all requested before any of them is needed.
+    uint2 w[R][U];
+    float sc[R][U], zc[R][U];
+    const int units_per_group = static_cast<int>(gs >> 4);
+    #pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int unit = tid + u * kI4Threads;
+        #pragma unroll
+        for (int r = 0; r < R; ++r) {
+            w[r][u] = (r0 + r < N && unit < units)
+                          ? __ldg(reinterpret_cast<const uint2*>(q + (r0 + r) * row_bytes) + unit)
+                          : make_uint2(0u, 0u);
+        }
+    }
+    #pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int unit = tid + u * kI4Threads;
+        const int g = unit / units_per_group;
+        #pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const bool ok = r0 + r < N && unit < units;
+            sc[r][u] = ok ? __ldg(scale + (r0 + r) * groups + g) : 0.0f;
+            zc[r][u] = ok ? __ldg(zero + (r0 + r) * groups + g) - 8.0f : 0.0f;
+        }
+    }
+
+    // Activations of this thread's slices, as loaded.
+    float4 xr[MT][U][4];
+    #pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        #pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t unit = tid + static_cast<int64_t>(u) * kI4Threads;
+            #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                xr[m][u][c] = (unit < units && m0 + m < M)
+                                  ? __ldg(reinterpret_cast<const float4*>(x + (m0 + m) * K + unit * 16) + c)
+                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+        }
+    }
+
+    float acc[R * MT];
+    #pragma unroll
+    for (int i = 0; i < R * MT; ++i) acc[i] = 0.0f;
+
+    // f32 layout: codes widened exactly, activations as pairs
+    // (x_2j, x_2j+1 / 16), packed multiply-adds.
+    auto dot_float = [&]() {
+        #pragma unroll
+        for (int u = 0; u < U; ++u) {
+            float2 xv[MT][8];
+            float xsum[MT];
+            #pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                float s = 0.0f;
+                #pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const float4 v = xr[m][u][c];
+                    s += (v.x + v.y) + (v.z + v.w);
+                    xv[m][2 * c] = make_float2(v.x, v.y * 0.0625f);
+                    xv[m][2 * c + 1] = make_float2(v.z, v.w * 0.0625f);
+                }
+                xsum[m] = s;
+            }
+            #pragma unroll
+            for (int r = 0; r < R; ++r) {
+                float2 a[MT];
+                #pragma unroll
+                for (int m = 0; m < MT; ++m) a[m] = make_float2(0.0f, 0.0f);
+                const uint32_t words[2] = {w[r][u].x, w[r][u].y};
+                #pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    float2 c[4];
+                    widen8(words[h], c);
+                    #pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        #pragma unroll
+                        for (int m = 0; m < MT; ++m) a[m] = __ffma2_rn(xv[m][4 * h + j], c[j], a[m]);
+                    }
+                }
+                #pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    const float d = fmaf(-zc[r][u], xsum[m], a[m].x + a[m].y);
+                    acc[r * MT + m] = fmaf(sc[r][u], d, acc[r * MT + m]);
+                }
+            }
+        }
+    };
+
+    if constexpr (MT == 1) {
+        // M = 1: the slice of x becomes 22-bit fixed point X (scaled by a
+        // power of two from the thread's max |x|), written as three bytes
+        // X = d2 * 2^16 + d1 * 2^8 + d0 (d0, d1 unsigned, d2 signed). The
+        // codes are bytes after one mask (even k) or a shift and a mask
+        // (odd k), so each dp4a multiplies four codes by four digits exactly:
+        // six dp4a finish eight codes. Per row and slice the int32 sum
+        // S = sum X c (|S| < 2^30) is exact; S - 8 sum X is rounded once to
+        // f32, the zero point enters as (z - 8) * sum X, and the power of two
+        // is undone exactly. A warp holding a non-finite x or a slice max
+        // outside [2^-90, 2^100] keeps the f32 layout.
+        uint32_t mb = 0;
+        #pragma unroll
+        for (int u = 0; u < U; ++u) {
+            #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float4 v = xr[0][u][c];
+                mb = max(mb, max(max(__float_as_uint(v.x) & 0x7FFFFFFFu, __float_as_uint(v.y) & 0x7FFFFFFFu),
+                                 max(__float_as_uint(v.z) & 0x7FFFFFFFu, __float_as_uint(v.w) & 0x7FFFFFFFu)));
+            }
+        }
+        const bool bad = mb != 0u && (mb < 0x12800000u || mb > 0x71800000u);
+        if (!__any_sync(0xffffffffu, bad)) {
+            float up = 1.0f, down = 1.0f;
+            if (mb != 0u) {
+                const int ex = 148 - static_cast<int>(mb >> 23);  // max |x| * 2^ex < 2^22
+                up = __int_as_float((ex + 127) << 23);
+                down = __int_as_float((127 - ex) << 23);
+            }
+            // digit[u][h][p][d]: digit d of the four activations that meet
+            // the even (p = 0) or odd (p = 1) codes of weight word h.
+            uint32_t digit[U][2][2][3];
+            int xs[U];
+            #pragma unroll
+            for (int u = 0; u < U; ++u) {
+                int xi[16];
+                #pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const float4 v = xr[0][u][c];
+                    xi[4 * c] = __float2int_rn(v.x * up);
+                    xi[4 * c + 1] = __float2int_rn(v.y * up);
+                    xi[4 * c + 2] = __float2int_rn(v.z * up);
+                    xi[4 * c + 3] = __float2int_rn(v.w * up);
+                }
+                int s = 0;
+                #pragma unroll
+                for (int e = 0; e < 16; ++e) s += xi[e];
+                xs[u] = s;
+                #pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    #pragma unroll
+                    for (int p = 0; p < 2; ++p) {
+                        const int e = 8 * h + p;
+                        const uint32_t a = xi[e], b = xi[e + 2], c = xi[e + 4], d = xi[e + 6];
+                        const uint32_t t01 = __byte_perm(a, b, 0x5140), t23 = __byte_perm(c, d, 0x5140);
+                        const uint32_t v01 = __byte_perm(a, b, 0x7362), v23 = __byte_perm(c, d, 0x7362);
+                        digit[u][h][p][0] = __byte_perm(t01, t23, 0x5410);
+                        digit[u][h][p][1] = __byte_perm(t01, t23, 0x7632);
+                        digit[u][h][p][2] = __byte_perm(v01, v23, 0x5410);
+                    }
+                }
+            }
+            #pragma unroll
+            for (int r = 0; r < R; ++r) {
+                float a = 0.0f;
+                #pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    unsigned s0 = 0u, s1 = 0u;
+                    int s2 = 0;
+                    const uint32_t words[2] = {w[r][u].x, w[r][u].y};
+                    #pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint32_t lo = words[h] & 0x0F0F0F0Fu;
+                        const uint32_t hi = (words[h] >> 4) & 0x0F0F0F0Fu;
+                        s0 = __dp4a(digit[u][h][0][0], lo, s0);
+                        s0 = __dp4a(digit[u][h][1][0], hi, s0);
+                        s1 = __dp4a(digit[u][h][0][1], lo, s1);
+                        s1 = __dp4a(digit[u][h][1][1], hi, s1);
+                        s2 = __dp4a(static_cast<int>(digit[u][h][0][2]), static_cast<int>(lo), s2);
+                        s2 = __dp4a(static_cast<int>(digit[u][h][1][2]), static_cast<int>(hi), s2);
+                    }
+                    const int t = s2 * 65536 + static_cast<int>(s1 * 256u + s0) - 8 * xs[u];
+                    const float d = fmaf(-zc[r][u], static_cast<float>(xs[u]), static_cast<float>(t));
+                    a = fmaf(sc[r][u], d, a);
+                }
+                acc[r] = a * down;
+            }
+        } else {
+            dot_float();
+        }
+    } else {
+        dot_float();
+    }
+
+    constexpr int V = R * MT;
+    const float total = i4_reduce_scatter<V>(acc, lane);
+    constexpr int span = 32 / V;
+    if ((lane % span) == 0) part[lane / span][warp] = total;
+    __syncthreads();
+    if (tid < V) {
+        const int r = tid / MT;
+        const int m = tid % MT;
+        float s = 0.0f;
+        #pragma unroll
+        for (int wv = 0; wv < kI4Warps; ++wv) s += part[tid][wv];
+        if (r0 + r < N && m0 + m < M) out[(m0 + m) * N + r0 + r] = s;
+    }
+}
+
+// Position of element i of a group in the order in which popcorn's min/max
+// block (256 threads, thread t scanning t, t + 256, ...; a halving tree that
+// keeps the lower partner on a tie) lets it win a tie: threads rank by their
+// bit-reversed index, then by their scan order. Smaller wins.
+__device__ __forceinline__ uint64_t i4_tie_rank(int64_t i) {
+    const uint64_t rev = __brev(static_cast<uint32_t>(i & 255)) >> 24;
+    return (rev << 56) | static_cast<uint64_t>(i >> 8);
+}
+
+__device__ __forceinline__ uint32_t i4_code(float v, float sc, float zp) {
+    float qv = rintf(__fadd_rn(__fdiv_rn(v, sc), zp));
+    if (qv < 0.0f) qv = 0.0f;
+    if (qv > 15.0f) qv = 15.0f;
+    return (qv != qv) ? 0u : static_cast<uint32_t>(qv);  // a NaN code packs as 0
+}
+
+// One warp per (row, group); grid-stride over all groups. With PACK (even
+// group sizes) the warp also writes the group's gs / 2 packed bytes.
+template <bool PACK>
+__global__ void __launch_bounds__(256)
+i4_quantize_kernel(uint8_t* __restrict__ out, float* __restrict__ scale, float* __restrict__ zero,
+                   const float* __restrict__ in, int64_t N, int64_t K, int64_t gs) {
+    const int lane = threadIdx.x & 31;
+    const int64_t groups = K / gs;
+    const int64_t total = N * groups;
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t item = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); item < total;
+         item += nwarps) {
+        const int64_t row = item / groups;
+        const int64_t g = item - row * groups;
+        const float* r = in + row * K + g * gs;
+        // (value, tie rank) minimum and maximum; NaN fails every compare.
+        float mn = __int_as_float(0x7f800000), mx = -__int_as_float(0x7f800000);
+        uint64_t mnk = ~uint64_t{0}, mxk = ~uint64_t{0};
+        for (int64_t i = lane; i < gs; i += 32) {
+            const float v = __ldg(r + i);
+            const uint64_t key = i4_tie_rank(i);
+            if (v < mn || (v == mn && key < mnk)) { mn = v; mnk = key; }
+            if (v > mx || (v == mx && key < mxk)) { mx = v; mxk = key; }
+        }
+        #pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float omn = __shfl_xor_sync(0xffffffffu, mn, off);
+            const uint64_t omnk = __shfl_xor_sync(0xffffffffu, mnk, off);
+            const float omx = __shfl_xor_sync(0xffffffffu, mx, off);
+            const uint64_t omxk = __shfl_xor_sync(0xffffffffu, mxk, off);
+            if (omn < mn || (omn == mn && omnk < mnk)) { mn = omn; mnk = omnk; }
+            if (omx > mx || (omx == mx && omxk < mxk)) { mx = omx; mxk = omxk; }
+        }
+        float sc = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+        if (sc == 0.0f) sc = 1.0f;
+        const float zp = __fdiv_rn(-mn, sc);
+        if (lane == 0) {
+            scale[item] = sc;
+            zero[item] = zp;
+        }
+        if (PACK) {
+            uint8_t* o = out + row * (K >> 1) + ((g * gs) >> 1);
+            for (int64_t b = lane; b < (gs >> 1); b += 32) {
+                const uint32_t lo = i4_code(__ldg(r + 2 * b), sc, zp);
+                const uint32_t hi = i4_code(__ldg(r + 2 * b + 1), sc, zp);
+                o[b] = static_cast<uint8_t>((hi << 4) | lo);
+            }
+        }
+    }
+}
+
+// Odd group sizes: one thread per packed byte, each nibble with the
+// parameters of its own group (stored by i4_quantize_kernel<false>).
+__global__ void __launch_bounds__(256)
+i4_pack_kernel(uint8_t* __restrict__ out, const float* __restrict__ scale, const float* __restrict__ zero,
+               const float* __restrict__ in, int64_t N, int64_t K, int64_t gs) {
+    const int64_t row_bytes = K >> 1;
+    const int64_t groups = K / gs;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < N * row_bytes; t += stride) {
+        const int64_t row = t / row_bytes;
+        const int64_t k = 2 * (t - row * row_bytes);
+        const int64_t glo = row * groups + k / gs;
+        const int64_t ghi = row * groups + (k + 1) / gs;
+        const uint32_t lo = i4_code(__ldg(in + row * K + k), scale[glo], zero[glo]);
+        const uint32_t hi = i4_code(__ldg(in + row * K + k + 1), scale[ghi], zero[ghi]);
+        out[t] = static_cast<uint8_t>((hi << 4) | lo);
+    }
+}
+
+template <int MT, int U, int R>
+popcornStatus_t launch_i4_xs(float* out, const float* x, const uint8_t* q, const float* scale, const float* zero,
+                             int64_t M, int64_t N, int64_t K, int64_t gs, cudaStream_t stream) {
+    const int64_t gx = ceil_div(N, R);
+    const int64_t gy = ceil_div(M, MT);
+    cudaLaunchAttribute attr[1];
+    const cudaLaunchConfig_t cfg = pdl_config(dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)),
+                                              dim3(kI4Threads), 0, stream, attr);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, i4_xs_kernel<MT, U, R>, out, x, q, scale, zero, M, N, K, gs);
+    if (e != cudaSuccess) return record_cuda(e);
+    return check_launch();
+}
+
+}  // namespace
+}  // namespace pcb
+
+extern "C" popcornStatus_t popcornDequantizeMatmulGrouped_i4f32(float* out, const float* x, const uint8_t* qweight,
+                                                               const float* scale, const float* zero, int64_t M,
+                                                               int64_t N, int64_t K, int64_t group_size,
+                                                               cudaStream_t stream) {
+    using namespace pcb;
+    if (out == nullptr || x == nullptr || qweight == nullptr || scale == nullptr || zero == nullptr) {
+        return POPCORN_ERROR_INVALID_VALUE;
+    }
+    if (M <= 0 || N <= 0 || K <= 0) return POPCORN_SUCCESS;
+    if (group_size <= 0 || K % group_size != 0) return POPCORN_ERROR_INVALID_VALUE;
+    if (K % 2 != 0) return POPCORN_ERROR_INVALID_VALUE;
+    const bool aligned = aligned16(x) && (reinterpret_cast<uintptr_t>(qweight) & 7u) == 0 && K % 16 == 0;
+    const int64_t slices = ceil_div(K / 16, kI4Threads);
+    const bool tiny = M * N * K <= (int64_t{1} << 22);
+    const bool grid_ok = ceil_div(M, 4) <= 65535 && ceil_div(N, 2) <= 0x7FFFFFFF;
+    if (!tiny && aligned && group_size % 16 == 0 && slices <= 4 && grid_ok) {
+        if (M == 1) {
+            if (slices == 1) return launch_i4_xs<1, 1, 8>(out, x, qweight, scale, zero, M, N, K, group_size, stream);
+            if (slices == 2) return launch_i4_xs<1, 2, 4>(out, x, qweight, scale, zero, M, N, K, group_size, stream);
+            return launch_i4_xs<1, 4, 2>(out, x, qweight, scale, zero, M, N, K, group_size, stream);
+        }
+        if (M == 2 && slices <= 2) {
+            if (slices == 1) return launch_i4_xs<2, 1, 8>(out, x, qweight, scale, zero, M, N, K, group_size, stream);
+            return launch_i4_xs<2, 2, 4>(out, x, qweight, scale, zero, M, N, K, group_size, stream);
+        }
+        if (slices == 1) return launch_i4_xs<4, 1, 4>(out, x, qweight, scale, zero, M, N, K, group_size, stream);
+    }
+    int64_t blocks = ceil_div(M * N, 256);
+    const int64_t cap = static_cast<int64_t>(device_sm_count()) * 32;
+    if (blocks > cap) blocks = cap;
+    i4_seq_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(out, x, qweight, scale, zero, M, N, K,
+                                                                     group_size);
+    return check_launch();
+}
+
+extern "C" popcornStatus_t popcornQuantizeGrouped_f32i4(uint8_t* out, float* scale, float* zero, const float* input,
+                                                       int64_t N, int64_t K, int64_t group_size,
+                                                       cudaStream_t stream) {
+    using namespace pcb;
+    if (out == nullptr || scale == nullptr || zero == nullptr || input == nullptr) return POPCORN_ERROR_INVALID_VALUE;
+    if (N <= 0 || K <= 0) return POPCORN_SUCCESS;
+    if (group_size <= 0 || K % group_size != 0) return POPCORN_ERROR_INVALID_VALUE;
+    if (K % 2 != 0) return POPCORN_ERROR_INVALID_VALUE;
+    const int64_t items = N * (K / group_size);
+    int64_t blocks = ceil_div(items, kI4Warps);
+    const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
+    if (blocks > cap) blocks = cap;
+    if (group_size % 2 == 0) {
+        i4_quantize_kernel<true><<<static_cast<unsigned>(blocks), kI4Threads, 0, stream>>>(out, scale, zero, input, N,
+                                                                                          K, group_size);
+        return check_launch();
+    }
+    i4_quantize_kernel<false><<<static_cast<unsigned>(blocks), kI4Threads, 0, stream>>>(out, scale, zero, input, N, K,
+                                                                                       group_size);
+    const popcornStatus_t st = check_launch();
+    if (st != POPCORN_SUCCESS) return st;
+    int64_t pblocks = ceil_div(N * (K / 2), 256);
+    const int64_t pcap = static_cast<int64_t>(device_sm_count()) * 32;
+    if (pblocks > pcap) pblocks = pcap;
+    i4_pack_kernel<<<static_cast<unsigned>(pblocks), 256, 0, stream>>>(out, scale, zero, input, N, K, group_size);
+    return check_launch();
+}

@@ -11,7 +11,9 @@ seeded host-parity configuration (M=16, K=1024, N=1024; X ~ N(0,1), W ~
 N(0,0.02), per-row int8). Expected outputs come from the reference loops
 ``ref_dequant_matmul_i8`` (:24-41), ``ref_quantize_i8`` (:677-706) and their
 per-group forms ``ref_dequant_matmul_grouped_i8`` (:42-61) and
-``ref_quantize_grouped_i8`` (:709-742), compiled from the reference sources,
+``ref_quantize_grouped_i8`` (:709-742) and the int4 loops
+``ref_dequant_matmul_grouped_i4`` (:67-99) and ``ref_quantize_grouped_i4``
+(:746-789), compiled from the reference sources,
 never from this repository's code. Cases whose
 values the test spells out (the identity test) also store those values.
 """
@@ -114,6 +116,25 @@ def grouped_cases():
     return cases
 
 
+def int4_cases():
+    cases = {}
+    # dequant_matmul_grouped_i4_basic, test_quantize.cu:525-572 (M2 N2 K8, group 4)
+    x = f32([[1, 2, 3, 4, 5, 6, 7, 8], [0.5, 1, 1.5, 2, 2.5, 3, 3.5, 4]])
+    q = np.array([[0x21, 0x43, 0x65, 0x87], [0x10, 0x32, 0x54, 0x76]], dtype=np.uint8)
+    s = f32([[0.5, 0.25], [1.0, 0.5]])
+    z = f32([[8, 8], [7, 7]])
+    cases["i4_basic"] = (x, q, s, z, 4)
+    # dequant_matmul_grouped_i4_large, :574-626 (M16 N32 K64, group 32, patterned data)
+    M, N, K, gs = 16, 32, 64, 32
+    x = ((np.arange(M * K) % 50).astype(np.float32) - np.float32(25.0)) * np.float32(0.02)
+    q = ((np.arange(N * (K // 2)) * 7 + 3) % 256).astype(np.uint8)
+    g = np.arange(N * (K // gs))
+    s = np.float32(0.01) + (g % 10).astype(np.float32) * np.float32(0.002)
+    z = np.float32(7.5) + (g % 3).astype(np.float32) * np.float32(0.5)
+    cases["i4_large"] = (x.reshape(M, K), q.reshape(N, K // 2), s.reshape(N, K // gs), z.reshape(N, K // gs), gs)
+    return cases
+
+
 def config1_inputs():
     c = CONFIG1
     x = oracle.fill_normal(c["M"] * c["K"], c["x_seed"], c["x_sigma"]).reshape(c["M"], c["K"])
@@ -150,6 +171,17 @@ def main():
     qr, sr = oracle.ref_quantize_grouped(w, 4)
     data["qg_basic/w"], data["qg_basic/codes_test_loop"], data["qg_basic/scale"] = w, qr, sr
     data["qg_basic/group_size"] = np.array(4, dtype=np.int64)
+
+    for name, (x, q, s, z, gs) in int4_cases().items():
+        data[f"{name}/x"], data[f"{name}/q"], data[f"{name}/scale"], data[f"{name}/zero"] = x, q, s, z
+        data[f"{name}/group_size"] = np.array(gs, dtype=np.int64)
+        data[f"{name}/out"] = oracle.ref_dequant_matmul_grouped_i4(x, q, s, z, gs)
+    # quantize_grouped_i4_basic, :919-968 (N2 K8, group 4)
+    w = f32([[0, 1, 2, 3, 4, 5, 6, 7], [-1, 0, 1, 2, 10, 11, 12, 13]])
+    qr, sr, zr = oracle.ref_quantize_grouped_i4(w, 4)
+    data["qi4_basic/w"], data["qi4_basic/packed_test_loop"] = w, qr
+    data["qi4_basic/scale"], data["qi4_basic/zero"] = sr, zr
+    data["qi4_basic/group_size"] = np.array(4, dtype=np.int64)
 
     x, w = config1_inputs()
     q, s = oracle.ref_quantize(w)

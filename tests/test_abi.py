@@ -53,6 +53,12 @@ def test_popcorn_h_keeps_the_reference_signatures():
         "const float* scale, int64_t M, int64_t N, int64_t K, int64_t group_size, cudaStream_t stream );",
         "popcornStatus_t popcornQuantizeGrouped_f32i8( int8_t* out, float* scale, const float* input, int64_t N, "
         "int64_t K, int64_t group_size, cudaStream_t stream );",
+        # include/popcorn.h:506-517, :552-561
+        "popcornStatus_t popcornDequantizeMatmulGrouped_i4f32( float* out, const float* x, const uint8_t* qweight, "
+        "const float* scale, const float* zero, int64_t M, int64_t N, int64_t K, int64_t group_size, "
+        "cudaStream_t stream );",
+        "popcornStatus_t popcornQuantizeGrouped_f32i4( uint8_t* out, float* scale, float* zero, const float* input, "
+        "int64_t N, int64_t K, int64_t group_size, cudaStream_t stream );",
     ]:
         assert proto in norm, proto
 
@@ -205,6 +211,31 @@ def test_grouped_conventions(lib):
         assert mm(FAKE, FAKE, FAKE, FAKE, 2, 2, 10, gs, None) == pc.POPCORN_ERROR_INVALID_VALUE, gs
         assert qg(FAKE, FAKE, FAKE, 2, 10, gs, None) == pc.POPCORN_ERROR_INVALID_VALUE, gs
     assert mm(FAKE, FAKE, FAKE, FAKE, 2, 2, 10, 4, None) == pc.POPCORN_ERROR_INVALID_VALUE
+
+
+def test_int4_conventions(lib):
+    # popcorn src/quantize.cu:418-433, :846-860: null -> invalid, sizes <= 0 ->
+    # success, then group_size <= 0 or not dividing K -> invalid, then odd K
+    # -> invalid (test/test_quantize.cu:628-670: K=9, group 3).
+    mm = lib.popcornDequantizeMatmulGrouped_i4f32
+    qg = lib.popcornQuantizeGrouped_f32i4
+    for i in range(5):
+        args = [FAKE] * 5
+        args[i] = 0
+        assert mm(*args, 1, 1, 8, 4, None) == pc.POPCORN_ERROR_INVALID_VALUE, i
+    for i in range(4):
+        args = [FAKE] * 4
+        args[i] = 0
+        assert qg(*args, 1, 8, 4, None) == pc.POPCORN_ERROR_INVALID_VALUE, i
+    for (M, N, K) in [(0, 2, 8), (2, 0, 8), (2, 2, 0), (-1, 2, 8), (2, 2, -9)]:
+        assert mm(FAKE, FAKE, FAKE, FAKE, FAKE, M, N, K, 3, None) == pc.POPCORN_SUCCESS
+    assert qg(FAKE, FAKE, FAKE, FAKE, 0, 9, 3, None) == pc.POPCORN_SUCCESS
+    assert qg(FAKE, FAKE, FAKE, FAKE, 2, 0, 3, None) == pc.POPCORN_SUCCESS
+    for gs in (0, -4, 3, 16):
+        assert mm(FAKE, FAKE, FAKE, FAKE, FAKE, 2, 2, 10, gs, None) == pc.POPCORN_ERROR_INVALID_VALUE, gs
+        assert qg(FAKE, FAKE, FAKE, FAKE, 2, 10, gs, None) == pc.POPCORN_ERROR_INVALID_VALUE, gs
+    assert mm(FAKE, FAKE, FAKE, FAKE, FAKE, 2, 2, 9, 3, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    assert qg(FAKE, FAKE, FAKE, FAKE, 2, 9, 3, None) == pc.POPCORN_ERROR_INVALID_VALUE
 
 
 def test_batched_size_overflow_is_rejected(lib):

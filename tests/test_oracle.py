@@ -180,3 +180,127 @@ def test_grouped_oracle_equals_reference_loops_random(shape):
     np.testing.assert_array_equal(sr, so)
     np.testing.assert_array_equal(oracle.ref_dequant_matmul_grouped(x, qr, sr, gs),
                                   oracle.dequant_matmul_grouped(x, qr, sr, gs, threads=2))
+
+
+# ---------------------------------------------------------------------------
+# Int4 packed asymmetric per-group (popcorn src/quantize.cu:329-446, :699-888;
+# its CPU loops test/test_quantize.cu:67-99, :746-789).
+# ---------------------------------------------------------------------------
+def _unpack_i4(q):
+    """[N, K/2] bytes -> [N, K] codes, low nibble first (numpy, independent of the oracle)."""
+    q = np.asarray(q, dtype=np.uint8)
+    codes = np.empty((q.shape[0], 2 * q.shape[1]), dtype=np.int64)
+    codes[:, 0::2] = q & 0x0F
+    codes[:, 1::2] = q >> 4
+    return codes
+
+
+@pytest.mark.parametrize("case", ["i4_basic", "i4_large"])
+def test_int4_matmul_matches_reference_loop_bitwise(golden, case):
+    x, q = golden[f"{case}/x"], golden[f"{case}/q"]
+    s, z = golden[f"{case}/scale"], golden[f"{case}/zero"]
+    gs = int(golden[f"{case}/group_size"])
+    for threads in (1, 3):
+        out = oracle.dequant_matmul_grouped_i4(x, q, s, z, gs, threads=threads)
+        np.testing.assert_array_equal(out, golden[f"{case}/out"])
+    # The same product from the unpacked codes in float64.
+    codes = _unpack_i4(q)
+    g = np.arange(codes.shape[1]) // gs
+    w = (codes - z[:, g].astype(np.float64)) * s[:, g].astype(np.float64)
+    ref = x.astype(np.float64) @ w.T
+    assert oracle.normwise_rel_err(golden[f"{case}/out"], ref) <= 1e-6
+
+
+def test_int4_basic_layout_is_low_nibble_first(golden):
+    # The test's comment spells out the codes of row 0 (1..8) and row 1 (0..7).
+    np.testing.assert_array_equal(_unpack_i4(golden["i4_basic/q"]), [[1, 2, 3, 4, 5, 6, 7, 8],
+                                                                      [0, 1, 2, 3, 4, 5, 6, 7]])
+
+
+def test_int4_swapped_nibbles_are_caught(golden):
+    q = golden["i4_large/q"]
+    swapped = ((q >> 4) | (q << 4)).astype(np.uint8)
+    out = oracle.dequant_matmul_grouped_i4(golden["i4_large/x"], swapped, golden["i4_large/scale"],
+                                           golden["i4_large/zero"], int(golden["i4_large/group_size"]))
+    assert oracle.normwise_rel_err(out, golden["i4_large/out"]) > 1e-3
+
+
+def test_int4_quantize_test_loop_matches_reference(golden):
+    q, s, z = oracle.quantize_grouped_i4(golden["qi4_basic/w"], int(golden["qi4_basic/group_size"]), test_loop=True)
+    np.testing.assert_array_equal(q, golden["qi4_basic/packed_test_loop"])
+    np.testing.assert_array_equal(s.view(np.uint32), golden["qi4_basic/scale"].view(np.uint32))
+    np.testing.assert_array_equal(z.view(np.uint32), golden["qi4_basic/zero"].view(np.uint32))
+    # Group (0..3): scale 3/15, zero 0, codes round(v * 5) -> 0, 5, 10, 15.
+    np.testing.assert_array_equal(_unpack_i4(q)[0, :4], [0, 5, 10, 15])
+
+
+def test_int4_quantize_variants_differ_only_on_ties():
+    w = oracle.fill_normal(16 * 512, 41, 0.02).reshape(16, 512)
+    qk, sk, zk = oracle.quantize_grouped_i4(w, 64)
+    qt, st, zt = oracle.quantize_grouped_i4(w, 64, test_loop=True)
+    np.testing.assert_array_equal(sk, st)
+    np.testing.assert_array_equal(zk, zt)
+    ck, ct = _unpack_i4(qk), _unpack_i4(qt)
+    g = np.arange(512) // 64
+    d = w / sk[:, g] + zk[:, g]
+    ties = (d - np.floor(d)) == 0.5
+    assert np.all(ck[~ties] == ct[~ties])
+    assert np.all(np.abs(ck - ct) <= 1)
+
+
+def _kernel_order_key(i):
+    """Rank of element i of a group in popcorn's 256-thread min/max block:
+    thread i % 256 (its tree keeps the lower partner, so threads rank by their
+    bit-reversed index), then the thread's own scan order i // 256."""
+    t = i % 256
+    rev = int(f"{t:08b}"[::-1], 2)
+    return (rev, i // 256)
+
+
+@pytest.mark.parametrize("gs", [256, 512, 96, 2048])
+def test_int4_quantize_zero_sign_follows_the_kernel_block_order(gs):
+    rng = np.random.default_rng(gs)
+    for trial in range(20):
+        w = np.zeros((1, gs), dtype=np.float32)
+        neg = rng.choice(gs, size=int(rng.integers(1, 4)), replace=False)
+        w[0, neg] = -0.0
+        q, s, z = oracle.quantize_grouped_i4(w, gs)
+        # All values compare equal, so min is the element the block keeps:
+        # the smallest key; zero = -min / 1.
+        first = min(range(gs), key=_kernel_order_key)
+        min_is_neg = np.signbit(w[0, first])
+        assert s[0, 0] == 1.0
+        assert np.signbit(z[0, 0]) == (not min_is_neg)
+        assert np.all(q == 0)
+
+
+def test_int4_quantize_nan_and_inf():
+    w = oracle.fill_normal(4 * 32, 3, 1.0).reshape(4, 32).copy()
+    w[0, 5] = np.nan                 # skipped by min/max; its own code packs as 0
+    w[1, :16] = np.nan               # a group of NaN only: min +inf, max -inf
+    w[2, 3] = np.inf
+    q, s, z = oracle.quantize_grouped_i4(w, 16)
+    finite = np.delete(w[0, :16], 5)
+    assert s[0, 0] == np.float32(np.float32(finite.max() - finite.min()) / np.float32(15))
+    assert _unpack_i4(q)[0, 5] == 0
+    assert s[1, 0] == -np.inf and np.isnan(z[1, 0]) and np.all(_unpack_i4(q)[1, :16] == 0)
+    assert s[2, 0] == np.inf
+
+
+@pytest.mark.skipif(not oracle.have_ref_loops(), reason="reference loops not built (oracle/_ref)")
+@pytest.mark.parametrize("shape", [(1, 7, 8, 4), (3, 17, 64, 16), (5, 33, 96, 32), (4, 40, 256, 128), (2, 9, 36, 6),
+                                   (2, 5, 30, 3)])
+def test_int4_oracle_equals_reference_loops_random(shape):
+    M, N, K, gs = shape
+    x = oracle.fill_normal(M * K, M + N, 1.0).reshape(M, K)
+    w = oracle.fill_normal(N * K, K, 0.02).reshape(N, K)
+    if gs % 2 == 0:
+        qr, sr, zr = oracle.ref_quantize_grouped_i4(w, gs)
+        qo, so, zo = oracle.quantize_grouped_i4(w, gs, test_loop=True)
+        np.testing.assert_array_equal(qr, qo)
+        np.testing.assert_array_equal(sr, so)
+        np.testing.assert_array_equal(zr, zo)
+    else:
+        qr, sr, zr = oracle.quantize_grouped_i4(w, gs)
+    np.testing.assert_array_equal(oracle.ref_dequant_matmul_grouped_i4(x, qr, sr, zr, gs),
+                                  oracle.dequant_matmul_grouped_i4(x, qr, sr, zr, gs, threads=2))
