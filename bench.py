@@ -48,6 +48,9 @@ WORKLOADS = {
     # Int4 packed asymmetric (popcornDequantizeMatmulGrouped_i4f32), decode size,
     # group 128: algorithmic bytes = packed codes + group scales and zero points.
     "int4_decode": dict(M=1, K=4096, N=4096, unit="GB/s", bound="hbm", group_size=128, bits=4),
+    # The same two formats at prefill size (tensor cores, group factors in the converters).
+    "grouped_prefill": dict(M=2048, K=4096, N=4096, unit="TFLOP/s", bound="tensor", group_size=128),
+    "int4_prefill": dict(M=2048, K=4096, N=4096, unit="TFLOP/s", bound="tensor", group_size=128, bits=4),
 }
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of
@@ -67,7 +70,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
-    p.add_argument("--extras", default="skinny,prefill,grouped_decode,int4_decode",
+    p.add_argument("--extras", default="skinny,prefill,grouped_decode,int4_decode,grouped_prefill,int4_prefill",
                    help="comma-separated extra single-GPU workloads reported beside the headline (N=1 only)")
     p.add_argument("--stack", default="1,128",
                    help="M values of the 32-layer 7B-shaped linear stack timed at every N ('none' to skip)")
@@ -254,16 +257,22 @@ class Setup:
         if self.world > 1:
             self.torch.distributed.all_gather_into_tensor(self.gathered, self.out[j].view(-1), group=group)
 
+    def grouped_tensor(self):
+        """Per-group formats take the tensor-core path (prologue + GEMM) above
+        four activation rows and 2^27 multiply-adds."""
+        return bool(self.gs) and self.M > 4 and self.M * self.Nl * self.K >= (1 << 27) and self.gs % 32 == 0
+
     def launches_per_step(self):
-        if self.fused is not None or self.gs:
+        if self.fused is not None:
             return 1
+        if self.gs:
+            return 2 if self.grouped_tensor() else 1
         return self.pc.launch_count(self.x[0].data_ptr(), self.q[0].data_ptr(), self.M, self.Nl, self.K)
 
     def path(self):
-        if self.bits == 4:
-            return f"int4_f32 (group {self.gs})"
         if self.gs:
-            return f"grouped_f32 (group {self.gs})"
+            fmt = "int4" if self.bits == 4 else "grouped"
+            return f"{fmt}_{'tensor_f16' if self.grouped_tensor() else 'f32'} (group {self.gs})"
         return self.pc.PATH_NAMES[self.pc.select_path(self.x[0].data_ptr(), self.q[0].data_ptr(),
                                                       self.M, self.Nl, self.K)]
 

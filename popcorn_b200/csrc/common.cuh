@@ -20,6 +20,10 @@ constexpr int kB200Sms = 148;
 // Ranks of one tensor-parallel group (GPUs of one node).
 constexpr int kPeerMaxRanks = 8;
 
+// Weight formats of the tensor-core path: per-channel int8 (one scale per
+// row), per-group int8, per-group int4 with zero points.
+enum WeightFormat : int { kFmtChannel = 0, kFmtGroup8 = 1, kFmtGroup4 = 2 };
+
 // Collective fused into the decode GEMV.
 enum PeerMode : int { kPeerNone = 0, kPeerGather = 1, kPeerReduce = 2 };
 
@@ -109,6 +113,13 @@ popcornStatus_t tc_dequant_matmul(float* out, const float* x, const int8_t* q,
                                   const float* scale, int64_t M, int64_t N,
                                   int64_t K, cudaStream_t stream);
 int tc_launch_count(int64_t M, int64_t N, int64_t K);
+
+// tcgen05 path for the per-group formats (int8 codes [N, K] or packed int4
+// [N, K/2]; zero is null for int8); requires tc_grouped_supported(...).
+bool tc_grouped_supported(const void* q, int64_t M, int64_t N, int64_t K, int64_t gs);
+popcornStatus_t tc_dequant_matmul_grouped(WeightFormat fmt, float* out, const float* x, const void* q,
+                                          const float* scale, const float* zero, int64_t M, int64_t N, int64_t K,
+                                          int64_t gs, cudaStream_t stream);
 
 // Fused decode GEMV + all-gather / all-reduce (gemv.cu). `rows` is the
 // number of weight rows of this rank's call (n_local, or N for a reduce).

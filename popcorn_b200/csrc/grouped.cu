@@ -264,6 +264,12 @@ extern "C" popcornStatus_t popcornDequantizeMatmulGrouped_i8f32(float* out, cons
     if (out == nullptr || x == nullptr || qweight == nullptr || scale == nullptr) return POPCORN_ERROR_INVALID_VALUE;
     if (M <= 0 || N <= 0 || K <= 0) return POPCORN_SUCCESS;
     if (group_size <= 0 || K % group_size != 0) return POPCORN_ERROR_INVALID_VALUE;
+    // More than four activation rows and >= 2^27 multiply-adds: tensor cores,
+    // the group factors applied by the converters.
+    if (M > 4 && static_cast<double>(M) * static_cast<double>(N) * static_cast<double>(K) >= 134217728.0 &&
+        tc_grouped_supported(qweight, M, N, K, group_size)) {
+        return tc_dequant_matmul_grouped(kFmtGroup8, out, x, qweight, scale, nullptr, M, N, K, group_size, stream);
+    }
     const bool aligned = aligned16(x) && aligned16(qweight) && K % 16 == 0;
     const int64_t slices = ceil_div(K / 16, kGThreads);
     const bool tiny = M * N * K <= (int64_t{1} << 22);

@@ -448,6 +448,12 @@ extern "C" popcornStatus_t popcornDequantizeMatmulGrouped_i4f32(float* out, cons
     if (M <= 0 || N <= 0 || K <= 0) return POPCORN_SUCCESS;
     if (group_size <= 0 || K % group_size != 0) return POPCORN_ERROR_INVALID_VALUE;
     if (K % 2 != 0) return POPCORN_ERROR_INVALID_VALUE;
+    // More than four activation rows and >= 2^27 multiply-adds: tensor cores,
+    // the group factors applied by the converters.
+    if (M > 4 && static_cast<double>(M) * static_cast<double>(N) * static_cast<double>(K) >= 134217728.0 &&
+        tc_grouped_supported(qweight, M, N, K, group_size)) {
+        return tc_dequant_matmul_grouped(kFmtGroup4, out, x, qweight, scale, zero, M, N, K, group_size, stream);
+    }
     const bool aligned = aligned16(x) && (reinterpret_cast<uintptr_t>(qweight) & 7u) == 0 && K % 16 == 0;
     const int64_t slices = ceil_div(K / 16, kI4Threads);
     const bool tiny = M * N * K <= (int64_t{1} << 22);

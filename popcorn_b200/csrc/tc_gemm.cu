@@ -11,19 +11,29 @@
 // Two launches per call:
 //  1. x_to_f16_kernel: x f32 [M, K] -> x16 f16 [M, K] + rowscale [M] = 2^-e_m
 //     in stream-ordered scratch from a private memory pool.
-//  2. tc_gemm_kernel<BM>: one CTA per 128 (weight rows) x BM (activation rows)
-//     output tile; swap-AB so the weight tile is the MMA "A" operand:
-//       warp 0      TMA producer: x16 tile [BM x 64] (128B swizzle) and the
-//                   int8 weight tile [128 x 64] (64B swizzle) per stage;
+//  2. tc_gemm_kernel<BM, FMT>: one CTA per 128 (weight rows) x BM (activation
+//     rows) output tile (cluster split-K when the tiles fill less than half
+//     the GPU), or tc_gemm_pair_kernel<RX, FMT>: a CTA pair per 256 x 2 RX
+//     tile with tcgen05.mma.cta_group::2. Swap-AB, so the weight tile is the
+//     MMA "A" operand; per 128-deep k-block stage:
+//       warp 0      TMA producer: x16 tile (128B swizzle) and the weight-code
+//                   tile [128 rows x 128 int8 (128B swizzle) or 64 bytes of
+//                   packed int4 (64B swizzle)];
 //       warp 1      tcgen05.mma issuer (A from tensor memory, B = x16 tile
-//                   from shared memory, D = f32 [128 x BM] in tensor memory);
-//       warps 2-5   converters: each thread owns one weight row, widens its
-//                   64 codes to f16 with the exponent trick and writes them
-//                   to tensor memory (tcgen05.st) as the A operand;
-//       warps 6-9   epilogue: tcgen05.ld of the accumulator, one row per
+//                   from shared memory, D = f32 in tensor memory);
+//       warps 2-9   converters in two groups of four: each thread owns one
+//                   weight row, group g converts codes [64 g, 64 g + 64) of
+//                   every k-block to f16 and writes them to tensor memory
+//                   (tcgen05.st) as the A operand;
+//       warps 10-13 epilogue: tcgen05.ld of the accumulator, one row per
 //                   lane, so each column m is a coalesced 128-byte store.
+// Weight formats (FMT): per-channel int8 codes are exact in f16 and the
+// epilogue multiplies by scale[n]; per-group int8 codes are written as
+// code * scale[n, g] * 2^e_n and int4 codes as (code - zero[n, g]) *
+// scale[n, g] * 2^e_n (one rounding to f16), 2^e_n a power of two per row
+// that keeps the row inside f16's range, undone by the epilogue.
 // Keeping the widened weights in tensor memory means shared memory carries
-// only the int8 codes and the f16 activations, not a second f16 copy.
+// only the weight codes and the f16 activations, not a second f16 copy.
 //
 // Roofline: tensor (dense f16) for large M; algorithmic work 2*M*N*K.
 #include <cuda.h>
@@ -49,7 +59,7 @@ constexpr int kThreads = 448;  // 14 warps
 constexpr int kWarpTma = 0;
 constexpr int kWarpMma = 1;
 constexpr int kWarpConv0 = 2;  // two groups of four converter warps: 2-5, 6-9
-constexpr int kConvGroups = 2;
+constexpr int kConvGroups = 2;  // group g converts codes [64 g, 64 g + 64) of every k-block
 constexpr int kWarpEpi0 = 10;
 
 // Per activation-tile height BM: k-blocks of 128 (one [128 x 128] int8 weight
@@ -57,17 +67,19 @@ constexpr int kWarpEpi0 = 10;
 // ring of kStages stages; ring slot s is also tensor-memory A buffer s, so
 // one barrier per slot says "its tiles and its A buffer are free again".
 // Tensor memory: accumulator (BM columns) + kStages A buffers of 64 columns.
-template <int BM>
+template <int BM, int FMT = kFmtChannel>
 struct Cfg {
     static constexpr int kBK = 128;
     static constexpr int kSub = kBK / 64;           // 64-wide f16 swizzle atoms per stage
     static constexpr int kACols = kBK / 2;          // tensor-memory columns per A buffer
     static constexpr int kStages = BM >= 128 ? 4 : (BM >= 64 ? 6 : 7);
     static constexpr int kXBytes = BM * kBK * 2;   // f16 activation tile per stage
-    static constexpr int kWBytes = kTileN * kBK;   // int8 weight tile per stage
+    static constexpr int kWRow = FMT == kFmtGroup4 ? kBK / 2 : kBK;  // weight bytes per row and stage
+    static constexpr int kWBytes = kTileN * kWRow;  // weight tile per stage
     static constexpr int kTmemCols = 512;
     static constexpr int kNumBars = 3 * kStages + 2;
-    static constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16;
+    // ring, barriers, tensor-memory slot (16 B), per-row output scales
+    static constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16 + kTileN * 4;
     // Split-K reduction buffer: [128 weight rows][BM + 4] f32 in the idle ring.
     static constexpr int kRedStride = BM + 4;
     static_assert(kXBytes % 1024 == 0, "x16 stages must stay 1024-byte aligned");
@@ -259,29 +271,190 @@ __device__ __forceinline__ void widen4_f16(uint32_t word, uint32_t& lo, uint32_t
     hi = *reinterpret_cast<uint32_t*>(&h);
 }
 
+__device__ __forceinline__ uint32_t f16x2_bits(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Per-group formats: the converters write w * 2^e_n to tensor memory as f16
+// and the epilogue multiplies by 2^-e_n (exact). 2^e_n brings the largest
+// weight row n can hold -- 128 |s| for int8 codes, (15 + |z|) |s| for int4 --
+// into [2^13, 2^14), far inside f16's range, whatever the scales' magnitude.
+template <int FMT>
+__device__ __forceinline__ int group_row_exp(const float* __restrict__ scale, const float* __restrict__ zero, int n,
+                                             int N, int groups) {
+    if (n >= N) return 0;
+    const float* sr = scale + static_cast<int64_t>(n) * groups;
+    const float* zr = zero + static_cast<int64_t>(n) * groups;
+    float m = 0.0f;
+    // 32 groups per pass, every load of a pass in flight at once (the scales
+    // usually come from HBM: one round trip per pass).
+    for (int g0 = 0; g0 < groups; g0 += 32) {
+        float a[32], z[32];
+        #pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            a[j] = (g0 + j < groups) ? __ldg(sr + g0 + j) : 0.0f;
+            if constexpr (FMT == kFmtGroup4) z[j] = (g0 + j < groups) ? __ldg(zr + g0 + j) : 0.0f;
+        }
+        #pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            float b;
+            if constexpr (FMT == kFmtGroup4) {
+                b = (15.0f + fabsf(z[j])) * fabsf(a[j]);
+            } else {
+                b = 128.0f * fabsf(a[j]);
+            }
+            m = b > m ? b : m;  // NaN skipped
+        }
+    }
+    int e = 0;
+    if (m > 0.0f && m <= 3.402823466e38f) {
+        int p;
+        frexpf(m, &p);  // m in [2^(p-1), 2^p)
+        e = 14 - p;     // m * 2^e in [2^13, 2^14)
+        e = e < -126 ? -126 : (e > 126 ? 126 : e);
+    }
+    return e;
+}
+
+// Group factors of half `h` (64 codes) of a 128-deep k-block of weight row n,
+// per 32-code quarter: f[j] = scale[n, g] * 2^e_n and (int4) zf[j] =
+// zero[n, g] * f[j] for quarter 2h + j; zero for rows past N and quarters past
+// K (whose codes and activations are zero-filled).
+template <int FMT>
+__device__ __forceinline__ void group_factors(const float* __restrict__ scale, const float* __restrict__ zero, int n,
+                                              int N, int K, int gs, int kb, int h, float pw, float (&f)[2],
+                                              float (&zf)[2]) {
+    const int groups = K / gs;
+    #pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const int k = kb * 128 + h * 64 + q * 32;
+        f[q] = 0.0f;
+        zf[q] = 0.0f;
+        if (n < N && k < K) {
+            const int64_t i = static_cast<int64_t>(n) * groups + k / gs;
+            f[q] = __ldg(scale + i) * pw;
+            if constexpr (FMT == kFmtGroup4) zf[q] = __ldg(zero + i) * f[q];
+        }
+    }
+}
+
+// Four int8 codes -> two f16x2 words of code * f: the codes widen exactly
+// (widen4_f16), then one packed f16 multiply by f rounded to f16 (f16x2 in
+// both halves). Relative error <= 2^-11 per weight (f's rounding and the
+// product's), normwise ~4e-4 with the f16 activations.
+__device__ __forceinline__ void widen4_scaled(uint32_t word, __half2 f2, uint32_t& lo, uint32_t& hi) {
+    uint32_t a, b;
+    widen4_f16(word, a, b);
+    __half2 l = __hmul2(*reinterpret_cast<const __half2*>(&a), f2);
+    __half2 h = __hmul2(*reinterpret_cast<const __half2*>(&b), f2);
+    lo = *reinterpret_cast<uint32_t*>(&l);
+    hi = *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Eight int4 codes (one word, low nibble first) -> four f16x2 words of
+// code * f - zero * f.
+__device__ __forceinline__ void widen8_i4_scaled(uint32_t word, float f, float zf, uint32_t* h) {
+    const uint32_t lo = word & 0x0F0F0F0Fu;         // even k
+    const uint32_t hi = (word >> 4) & 0x0F0F0F0Fu;  // odd k
+    const float2 bias = make_float2(-8388608.0f, -8388608.0f);  // -2^23
+    const float2 ff = make_float2(f, f);
+    const float2 nz = make_float2(-zf, -zf);
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float2 c = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440 + j)),
+                               __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440 + j)));
+        c = __ffma2_rn(__fadd2_rn(c, bias), ff, nz);
+        h[j] = f16x2_bits(c.x, c.y);
+    }
+}
+
+// The codes of half g (codes [64 g, 64 g + 64)) of weight row r of a ring
+// stage at `tile`, in k order: 16 words of int8 codes (128B swizzle: chunk ^=
+// r & 7) or 8 words of packed int4 codes (64B swizzle: chunk ^= (r >> 1) & 3).
+template <int FMT>
+__device__ __forceinline__ void load_half(const uint8_t* tile, int r, int g, uint32_t (&w)[16]) {
+    if constexpr (FMT == kFmtGroup4) {
+        const uint8_t* row = tile + r * 64;
+        #pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+            const int c = 2 * g + c2;
+            const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ ((r >> 1) & 3)) << 4));
+            w[4 * c2 + 0] = v.x;
+            w[4 * c2 + 1] = v.y;
+            w[4 * c2 + 2] = v.z;
+            w[4 * c2 + 3] = v.w;
+        }
+    } else {
+        const uint8_t* row = tile + r * 128;
+        #pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+            const int c = g * 4 + c4;
+            const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) << 4));
+            w[4 * c4 + 0] = v.x;
+            w[4 * c4 + 1] = v.y;
+            w[4 * c4 + 2] = v.z;
+            w[4 * c4 + 3] = v.w;
+        }
+    }
+}
+
+// Those 64 codes -> 32 f16x2 words of the A operand: int8 codes widened
+// exactly (per-channel) or scaled per group, int4 codes with zero point and
+// scale. f, zf: the factors of the half's two 32-code quarters.
+template <int FMT>
+__device__ __forceinline__ void widen_half(const uint32_t (&w)[16], const float (&f)[2], const float (&zf)[2],
+                                           uint32_t (&h)[32]) {
+    if constexpr (FMT == kFmtGroup4) {
+        #pragma unroll
+        for (int k = 0; k < 8; ++k) widen8_i4_scaled(w[k], f[k / 4], zf[k / 4], h + 4 * k);
+    } else if constexpr (FMT == kFmtGroup8) {
+        const __half2 f2[2] = {__float2half2_rn(f[0]), __float2half2_rn(f[1])};
+        #pragma unroll
+        for (int k = 0; k < 16; ++k) widen4_scaled(w[k], f2[k / 8], h[2 * k], h[2 * k + 1]);
+    } else {
+        #pragma unroll
+        for (int k = 0; k < 16; ++k) widen4_f16(w[k], h[2 * k], h[2 * k + 1]);
+    }
+}
+
+// Half g of a 128-deep k-block of weight row r into A-buffer columns
+// [32 g, 32 g + 32) of tensor-memory lane r (`taddr` = the A buffer at this
+// warp's lanes).
+template <int FMT>
+__device__ __forceinline__ void convert_half(const uint8_t* tile, int r, int g, uint32_t taddr, const float (&f)[2],
+                                             const float (&zf)[2]) {
+    uint32_t w[16];
+    load_half<FMT>(tile, r, g, w);
+    uint32_t h[32];
+    widen_half<FMT>(w, f, zf, h);
+    tmem_st_32x32b_x32(taddr + g * 32, h);
+}
+
 // Split-K over a cluster: with `splits` = C > 1 the C CTAs of a cluster
 // (consecutive blockIdx.x) share one 128-row tile, rank r taking k-blocks
 // [num_kb * r / C, num_kb * (r + 1) / C). Each rank copies its accumulator
 // into its idle ring, and after a cluster barrier rank r adds the C partials
 // of weight rows [128 r / C, 128 (r + 1) / C) in rank order 0..C-1 through
 // distributed shared memory, so results do not depend on timing.
-template <int BM>
+template <int BM, int FMT>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                float* __restrict__ out, const float* __restrict__ scale, const float* __restrict__ rowscale,
-               int M, int N, int K, int splits) {
-    using C = Cfg<BM>;
+               const float* __restrict__ zero, int gs, int M, int N, int K, int splits) {
+    using C = Cfg<BM, FMT>;
     constexpr int S = C::kStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr int kBK = C::kBK;
     uint8_t* xs = smem;                                  // S x kSub x [BM][64] f16, 128B swizzle
-    uint8_t* ws = smem + S * C::kXBytes;                 // S x [128][128] int8, 128B swizzle
+    uint8_t* ws = smem + S * C::kXBytes;                 // S x [128][kWRow] weight codes
     uint64_t* bars = reinterpret_cast<uint64_t*>(ws + S * C::kWBytes);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+    float* rsc = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(tmem_slot) + 16);  // [128] output scales
     float* red = reinterpret_cast<float*>(smem);         // split-K partial, reuses the ring
 
-    // full[s]: stage s landed (TMA). afull[s]: A buffer s written (4 converter
+    // full[s]: stage s landed (TMA). afull[s]: A buffer s written (8 converter
     // warps). release[s]: the MMAs reading stage s and A buffer s finished.
     const uint32_t full0 = smem_addr(bars);
     const uint32_t afull0 = full0 + 8 * S;
@@ -301,7 +474,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(full0 + 8 * s, 1);
-            mbar_init(afull0 + 8 * s, 4);
+            mbar_init(afull0 + 8 * s, 4 * kConvGroups);
             mbar_init(release0 + 8 * s, 1);
         }
         mbar_init(acc_full, 1);
@@ -320,7 +493,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
     // with this CTA's first weight tiles (written before the prologue ran,
     // so already complete), then wait for x16 and rowscale.
     if (warp == kWarpTma && lane == 0) {
-        for (int i = 0; i < S && i < n_kb; ++i) tma_prefetch_l2_2d(&tmap_w, (kb0 + i) * kBK, n0);
+        for (int i = 0; i < S && i < n_kb; ++i) tma_prefetch_l2_2d(&tmap_w, (kb0 + i) * C::kWRow, n0);
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
     tc_fence_before();
@@ -342,7 +515,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
                     tma_load_2d(smem_addr(xs + s * C::kXBytes + sub * BM * 128), &tmap_x, kb * kBK + sub * 64, 0,
                                 full0 + 8 * s);
                 }
-                tma_load_2d(smem_addr(ws + s * C::kWBytes), &tmap_w, kb * kBK, n0, full0 + 8 * s);
+                tma_load_2d(smem_addr(ws + s * C::kWBytes), &tmap_w, kb * C::kWRow, n0, full0 + 8 * s);
             }
             // Nothing of ours may still be landing in shared memory at exit:
             // wait (bounded) for the last fill of every stage.
@@ -376,38 +549,38 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
         }
     } else if (warp < kWarpEpi0) {
         // Converters: thread owns weight row r of the tile = tensor-memory lane r.
-        // Two groups of four warps take alternate k-blocks, so two conversions
-        // are always in flight.
+        // Both groups of four warps convert every k-block, group g its codes
+        // [64 g, 64 g + 64), so a block is ready in half a conversion's time.
         const int quarter = warp & 3;
         const int group = (warp - kWarpConv0) >> 2;
         const int r = quarter * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-        for (int i = group; i < n_kb; i += kConvGroups) {
+        float pw = 1.0f;
+        if constexpr (FMT != kFmtChannel) {
+            pw = __int_as_float((group_row_exp<FMT>(scale, zero, n0 + r, N, K / gs) + 127) << 23);
+        }
+        // Group factors one k-block ahead: the loads for the next block overlap
+        // this block's wait and conversion.
+        float f[2] = {}, zf[2] = {};
+        if constexpr (FMT != kFmtChannel) {
+            if (n_kb > 0) group_factors<FMT>(scale, zero, n0 + r, N, K, gs, kb0, group, pw, f, zf);
+        }
+        for (int i = 0; i < n_kb; ++i) {
             const int s = i % S;
+            float fn[2] = {}, zn[2] = {};
+            if constexpr (FMT != kFmtChannel) {
+                if (i + 1 < n_kb) group_factors<FMT>(scale, zero, n0 + r, N, K, gs, kb0 + i + 1, group, pw, fn, zn);
+            }
             bool ok = mbar_wait(full0 + 8 * s, (i / S) & 1, err, 8u);
             if (ok && i >= S) ok = mbar_wait(release0 + 8 * s, ((i / S) - 1) & 1, err, 16u);
             // tcgen05.st below is warp-collective: leave together or not at all.
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
-            const uint8_t* row = ws + s * C::kWBytes + r * kBK;
+            convert_half<FMT>(ws + s * C::kWBytes, r, group, tmem + lane_addr + BM + s * C::kACols, f, zf);
             #pragma unroll
-            for (int g = 0; g < kBK / 64; ++g) {
-                // 64 codes (four 16-byte chunks, 128B swizzle: chunk ^= r & 7)
-                // -> 32 f16x2 columns.
-                uint32_t w[16];
-                #pragma unroll
-                for (int c4 = 0; c4 < 4; ++c4) {
-                    const int c = g * 4 + c4;
-                    const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) << 4));
-                    w[4 * c4 + 0] = v.x;
-                    w[4 * c4 + 1] = v.y;
-                    w[4 * c4 + 2] = v.z;
-                    w[4 * c4 + 3] = v.w;
-                }
-                uint32_t h[32];
-                #pragma unroll
-                for (int k = 0; k < 16; ++k) widen4_f16(w[k], h[2 * k], h[2 * k + 1]);
-                tmem_st_32x32b_x32(tmem + lane_addr + BM + s * C::kACols + g * 32, h);
+            for (int q = 0; q < 2; ++q) {
+                f[q] = fn[q];
+                zf[q] = zn[q];
             }
             tmem_wait_st();
             tc_fence_before();
@@ -420,13 +593,22 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
         const int row = quarter * 32 + lane;
         const int n = n0 + row;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        // Output scale of row n: scale[n], or 2^-e_n for a per-group format.
+        float sc = 0.0f;
+        if (n < N) {
+            if constexpr (FMT == kFmtChannel) {
+                sc = __ldg(scale + n);
+            } else {
+                sc = __int_as_float((127 - group_row_exp<FMT>(scale, zero, n, N, K / gs)) << 23);
+            }
+        }
+        rsc[row] = sc;
         const bool ok = mbar_wait(acc_full, 0, err, 32u);
         if (__all_sync(0xffffffffu, ok)) {
             tc_fence_after();
             // The ring's last asynchronous (TMA, MMA) accesses are complete;
             // order them before this thread's generic stores into it.
             if (splits > 1) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            const float sc = (n < N) ? __ldg(scale + n) : 0.0f;
             #pragma unroll 1
             for (int c0 = 0; c0 < BM; c0 += 32) {
                 if (c0 >= M) break;
@@ -483,7 +665,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
                 }
                 const int nn = n0 + rl;
                 if (nn < N) {
-                    const float sc = __ldg(scale + nn);
+                    const float sc = rsc[rl];
                     const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
                     #pragma unroll
                     for (int k = 0; k < 4; ++k) {
@@ -503,20 +685,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
 }
 
 // ------------------------------------------------------------ CTA-pair kernel
-// Large M: a cluster of two CTAs computes a 256 (weight rows) x 256
+// Large M: a cluster of two CTAs computes a 256 (weight rows) x 2*RX
 // (activation rows) tile with tcgen05.mma.cta_group::2. CTA r of the pair
 // converts its own 128 weight rows into its own tensor memory (the A operand
 // is split by rows across the pair) and loads only its half of the
 // activation tile (the B operand is split the same way), so each CTA moves
-// half the tiles a single CTA with the same output tile would (48 KB per
-// 128-deep k-step), and the pair's MMA work per k-step doubles.
+// half the tiles a single CTA with the same output tile would, and the
+// pair's MMA work per k-step doubles.
 // The leader CTA (rank 0) issues the MMAs; the pair synchronises through the
 // leader's mbarriers:
 //   full[s]   activation halves of both CTAs landed (TMA .cta_group::2 loads
 //             complete their bytes on the leader's barrier; only the leader
 //             posts the expected byte count);
 //   wfull[s]  this CTA's weight tile landed (local);
-//   afull[s]  both CTAs' converters wrote A buffer s (8 remote arrivals);
+//   afull[s]  both CTAs' converters wrote A buffer s (16 remote arrivals);
 //   release[s], acc_full, drain: multicast tcgen05.commit from the leader to
 //             the same barrier in both CTAs (release[s] frees ring slot s:
 //             its shared-memory tiles and A buffer s).
@@ -526,13 +708,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
 // RX activation rows per CTA (the pair's MMA is 256 x 2*RX): 128 for
 // prefill, 16/32/64 for skinny shapes with many weight tiles, where one MMA
 // instruction now covers both CTAs' 128 weight rows.
-template <int RX>
+template <int RX, int FMT = kFmtChannel>
 struct PairCfg {
     static constexpr int kBK = 128;
     static constexpr int kSub = kBK / 64;                  // 64-wide f16 swizzle atoms per stage
     static constexpr int kRowsX = RX;
     static constexpr int kXBytes = RX * kBK * 2;           // f16 activation half-tile per stage
-    static constexpr int kWBytes = kTileN * kBK;           // 16 KB int8 weight tile per stage
+    static constexpr int kWRow = FMT == kFmtGroup4 ? kBK / 2 : kBK;  // weight bytes per row and stage
+    static constexpr int kWBytes = kTileN * kWRow;         // weight tile per stage (16 KB int8, 8 KB int4)
     static constexpr int kACols = kBK / 2;
     static constexpr int kTmemCols = 512;                  // 2*RX accumulator + A buffers
     // Ring slot s is also A buffer s (one release barrier frees both):
@@ -548,12 +731,12 @@ struct PairCfg {
     static_assert(kXBytes % 1024 == 0, "x16 stages must stay 1024-byte aligned");
 };
 
-template <int RX>
+template <int RX, int FMT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                     float* __restrict__ out, const float* __restrict__ scale, const float* __restrict__ rowscale,
-                    int M, int N, int K) {
-    using P = PairCfg<RX>;
+                    const float* __restrict__ zero, int gs, int M, int N, int K) {
+    using P = PairCfg<RX, FMT>;
     constexpr int kBK = P::kBK;
     constexpr int kSub = P::kSub;
     constexpr int kRowsX = P::kRowsX;
@@ -566,7 +749,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* xs = smem;                                  // S x kSub x [RX][64] f16, 128B swizzle
-    uint8_t* ws = smem + S * kXBytes;                    // S x [128][128] int8, 128B swizzle
+    uint8_t* ws = smem + S * kXBytes;                    // S x [128][kWRow] weight codes
     uint64_t* bars = reinterpret_cast<uint64_t*>(ws + S * kWBytes);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
 
@@ -595,7 +778,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
             mbar_init(full0 + 8 * s, 1);
             mbar_init(wfull0 + 8 * s, 1);
             mbar_init(release0 + 8 * s, 1);
-            mbar_init(afull0 + 8 * s, 2 * 4);  // four converter warps in each CTA
+            mbar_init(afull0 + 8 * s, 2 * 4 * kConvGroups);  // every converter warp of both CTAs
         }
         mbar_init(acc_full, 1);
         mbar_init(drain, 1);
@@ -627,7 +810,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
             const int first = num_kb < S ? num_kb : S;
             for (int kb = 0; kb < first; ++kb) {
                 mbar_arrive_expect_tx(wfull0 + 8 * kb, kWBytes);
-                tma_load_2d(smem_addr(ws + kb * kWBytes), &tmap_w, kb * kBK, n0, wfull0 + 8 * kb);
+                tma_load_2d(smem_addr(ws + kb * kWBytes), &tmap_w, kb * P::kWRow, n0, wfull0 + 8 * kb);
             }
             asm volatile("griddepcontrol.wait;" ::: "memory");
             for (int kb = 0; kb < num_kb; ++kb) {
@@ -641,7 +824,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
                 }
                 if (kb >= first) {
                     mbar_arrive_expect_tx(wfull0 + 8 * s, kWBytes);
-                    tma_load_2d(smem_addr(ws + s * kWBytes), &tmap_w, kb * kBK, n0, wfull0 + 8 * s);
+                    tma_load_2d(smem_addr(ws + s * kWBytes), &tmap_w, kb * P::kWRow, n0, wfull0 + 8 * s);
                 }
             }
             // Leave no copy of ours in flight: the weight tiles signal this CTA;
@@ -672,37 +855,41 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
             mma_commit_pair(drain, 0x3);
         }
     } else if (warp < kWarpEpi0) {
-        // Converters: thread owns weight row r of this CTA's 128 = tensor-memory lane r.
+        // Converters: thread owns weight row r of this CTA's 128 = tensor-memory
+        // lane r; both groups convert every k-block, group g its codes
+        // [64 g, 64 g + 64).
         const int quarter = warp & 3;
         const int group = (warp - kWarpConv0) >> 2;
         const int r = quarter * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
         const uint32_t afull_leader0 = mapa_shared(afull0, 0);
-        for (int kb = group; kb < num_kb; kb += kConvGroups) {
+        float pw = 1.0f;
+        if constexpr (FMT != kFmtChannel) {
+            pw = __int_as_float((group_row_exp<FMT>(scale, zero, n0 + r, N, K / gs) + 127) << 23);
+        }
+        // Group factors one k-block ahead, their loads overlapping this block's
+        // waits and conversion.
+        float f[2] = {}, zf[2] = {};
+        if constexpr (FMT != kFmtChannel) {
+            if (num_kb > 0) group_factors<FMT>(scale, zero, n0 + r, N, K, gs, 0, group, pw, f, zf);
+        }
+        for (int kb = 0; kb < num_kb; ++kb) {
             const int s = kb % S;
             const int a = s;
+            float fn[2] = {}, zn[2] = {};
+            if constexpr (FMT != kFmtChannel) {
+                if (kb + 1 < num_kb) group_factors<FMT>(scale, zero, n0 + r, N, K, gs, kb + 1, group, pw, fn, zn);
+            }
             bool ok = mbar_wait(wfull0 + 8 * s, (kb / S) & 1, err, 8u);
             if (ok && kb >= S) ok = mbar_wait_cluster(release0 + 8 * s, ((kb / S) - 1) & 1, err, 16u);
+            // tcgen05.st is warp-collective: leave together or not at all.
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
-            const uint8_t* row = ws + s * kWBytes + r * kBK;
+            convert_half<FMT>(ws + s * kWBytes, r, group, tmem + lane_addr + 2 * kRowsX + a * kACols, f, zf);
             #pragma unroll
-            for (int g = 0; g < kBK / 64; ++g) {
-                // 64 codes -> 32 f16x2 columns; 128B swizzle: chunk ^= r & 7.
-                uint32_t w[16];
-                #pragma unroll
-                for (int c4 = 0; c4 < 4; ++c4) {
-                    const int c = g * 4 + c4;
-                    const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) << 4));
-                    w[4 * c4 + 0] = v.x;
-                    w[4 * c4 + 1] = v.y;
-                    w[4 * c4 + 2] = v.z;
-                    w[4 * c4 + 3] = v.w;
-                }
-                uint32_t h[32];
-                #pragma unroll
-                for (int i = 0; i < 16; ++i) widen4_f16(w[i], h[2 * i], h[2 * i + 1]);
-                tmem_st_32x32b_x32(tmem + lane_addr + 2 * kRowsX + a * kACols + g * 32, h);
+            for (int q = 0; q < 2; ++q) {
+                f[q] = fn[q];
+                zf[q] = zn[q];
             }
             tmem_wait_st();
             tc_fence_before();
@@ -715,11 +902,19 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
         const int quarter = warp & 3;
         const int n = n0 + quarter * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        // Output scale of row n: scale[n], or 2^-e_n for a per-group format.
+        float sc = 0.0f;
+        if (n < N) {
+            if constexpr (FMT == kFmtChannel) {
+                sc = __ldg(scale + n);
+            } else {
+                sc = __int_as_float((127 - group_row_exp<FMT>(scale, zero, n, N, K / gs)) << 23);
+            }
+        }
         asm volatile("griddepcontrol.wait;" ::: "memory");  // row scales come from the prologue
         const bool ok = mbar_wait_cluster(acc_full, 0, err, 32u);
         if (__all_sync(0xffffffffu, ok)) {
             tc_fence_after();
-            const float sc = (n < N) ? __ldg(scale + n) : 0.0f;
             #pragma unroll 1
             for (int c0 = 0; c0 < 2 * kRowsX; c0 += 32) {
                 if (mp + c0 >= M) break;
@@ -797,16 +992,16 @@ cudaError_t scratch_pool(cudaMemPool_t* out) {
     return cudaSuccess;
 }
 
-bool g_attr_set[kMaxDevices][8] = {};
+bool g_attr_set[kMaxDevices][24] = {};  // [device][launch slot + 8 * weight format]
 
 // Cluster size for the split-K launch of a tile grid: the largest C in
 // {8, 4, 2} that keeps every CTA resident at once (tiles * C clusters' worth
 // of SMs, checked with the occupancy API) and leaves each rank >= 4 k-blocks;
 // 1 when the tiles alone already fill half the GPU.
-template <int BM>
+template <int BM, int FMT>
 int pick_splits(int slot, int64_t tiles, int64_t num_kb) {
-    using C = Cfg<BM>;
-    static int cache[kMaxDevices][3][4] = {};  // [dev][slot][log2 C - 1]: 0 unknown, 1 no, 2 yes
+    using C = Cfg<BM, FMT>;
+    static int cache[kMaxDevices][3][4] = {};  // [dev][slot][log2 C - 1]: 0 unknown, 1 no, 2 + clusters
     const int64_t sms = device_sm_count();
     if (tiles * 2 > sms) return 1;
     int dev = 0;
@@ -828,7 +1023,7 @@ int pick_splits(int slot, int64_t tiles, int64_t num_kb) {
             attr[0].val.clusterDim.z = 1;
             cfg.attrs = attr;
             cfg.numAttrs = 1;
-            if (cudaOccupancyMaxActiveClusters(&clusters, tc_gemm_kernel<BM>, &cfg) != cudaSuccess) {
+            if (cudaOccupancyMaxActiveClusters(&clusters, tc_gemm_kernel<BM, FMT>, &cfg) != cudaSuccess) {
                 cudaGetLastError();
                 clusters = 0;
             }
@@ -841,19 +1036,21 @@ int pick_splits(int slot, int64_t tiles, int64_t num_kb) {
     return 1;
 }
 
-template <int BM>
+template <int BM, int FMT>
 popcornStatus_t launch_gemm(int slot, const CUtensorMap& tx, const CUtensorMap& tw, float* out, const float* scale,
-                            const float* rowscale, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
-    using C = Cfg<BM>;
+                            const float* rowscale, const float* zero, int gs, int64_t M, int64_t N, int64_t K,
+                            cudaStream_t stream) {
+    using C = Cfg<BM, FMT>;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < kMaxDevices && !g_attr_set[dev][slot]) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BM>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    if (dev >= 0 && dev < kMaxDevices && !g_attr_set[dev][slot + 8 * FMT]) {
+        cudaError_t e =
+            cudaFuncSetAttribute(tc_gemm_kernel<BM, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
         if (e != cudaSuccess) return record_cuda(e);
-        g_attr_set[dev][slot] = true;
+        g_attr_set[dev][slot + 8 * FMT] = true;
     }
     const int64_t tiles = ceil_div(N, kTileN);
-    const int splits = pick_splits<BM>(slot, tiles, ceil_div(K, C::kBK));
+    const int splits = pick_splits<BM, FMT>(slot, tiles, ceil_div(K, C::kBK));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(tiles * splits));
     cfg.blockDim = dim3(kThreads);
@@ -868,7 +1065,7 @@ popcornStatus_t launch_gemm(int slot, const CUtensorMap& tx, const CUtensorMap& 
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = splits > 1 ? 2 : 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BM>, tx, tw, out, scale, rowscale,
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BM, FMT>, tx, tw, out, scale, rowscale, zero, gs,
                                              static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), splits);
     if (e != cudaSuccess) return record_cuda(e);
     return check_launch();
@@ -882,39 +1079,41 @@ int pick_bm(int64_t M) {
 }
 
 // Tensor maps of one call: x16 [M, K] f16 in [xrows x 64] boxes (128B
-// swizzle), qweight [N, K] int8 in [128 x bk] boxes (bk = 64: 64B swizzle,
-// bk = 128: 128B swizzle).
-bool make_maps(PFN_cuTensorMapEncodeTiled_v12000 encode, __half* x16, const int8_t* q, int64_t M, int64_t N,
-               int64_t K, int xrows, int bk, CUtensorMap* tx, CUtensorMap* tw) {
+// swizzle), weight codes [N, wcols] bytes (wcols = K for int8, K / 2 for
+// packed int4) in [128 x bk] boxes (bk = 64: 64B swizzle, bk = 128: 128B
+// swizzle).
+bool make_maps(PFN_cuTensorMapEncodeTiled_v12000 encode, __half* x16, const void* q, int64_t M, int64_t N,
+               int64_t K, int64_t wcols, int xrows, int bk, CUtensorMap* tx, CUtensorMap* tw) {
     const int bm = xrows;
     const cuuint64_t xdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
     const cuuint64_t xstride[1] = {static_cast<cuuint64_t>(K) * 2};
     const cuuint32_t xbox[2] = {64, static_cast<cuuint32_t>(bm)};
-    const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
-    const cuuint64_t wstride[1] = {static_cast<cuuint64_t>(K)};
+    const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(wcols), static_cast<cuuint64_t>(N)};
+    const cuuint64_t wstride[1] = {static_cast<cuuint64_t>(wcols)};
     const cuuint32_t wbox[2] = {static_cast<cuuint32_t>(bk), kTileN};
     const cuuint32_t estride[2] = {1, 1};
     CUresult r1 = encode(tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, xdims, xstride, xbox, estride,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    CUresult r2 = encode(tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q), wdims, wstride, wbox, estride,
+    CUresult r2 = encode(tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(q), wdims, wstride, wbox, estride,
                          CU_TENSOR_MAP_INTERLEAVE_NONE,
                          bk == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r1 == CUDA_SUCCESS && r2 == CUDA_SUCCESS;
 }
 
-template <int RX>
+template <int RX, int FMT>
 popcornStatus_t launch_pair(int slot, const CUtensorMap& tx, const CUtensorMap& tw, float* out, const float* scale,
-                            const float* rowscale, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
-    using P = PairCfg<RX>;
+                            const float* rowscale, const float* zero, int gs, int64_t M, int64_t N, int64_t K,
+                            cudaStream_t stream) {
+    using P = PairCfg<RX, FMT>;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < kMaxDevices && !g_attr_set[dev][slot]) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_pair_kernel<RX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             P::kSmem);
+    if (dev >= 0 && dev < kMaxDevices && !g_attr_set[dev][slot + 8 * FMT]) {
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_pair_kernel<RX, FMT>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, P::kSmem);
         if (e != cudaSuccess) return record_cuda(e);
-        g_attr_set[dev][slot] = true;
+        g_attr_set[dev][slot + 8 * FMT] = true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(2 * ceil_div(N, 2 * kTileN)), static_cast<unsigned>(ceil_div(M, 2 * RX)));
@@ -926,8 +1125,8 @@ popcornStatus_t launch_pair(int slot, const CUtensorMap& tx, const CUtensorMap& 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<RX>, tx, tw, out, scale, rowscale,
-                                             static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<RX, FMT>, tx, tw, out, scale, rowscale, zero,
+                                             gs, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
     if (e != cudaSuccess) return record_cuda(e);
     return check_launch();
 }
@@ -935,44 +1134,39 @@ popcornStatus_t launch_pair(int slot, const CUtensorMap& tx, const CUtensorMap& 
 // The GEMM launch of the tensor path once x16 and rowscale are in place:
 // CTA pairs (256 x 256 tiles) for M > 128, single CTAs with BM activation
 // rows otherwise.
+template <int FMT>
 popcornStatus_t launch_tc_gemm(PFN_cuTensorMapEncodeTiled_v12000 encode, __half* x16, const float* rowscale,
-                               float* out, const int8_t* q, const float* scale, int64_t M, int64_t N, int64_t K,
-                               cudaStream_t stream) {
+                               float* out, const void* q, const float* scale, const float* zero, int gs, int64_t M,
+                               int64_t N, int64_t K, cudaStream_t stream) {
     const int bm = pick_bm(M);
+    const int64_t wcols = FMT == kFmtGroup4 ? K / 2 : K;
+    const int bk = FMT == kFmtGroup4 ? 64 : 128;
     CUtensorMap tx, tw;
     // CTA pairs: always for M > 128; for smaller M when there are more
     // 128-row weight tiles than half the SMs (the single-CTA kernel with
     // cluster split-K serves the rest).
     if (bm >= 256 || ceil_div(N, kTileN) * 2 > device_sm_count()) {
         const int rx = bm / 2;
-        if (!make_maps(encode, x16, q, M, N, K, rx, 128, &tx, &tw)) return POPCORN_ERROR_INVALID_VALUE;
+        if (!make_maps(encode, x16, q, M, N, K, wcols, rx, bk, &tx, &tw)) return POPCORN_ERROR_INVALID_VALUE;
         switch (rx) {
-            case 16: return launch_pair<16>(4, tx, tw, out, scale, rowscale, M, N, K, stream);
-            case 32: return launch_pair<32>(5, tx, tw, out, scale, rowscale, M, N, K, stream);
-            case 64: return launch_pair<64>(6, tx, tw, out, scale, rowscale, M, N, K, stream);
-            default: return launch_pair<128>(7, tx, tw, out, scale, rowscale, M, N, K, stream);
+            case 16: return launch_pair<16, FMT>(4, tx, tw, out, scale, rowscale, zero, gs, M, N, K, stream);
+            case 32: return launch_pair<32, FMT>(5, tx, tw, out, scale, rowscale, zero, gs, M, N, K, stream);
+            case 64: return launch_pair<64, FMT>(6, tx, tw, out, scale, rowscale, zero, gs, M, N, K, stream);
+            default: return launch_pair<128, FMT>(7, tx, tw, out, scale, rowscale, zero, gs, M, N, K, stream);
         }
     }
-    if (!make_maps(encode, x16, q, M, N, K, bm, 128, &tx, &tw)) return POPCORN_ERROR_INVALID_VALUE;
+    if (!make_maps(encode, x16, q, M, N, K, wcols, bm, bk, &tx, &tw)) return POPCORN_ERROR_INVALID_VALUE;
     switch (bm) {
-        case 32: return launch_gemm<32>(0, tx, tw, out, scale, rowscale, M, N, K, stream);
-        case 64: return launch_gemm<64>(1, tx, tw, out, scale, rowscale, M, N, K, stream);
-        default: return launch_gemm<128>(2, tx, tw, out, scale, rowscale, M, N, K, stream);
+        case 32: return launch_gemm<32, FMT>(0, tx, tw, out, scale, rowscale, zero, gs, M, N, K, stream);
+        case 64: return launch_gemm<64, FMT>(1, tx, tw, out, scale, rowscale, zero, gs, M, N, K, stream);
+        default: return launch_gemm<128, FMT>(2, tx, tw, out, scale, rowscale, zero, gs, M, N, K, stream);
     }
 }
 
-}  // namespace
-
-bool tc_supported(const float*, const int8_t* q, int64_t M, int64_t N, int64_t K) {
-    // TMA: 16-byte aligned weight base and row pitch; int32 tile coordinates.
-    return (K % 16 == 0) && aligned16(q) && M <= INT32_MAX && N <= INT32_MAX && K <= INT32_MAX &&
-           M * K <= (int64_t(1) << 40) && encode_fn() != nullptr;
-}
-
-int tc_launch_count(int64_t, int64_t, int64_t) { return 2; }
-
-popcornStatus_t tc_dequant_matmul(float* out, const float* x, const int8_t* q, const float* scale, int64_t M,
-                                  int64_t N, int64_t K, cudaStream_t stream) {
+// x -> f16 prologue into stream-ordered scratch, then the GEMM.
+template <int FMT>
+popcornStatus_t tc_run(float* out, const float* x, const void* q, const float* scale, const float* zero, int gs,
+                       int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
     PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
     if (encode == nullptr) return POPCORN_ERROR_INVALID_VALUE;
 
@@ -989,11 +1183,41 @@ popcornStatus_t tc_dequant_matmul(float* out, const float* x, const int8_t* q, c
     float* rowscale = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + x16_bytes);
 
     popcornStatus_t st = launch_x_to_f16(x16, rowscale, x, M, K, stream);
-
-    if (st == POPCORN_SUCCESS) st = launch_tc_gemm(encode, x16, rowscale, out, q, scale, M, N, K, stream);
+    if (st == POPCORN_SUCCESS) st = launch_tc_gemm<FMT>(encode, x16, rowscale, out, q, scale, zero, gs, M, N, K, stream);
     e = cudaFreeAsync(scratch, stream);
     if (st == POPCORN_SUCCESS && e != cudaSuccess) st = record_cuda(e);
     return st;
+}
+
+}  // namespace
+
+bool tc_supported(const float*, const int8_t* q, int64_t M, int64_t N, int64_t K) {
+    // TMA: 16-byte aligned weight base and row pitch; int32 tile coordinates.
+    return (K % 16 == 0) && aligned16(q) && M <= INT32_MAX && N <= INT32_MAX && K <= INT32_MAX &&
+           M * K <= (int64_t(1) << 40) && encode_fn() != nullptr;
+}
+
+int tc_launch_count(int64_t, int64_t, int64_t) { return 2; }
+
+popcornStatus_t tc_dequant_matmul(float* out, const float* x, const int8_t* q, const float* scale, int64_t M,
+                                  int64_t N, int64_t K, cudaStream_t stream) {
+    return tc_run<kFmtChannel>(out, x, q, scale, nullptr, 0, M, N, K, stream);
+}
+
+bool tc_grouped_supported(const void* q, int64_t M, int64_t N, int64_t K, int64_t gs) {
+    // Group factors are taken per 32 codes; 16-byte aligned base and row
+    // pitch for TMA (K % 32 == 0 follows from gs % 32 == 0 and gs | K).
+    return gs % 32 == 0 && K % gs == 0 && aligned16(q) && M <= INT32_MAX && N <= INT32_MAX && K <= INT32_MAX &&
+           M * K <= (int64_t(1) << 40) && encode_fn() != nullptr;
+}
+
+popcornStatus_t tc_dequant_matmul_grouped(WeightFormat fmt, float* out, const float* x, const void* q,
+                                          const float* scale, const float* zero, int64_t M, int64_t N, int64_t K,
+                                          int64_t gs, cudaStream_t stream) {
+    if (fmt == kFmtGroup4) {
+        return tc_run<kFmtGroup4>(out, x, q, scale, zero, static_cast<int>(gs), M, N, K, stream);
+    }
+    return tc_run<kFmtGroup8>(out, x, q, scale, nullptr, static_cast<int>(gs), M, N, K, stream);
 }
 
 }  // namespace pcb
@@ -1076,7 +1300,7 @@ extern "C" popcornStatus_t popcornDequantizeMatmulNoAlloc_i8f32(float* out, cons
     popcornStatus_t st = launch_x_to_f16(x16, rowscale, x, M, K, stream);
     if (st != POPCORN_SUCCESS) return st;
 
-    return launch_tc_gemm(encode, x16, rowscale, out, qweight, scale, M, N, K, stream);
+    return launch_tc_gemm<kFmtChannel>(encode, x16, rowscale, out, qweight, scale, nullptr, 0, M, N, K, stream);
 }
 
 namespace pcb {

@@ -166,3 +166,49 @@ def test_quantize_reference_fixture(cuda, golden):
     # can differ only on exact .5 quotients
     diff = q.cpu().numpy().astype(np.int32) - golden["qg_basic/codes_test_loop"].astype(np.int32)
     assert np.all(np.abs(diff) <= 1)
+
+
+# ---------------------------------------------------------------------------
+# Tensor-core path (M > 4, >= 2^27 multiply-adds, group size % 32 == 0): codes
+# times group scale (normalised per row by a power of two) enter the tensor
+# cores as f16, activations as f16 after a per-row power of two.
+# ---------------------------------------------------------------------------
+TC_SHAPES = [
+    (8, 4096, 4096, 128),     # single-CTA kernel, cluster split-K
+    (32, 11008, 4096, 128),   # CTA pairs, 16 activation rows per CTA
+    (64, 4096, 4096, 32),     # four groups per k-block
+    (100, 2000, 4096, 64),    # M and N tails
+    (256, 4096, 4096, 128),   # CTA pairs, 128 activation rows per CTA
+    (300, 1000, 2048, 256),
+    (16, 4096, 4096, 4096),   # one group per row
+    (5, 8192, 4096, 512),
+]
+
+
+@pytest.mark.parametrize("shape", TC_SHAPES)
+def test_tensor_path_matches_oracle(cuda, shape):
+    import torch
+
+    M, N, K, gs = shape
+    x, q, s = _case(M, N, K, gs, 7 * M + N)
+    got = _grouped(torch, cuda, x, q, s, gs)
+    ref = oracle.dequant_matmul_grouped(x, q, s, gs, fused=True, threads=8)
+    err = oracle.normwise_rel_err(got, ref)
+    assert err <= 1e-3, err   # bar: 2e-3
+
+
+@pytest.mark.parametrize("magnitude", [1e-30, 1e30])
+def test_tensor_path_extreme_scales(cuda, magnitude):
+    # Rows whose scales differ by many orders of magnitude: each row is
+    # normalised by its own power of two before f16.
+    import torch
+
+    M, N, K, gs = 16, 2048, 4096, 128
+    x, q, s = _case(M, N, K, gs, 99)
+    s = s.copy()
+    s[::2] *= np.float32(magnitude)
+    s[1::4] *= np.float32(1e-6 if magnitude > 1 else 1e6)
+    got = _grouped(torch, cuda, x, q, s, gs)
+    ref = oracle.dequant_matmul_grouped(x, q, s, gs, fused=True, threads=8)
+    for rows in (slice(0, None, 2), slice(1, None, 4), slice(3, None, 4)):
+        assert oracle.normwise_rel_err(got[:, rows], ref[:, rows]) <= 1e-3

@@ -239,3 +239,49 @@ def test_quantize_then_matmul(cuda):
     # (0.085 normwise for these inputs on the oracle)
     exact = x.astype(np.float64) @ w.astype(np.float64).T
     assert oracle.normwise_rel_err(out.cpu().numpy(), exact) <= 0.15
+
+
+# ---------------------------------------------------------------------------
+# Tensor-core path (M > 4, >= 2^27 multiply-adds, group size % 32 == 0): the
+# converters unpack the nibbles and write (code - zero) * scale, normalised per
+# row by a power of two, to tensor memory as f16.
+# ---------------------------------------------------------------------------
+TC_SHAPES = [
+    (8, 4096, 4096, 128),
+    (32, 11008, 4096, 128),
+    (64, 4096, 4096, 32),
+    (100, 2000, 4096, 64),
+    (256, 4096, 4096, 128),
+    (300, 1000, 2048, 256),
+    (16, 4096, 4096, 4096),
+    (5, 8192, 4096, 512),
+]
+
+
+@pytest.mark.parametrize("shape", TC_SHAPES)
+def test_tensor_path_matches_oracle(cuda, shape):
+    import torch
+
+    M, N, K, gs = shape
+    x, q, s, z = _case(M, N, K, gs, 7 * M + N)
+    got = _matmul(torch, cuda, x, q, s, z, gs)
+    ref = oracle.dequant_matmul_grouped_i4(x, q, s, z, gs, fused=True, threads=8)
+    err = oracle.normwise_rel_err(got, ref)
+    assert err <= 1e-3, err   # bar: 2e-3
+
+
+def test_tensor_path_off_centre_and_extreme(cuda):
+    import torch
+
+    M, N, K, gs = 24, 2048, 4096, 64
+    x = oracle.fill_normal(M * K, 5, 1.0).reshape(M, K)
+    w = np.abs(oracle.fill_normal(N * K, 6, 0.02)).reshape(N, K) + np.float32(0.05)
+    w[::2] *= -1.0
+    q, s, z = oracle.quantize_grouped_i4(w, gs)
+    s = s.copy()
+    s[::3] *= np.float32(1e-25)
+    s[1::3] *= np.float32(1e25)
+    got = _matmul(torch, cuda, x, q, s, z, gs)
+    ref = oracle.dequant_matmul_grouped_i4(x, q, s, z, gs, fused=True, threads=8)
+    for rows in (slice(0, None, 3), slice(1, None, 3), slice(2, None, 3)):
+        assert oracle.normwise_rel_err(got[:, rows], ref[:, rows]) <= 1e-3
