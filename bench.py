@@ -51,6 +51,11 @@ WORKLOADS = {
     # The same two formats at prefill size (tensor cores, group factors in the converters).
     "grouped_prefill": dict(M=2048, K=4096, N=4096, unit="TFLOP/s", bound="tensor", group_size=128),
     "int4_prefill": dict(M=2048, K=4096, N=4096, unit="TFLOP/s", bound="tensor", group_size=128, bits=4),
+    # Front of a gated MLP at decode size (7B shapes): RMSNorm -> gate and up
+    # projections 4096 -> 11008 -> SiLU(gate) * up, in one fused call
+    # (popcornRMSNormDequantizeMatmulSiluMul_i8f32); algorithmic bytes = both
+    # int8 weight matrices. The unfused sequence is timed beside it.
+    "mlp_decode": dict(M=1, K=4096, N=11008, unit="GB/s", bound="hbm", mlp=True),
 }
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of
@@ -72,7 +77,8 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
-    p.add_argument("--extras", default="skinny,prefill,grouped_decode,int4_decode,grouped_prefill,int4_prefill",
+    p.add_argument("--extras", default="skinny,prefill,grouped_decode,int4_decode,grouped_prefill,int4_prefill,"
+                                       "mlp_decode",
                    help="comma-separated extra single-GPU workloads reported beside the headline (N=1 only)")
     p.add_argument("--stack", default="1,128",
                    help="M values of the 32-layer 7B-shaped linear stack timed at every N ('none' to skip)")
@@ -279,6 +285,58 @@ class Setup:
                                                       self.M, self.Nl, self.K)]
 
 
+class MlpSetup:
+    """RMSNorm -> gate and up projections -> SiLU(gate) * up at decode size,
+    either as one fused call or as the unfused sequence (torch RMSNorm, two
+    popcornDequantizeMatmul_i8f32 calls, torch SiLU and multiply)."""
+
+    EPS = 1e-5
+
+    def __init__(self, torch, pc, wl, device, pool_bytes, fused=True):
+        M, K, N = wl["M"], wl["K"], wl["N"]
+        self.torch, self.M, self.K, self.N, self.fused = torch, M, K, N, fused
+        self.sets = max(2, math.ceil(pool_bytes / (2 * N * K)))
+        g = torch.Generator(device=device)
+        g.manual_seed(4321)
+        self.qg, self.sg, self.qu, self.su = [], [], [], []
+        for _ in range(self.sets):
+            for qs, ss in ((self.qg, self.sg), (self.qu, self.su)):
+                w = torch.randn((N, K), generator=g, device=device) * 0.02
+                q, sc = pc.quantize(w)
+                del w
+                qs.append(q)
+                ss.append(sc)
+        self.x = torch.randn((M, K), generator=g, device=device)
+        self.nw = 1.0 + 0.1 * torch.randn((K,), generator=g, device=device)
+        self.out = torch.empty((M, N), dtype=torch.float32, device=device)
+        self.u = torch.empty_like(self.out)
+        self.xn = torch.empty_like(self.x)
+        self.lib = pc.load_library()
+        torch.cuda.synchronize()
+
+    def step(self, i, stream_handle, group=None):
+        j = i % self.sets
+        lib, torch = self.lib, self.torch
+        if self.fused:
+            st = lib.popcornRMSNormDequantizeMatmulSiluMul_i8f32(
+                self.out.data_ptr(), self.x.data_ptr(), self.nw.data_ptr(), self.EPS, self.qg[j].data_ptr(),
+                self.sg[j].data_ptr(), self.qu[j].data_ptr(), self.su[j].data_ptr(), self.M, self.N, self.K,
+                stream_handle)
+            if st != 0:
+                raise RuntimeError(f"fused MLP call failed: {st}")
+            return
+        torch.mul(self.x * torch.rsqrt(self.x.pow(2).mean(-1, keepdim=True) + self.EPS), self.nw, out=self.xn)
+        for dst, q, sc in ((self.out, self.qg[j], self.sg[j]), (self.u, self.qu[j], self.su[j])):
+            st = lib.popcornDequantizeMatmul_i8f32(dst.data_ptr(), self.xn.data_ptr(), q.data_ptr(), sc.data_ptr(),
+                                                   self.M, self.N, self.K, stream_handle)
+            if st != 0:
+                raise RuntimeError(f"dequant-matmul call failed: {st}")
+        torch.mul(torch.nn.functional.silu(self.out), self.u, out=self.out)
+
+    def path(self):
+        return "fused rmsnorm + gate/up + silu*mul" if self.fused else "unfused sequence"
+
+
 def time_graph(torch, setup, steps, warmup, soak_s, sampler, dist_on):
     """Warm up, soak, then time exactly `steps` steps from one CUDA graph."""
     stream = torch.cuda.Stream()
@@ -391,6 +449,8 @@ def max_over_ranks(torch, value, dist_on, device):
 def weight_bytes(wl):
     """Algorithmic bytes of one call: the codes (int8, or int4 packed two per
     byte), plus the scales (and int4 zero points) of a grouped layout."""
+    if wl.get("mlp"):
+        return 2 * wl["N"] * wl["K"]
     gs = wl.get("group_size")
     bits = wl.get("bits", 8)
     params = (4 if bits == 8 else 8) * wl["N"] * (wl["K"] // gs) if gs else 0
@@ -613,7 +673,8 @@ def run_ours(args):
         extras = {}
         for name in [e for e in args.extras.split(",") if e in WORKLOADS and e != args.workload]:
             ewl = WORKLOADS[name]
-            es = Setup(torch, pc, ewl, 0, 1, device, pool)
+            es = MlpSetup(torch, pc, ewl, device, pool) if ewl.get("mlp") else Setup(torch, pc, ewl, 0, 1, device,
+                                                                                       pool)
             esteps = 200 if ewl["bound"] == "hbm" else 20
             ems, _ = time_graph(torch, es, esteps, 3, 0.0, None, False)
             eval_ = throughput(ewl, ems / esteps)
@@ -622,6 +683,12 @@ def run_ours(args):
                             "ms_per_step": round(ems / esteps, 6),
                             "roofline": roofline(ewl, ems / esteps, peaks, name)}
             del es
+            if ewl.get("mlp"):
+                eu = MlpSetup(torch, pc, ewl, device, pool, fused=False)
+                ums, _ = time_graph(torch, eu, esteps, 3, 0.0, None, False)
+                extras[name]["unfused_ms_per_step"] = round(ums / esteps, 6)
+                extras[name]["unfused"] = "torch RMSNorm + 2 x popcornDequantizeMatmul_i8f32 + torch silu * up"
+                del eu
             torch.cuda.empty_cache()
         if extras:
             line["extra_workloads"] = extras

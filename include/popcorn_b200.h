@@ -124,6 +124,69 @@ popcornStatus_t popcornDequantizeMatmulNoAlloc_i8f32(
  * the results of that launch are not valid. */
 int popcornB200DeviceErrors(unsigned int* flags);
 
+/*
+ * Fused neighbours of the dequant-matmul in a transformer block: the same
+ * results as the popcorn call sequences named below, in one pass over the
+ * activations and without the intermediate tensors. Arithmetic: popcorn's
+ * RMSNorm (src/reduction.cu:290-321: rms = sqrtf(sum(x^2) / K + eps),
+ * x * (1 / rms) * norm_weight[k], norm_weight may be NULL) and SiLU
+ * (src/unary.cu:76-81: g / (1 + expf(-g))); only the order of the sum of
+ * squares and of the k-sum differ, so results agree with the sequence to f32
+ * rounding (f32 path) or ~4e-4 normwise (tensor path, large M). Null
+ * buffers other than norm_weight -> POPCORN_ERROR_INVALID_VALUE; any size
+ * <= 0 -> no-op. Small problems, unaligned operands and K % 16 != 0 run the
+ * unfused sequence inside the library (with stream-ordered scratch from its
+ * pool).
+ */
+
+/* out = DequantizeMatmul(RMSNorm(x; norm_weight, eps), qweight, scale):
+ * popcornRMSNorm_f32 followed by popcornDequantizeMatmul_i8f32. */
+popcornStatus_t popcornRMSNormDequantizeMatmul_i8f32(
+    float* out,
+    const float* x,
+    const float* norm_weight,
+    float eps,
+    const int8_t* qweight,
+    const float* scale,
+    int64_t M,
+    int64_t N,
+    int64_t K,
+    cudaStream_t stream
+);
+
+/* out = silu(x @ (q_gate * s_gate)^T) * (x @ (q_up * s_up)^T): two
+ * popcornDequantizeMatmul_i8f32 calls, popcornSilu_f32 on the first result,
+ * popcornMul_f32 of the two. q_gate/q_up are [N, K], s_gate/s_up [N]. */
+popcornStatus_t popcornDequantizeMatmulSiluMul_i8f32(
+    float* out,
+    const float* x,
+    const int8_t* q_gate,
+    const float* s_gate,
+    const int8_t* q_up,
+    const float* s_up,
+    int64_t M,
+    int64_t N,
+    int64_t K,
+    cudaStream_t stream
+);
+
+/* Both: out = silu(RMSNorm(x) @ W_gate^T) * (RMSNorm(x) @ W_up^T), the front
+ * half of a gated MLP block. */
+popcornStatus_t popcornRMSNormDequantizeMatmulSiluMul_i8f32(
+    float* out,
+    const float* x,
+    const float* norm_weight,
+    float eps,
+    const int8_t* q_gate,
+    const float* s_gate,
+    const int8_t* q_up,
+    const float* s_up,
+    int64_t M,
+    int64_t N,
+    int64_t K,
+    cudaStream_t stream
+);
+
 #ifdef __cplusplus
 }
 #endif

@@ -50,7 +50,9 @@ def _load():
         lib.oracle_quantize_grouped_i8.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _int]
         lib.oracle_dequant_matmul_grouped_i4.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int]
         lib.oracle_quantize_grouped_i4.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int]
-        for f in (lib.oracle_dequant_matmul_i8, lib.oracle_dequant_matmul_i8_mt, lib.oracle_quantize_i8,
+        lib.oracle_rmsnorm.argtypes = [_vp, _vp, _vp, _i64, _i64, ctypes.c_float, _int]
+        lib.oracle_silu.argtypes = [_vp, _vp, _i64]
+        for f in (lib.oracle_rmsnorm, lib.oracle_silu, lib.oracle_dequant_matmul_i8, lib.oracle_dequant_matmul_i8_mt, lib.oracle_quantize_i8,
                   lib.oracle_dequantize_i8, lib.oracle_fill_normal, lib.oracle_dequant_matmul_grouped_i8,
                   lib.oracle_quantize_grouped_i8, lib.oracle_dequant_matmul_grouped_i4,
                   lib.oracle_quantize_grouped_i4):
@@ -154,6 +156,24 @@ def quantize_grouped_i4(w, group_size: int, test_loop: bool = False):
     z = np.empty((N, K // group_size), dtype=np.float32)
     _load().oracle_quantize_grouped_i4(_ptr(q), _ptr(s), _ptr(z), _ptr(w), N, K, group_size, int(test_loop))
     return q, s, z
+
+
+def rmsnorm(x, weight=None, eps: float = 1e-5, fused: bool = True) -> np.ndarray:
+    """popcorn's RMSNorm of the rows of x (weight may be None); fused: its GPU kernel's fmaf sum."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, K = x.shape
+    out = np.empty_like(x)
+    w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
+    _load().oracle_rmsnorm(_ptr(out), _ptr(x), None if w is None else _ptr(w), rows, K, eps, int(fused))
+    return out
+
+
+def silu(x) -> np.ndarray:
+    """popcorn's SiLU, x / (1 + expf(-x)), with the host's expf."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    _load().oracle_silu(_ptr(out), _ptr(x), x.size)
+    return out
 
 
 def dequantize(q, scale) -> np.ndarray:
@@ -292,5 +312,11 @@ def popcorn_ref_gpu():
         lib.popcornDequantizeMatmulGrouped_i4f32.restype = _int
         lib.popcornQuantizeGrouped_f32i4.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]
         lib.popcornQuantizeGrouped_f32i4.restype = _int
+        lib.popcornRMSNorm_f32.argtypes = [_vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]
+        lib.popcornRMSNorm_f32.restype = _int
+        lib.popcornSilu_f32.argtypes = [_vp, _vp, _i64, _vp]
+        lib.popcornSilu_f32.restype = _int
+        lib.popcornMul_f32.argtypes = [_vp, _vp, _vp, _i64, _vp]
+        lib.popcornMul_f32.restype = _int
         _ref_gpu = lib
     return _ref_gpu

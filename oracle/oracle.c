@@ -351,6 +351,34 @@ void oracle_quantize_grouped_i4(uint8_t* out, float* scale, float* zero, const f
     }
 }
 
+void oracle_rmsnorm(float* out, const float* in, const float* weight, int64_t rows, int64_t K, float eps, int fused) {
+    for (int64_t r = 0; r < rows; r++) {
+        const float* x = in + r * K;
+        float* o = out + r * K;
+        /* src/reduction.cu:303-313 */
+        float sum_sq = 0.0f;
+        for (int64_t k = 0; k < K; k++) {
+            if (fused) {
+                sum_sq = fmaf(x[k], x[k], sum_sq);
+            } else {
+                const float p = x[k] * x[k];
+                sum_sq = sum_sq + p;
+            }
+        }
+        const float rms = sqrtf(sum_sq / (float)K + eps);
+        const float inv = 1.0f / rms;
+        for (int64_t k = 0; k < K; k++) {
+            float v = x[k] * inv;
+            if (weight != NULL) v = v * weight[k];
+            o[k] = v;
+        }
+    }
+}
+
+void oracle_silu(float* out, const float* in, int64_t n) {
+    for (int64_t i = 0; i < n; i++) out[i] = in[i] / (1.0f + expf(-in[i]));
+}
+
 void oracle_dequantize_i8(float* out, const int8_t* q, const float* scale, int64_t N, int64_t K) {
     for (int64_t n = 0; n < N; n++) {
         const float sc = scale[n];

@@ -72,6 +72,16 @@ void oracle_dequant_matmul_grouped_i4(float* out, const float* x, const uint8_t*
 void oracle_quantize_grouped_i4(uint8_t* out, float* scale, float* zero, const float* in, int64_t N, int64_t K,
                                 int64_t gs, int variant);
 
+/* popcorn's RMSNorm (src/reduction.cu:290-321, one thread per row): the row's
+ * sum of squares in k order (fused = 1: fmaf, as nvcc contracts
+ * `sum_sq += x * x` in that kernel; fused = 0: product and sum rounded
+ * separately), rms = sqrtf(sum / K + eps), inv = 1 / rms, then
+ * out = (x * inv) * weight[k] (weight may be NULL: no scaling). */
+void oracle_rmsnorm(float* out, const float* in, const float* weight, int64_t rows, int64_t K, float eps, int fused);
+
+/* popcorn's SiLU (src/unary.cu:76-81): x / (1 + expf(-x)), with the host's expf. */
+void oracle_silu(float* out, const float* in, int64_t n);
+
 /* out[n,k] = (float)q[n,k] * scale[n]. */
 void oracle_dequantize_i8(float* out, const int8_t* q, const float* scale, int64_t N, int64_t K);
 

@@ -55,6 +55,9 @@ EXT_SYMBOLS = (
     "popcornDequantizeMatmulNoAlloc_i8f32",
     "popcornDequantizeMatmulAllGather_i8f32",
     "popcornDequantizeMatmulAllReduce_i8f32",
+    "popcornRMSNormDequantizeMatmul_i8f32",
+    "popcornDequantizeMatmulSiluMul_i8f32",
+    "popcornRMSNormDequantizeMatmulSiluMul_i8f32",
 )
 
 TP_MAX_RANKS = 8
@@ -94,6 +97,10 @@ _SIGNATURES = {
     "popcornDequantizeMatmulNoAlloc_i8f32": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "popcornDequantizeMatmulAllGather_i8f32": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp]),
     "popcornDequantizeMatmulAllReduce_i8f32": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "popcornRMSNormDequantizeMatmul_i8f32": (_int, [_vp, _vp, _vp, ctypes.c_float, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "popcornDequantizeMatmulSiluMul_i8f32": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "popcornRMSNormDequantizeMatmulSiluMul_i8f32": (_int, [_vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp, _vp, _i64,
+                                                           _i64, _i64, _vp]),
 }
 
 _lib = None
@@ -320,6 +327,48 @@ def dequantize_matmul_grouped_i4(x, qweight, scale, zero, group_size: int, out=N
     _check(popcornDequantizeMatmulGrouped_i4f32(out.data_ptr(), x.data_ptr(), qweight.data_ptr(), scale.data_ptr(),
                                                 zero.data_ptr(), M, N, K, group_size, st),
            "popcornDequantizeMatmulGrouped_i4f32")
+    return out
+
+
+def _ptr_or_null(t):
+    return None if t is None else t.data_ptr()
+
+
+def rmsnorm_dequantize_matmul(x, norm_weight, eps: float, qweight, scale, out=None, stream=None):
+    """out[M, N] = RMSNorm(x; norm_weight, eps) @ (qweight * scale[:, None]).T (norm_weight may be None)."""
+    import torch
+
+    M, K = x.shape
+    N = qweight.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    st = _stream_handle(stream)
+    _check(load_library().popcornRMSNormDequantizeMatmul_i8f32(out.data_ptr(), x.data_ptr(), _ptr_or_null(norm_weight),
+                                                              eps, qweight.data_ptr(), scale.data_ptr(), M, N, K, st),
+           "popcornRMSNormDequantizeMatmul_i8f32")
+    return out
+
+
+def dequantize_matmul_silu_mul(x, q_gate, s_gate, q_up, s_up, norm_weight=None, eps=None, out=None, stream=None):
+    """out[M, N] = silu(x' @ W_gate.T) * (x' @ W_up.T) with x' = x, or RMSNorm(x; norm_weight, eps)
+    when eps is given (norm_weight may then be None)."""
+    import torch
+
+    M, K = x.shape
+    N = q_gate.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    st = _stream_handle(stream)
+    lib = load_library()
+    if eps is None:
+        _check(lib.popcornDequantizeMatmulSiluMul_i8f32(out.data_ptr(), x.data_ptr(), q_gate.data_ptr(),
+                                                        s_gate.data_ptr(), q_up.data_ptr(), s_up.data_ptr(), M, N, K,
+                                                        st), "popcornDequantizeMatmulSiluMul_i8f32")
+    else:
+        _check(lib.popcornRMSNormDequantizeMatmulSiluMul_i8f32(out.data_ptr(), x.data_ptr(), _ptr_or_null(norm_weight),
+                                                               eps, q_gate.data_ptr(), s_gate.data_ptr(),
+                                                               q_up.data_ptr(), s_up.data_ptr(), M, N, K, st),
+               "popcornRMSNormDequantizeMatmulSiluMul_i8f32")
     return out
 
 

@@ -114,6 +114,17 @@ popcornStatus_t tc_dequant_matmul(float* out, const float* x, const int8_t* q,
                                   int64_t K, cudaStream_t stream);
 int tc_launch_count(int64_t M, int64_t N, int64_t K);
 
+// tcgen05 path with the activation-side RMSNorm folded into the prologue
+// (norm) and, with q_up, the gate/up pair: out = silu(x Wq^T) * (x Wup^T).
+// Requires tc_supported(...) for q and q_up.
+popcornStatus_t tc_dequant_matmul_fused(float* out, const float* x, const float* norm_w, float eps, bool norm,
+                                        const int8_t* q, const float* scale, const int8_t* q_up, const float* s_up,
+                                        int64_t M, int64_t N, int64_t K, cudaStream_t stream);
+
+// Stream-ordered scratch from the library's private pool (kept between calls).
+cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t stream);
+cudaError_t scratch_free(void* p, cudaStream_t stream);
+
 // tcgen05 path for the per-group formats (int8 codes [N, K] or packed int4
 // [N, K/2]; zero is null for int8); requires tc_grouped_supported(...).
 bool tc_grouped_supported(const void* q, int64_t M, int64_t N, int64_t K, int64_t gs);

@@ -93,10 +93,24 @@ __device__ __forceinline__ float absmax_step(float m, float v) {
     return (a > m) ? a : m;
 }
 
+// Optional RMSNorm of the activation rows inside the prologue, with
+// popcorn's arithmetic (src/reduction.cu:290-321): rms = sqrtf(sum(x^2) / K +
+// eps), inv = 1 / rms, x' = (x * inv) * norm_w[k] (norm_w may be null). Only
+// the order of the sum of squares differs from popcorn's sequential loop.
+struct RowNorm {
+    const float* w;  // [K] or null
+    float eps;
+    int on;
+};
+
+__device__ __forceinline__ float row_inv_rms(float sum_sq, int64_t K, float eps) {
+    return 1.0f / sqrtf(sum_sq / static_cast<float>(K) + eps);
+}
+
 // x f32 [M, K] -> x16 f16 [M, K] with per-row power-of-two scaling; one warp per row.
 __global__ void __launch_bounds__(256)
 x_to_f16_kernel(__half* __restrict__ x16, float* __restrict__ rowscale, const float* __restrict__ x,
-                int64_t M, int64_t K, int vec) {
+                int64_t M, int64_t K, int vec, RowNorm nrm) {
     // The GEMM that follows is launched as a programmatic dependent: let it
     // start its set-up now; it waits for this grid before reading x16.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -106,8 +120,25 @@ x_to_f16_kernel(__half* __restrict__ x16, float* __restrict__ rowscale, const fl
          row += nwarps) {
         const float* r = x + row * K;
         __half* o = x16 + row * K;
+        float inv = 1.0f;
+        if (nrm.on) {
+            float ss = 0.0f;
+            for (int64_t k = lane; k < K; k += 32) {
+                const float v = __ldg(r + k);
+                ss = fmaf(v, v, ss);
+            }
+            #pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+            inv = row_inv_rms(ss, K, nrm.eps);
+        }
+        // The value entering the GEMM: x, or its normalised form.
+        auto val = [&](int64_t k, float v) {
+            if (!nrm.on) return v;
+            v = v * inv;
+            return nrm.w != nullptr ? v * __ldg(nrm.w + k) : v;
+        };
         float m = 0.0f;
-        if (vec) {
+        if (vec && !nrm.on) {
             const float4* r4 = reinterpret_cast<const float4*>(r);
             #pragma unroll 4
             for (int64_t i = lane; i < (K >> 2); i += 32) {
@@ -115,7 +146,7 @@ x_to_f16_kernel(__half* __restrict__ x16, float* __restrict__ rowscale, const fl
                 m = absmax_step(absmax_step(absmax_step(absmax_step(m, v.x), v.y), v.z), v.w);
             }
         } else {
-            for (int64_t k = lane; k < K; k += 32) m = absmax_step(m, __ldg(r + k));
+            for (int64_t k = lane; k < K; k += 32) m = absmax_step(m, val(k, __ldg(r + k)));
         }
         #pragma unroll
         for (int off = 16; off > 0; off >>= 1) {
@@ -131,7 +162,7 @@ x_to_f16_kernel(__half* __restrict__ x16, float* __restrict__ rowscale, const fl
         }
         const float up = __int_as_float((e + 127) << 23);
         if (lane == 0) rowscale[row] = __int_as_float((127 - e) << 23);
-        if (vec) {
+        if (vec && !nrm.on) {
             const float4* r4 = reinterpret_cast<const float4*>(r);
             uint4* o8 = reinterpret_cast<uint4*>(o);
             for (int64_t c = lane; c < (K >> 3); c += 32) {
@@ -149,7 +180,7 @@ x_to_f16_kernel(__half* __restrict__ x16, float* __restrict__ rowscale, const fl
                 o8[c] = packed;
             }
         } else {
-            for (int64_t k = lane; k < K; k += 32) o[k] = __float2half_rn(__ldg(r + k) * up);
+            for (int64_t k = lane; k < K; k += 32) o[k] = __float2half_rn(val(k, __ldg(r + k)) * up);
         }
     }
 }
@@ -157,15 +188,16 @@ x_to_f16_kernel(__half* __restrict__ x16, float* __restrict__ rowscale, const fl
 // Same conversion, one block per row with the row held in registers (U
 // 16-float slices per thread, K <= 16 * 256 * U): x is read from HBM once and
 // every thread has all of its loads in flight at once. Needs K % 16 == 0 and
-// a 16-byte aligned x.
+// a 16-byte aligned x (and norm weights).
 constexpr int kRowThreads = 256;
 
 template <int U>
 __global__ void __launch_bounds__(kRowThreads)
 x_to_f16_row_kernel(__half* __restrict__ x16, float* __restrict__ rowscale, const float* __restrict__ x, int64_t M,
-                    int64_t K) {
+                    int64_t K, RowNorm nrm) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // see x_to_f16_kernel
     __shared__ float red[2][kRowThreads / 32];
+    __shared__ float ssq[2][kRowThreads / 32];
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
@@ -180,6 +212,46 @@ x_to_f16_row_kernel(__half* __restrict__ x16, float* __restrict__ rowscale, cons
             #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 v[u][c] = (unit < units) ? __ldg(r4 + unit * 4 + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+        }
+        if (nrm.on) {
+            float ss = 0.0f;
+            #pragma unroll
+            for (int u = 0; u < U; ++u)
+                #pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    ss = fmaf(v[u][c].x, v[u][c].x, ss);
+                    ss = fmaf(v[u][c].y, v[u][c].y, ss);
+                    ss = fmaf(v[u][c].z, v[u][c].z, ss);
+                    ss = fmaf(v[u][c].w, v[u][c].w, ss);
+                }
+            #pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+            if (lane == 0) ssq[parity][warp] = ss;
+            __syncthreads();
+            float total = 0.0f;
+            #pragma unroll
+            for (int w = 0; w < kRowThreads / 32; ++w) total += ssq[parity][w];
+            const float inv = row_inv_rms(total, K, nrm.eps);
+            #pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int64_t unit = tid + static_cast<int64_t>(u) * kRowThreads;
+                #pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    float4 a = v[u][c];
+                    a.x *= inv;
+                    a.y *= inv;
+                    a.z *= inv;
+                    a.w *= inv;
+                    if (nrm.w != nullptr && unit < units) {
+                        const float4 g = __ldg(reinterpret_cast<const float4*>(nrm.w) + unit * 4 + c);
+                        a.x *= g.x;
+                        a.y *= g.y;
+                        a.z *= g.z;
+                        a.w *= g.w;
+                    }
+                    v[u][c] = a;
+                }
             }
         }
         float m = 0.0f;
@@ -237,23 +309,24 @@ x_to_f16_row_kernel(__half* __restrict__ x16, float* __restrict__ rowscale, cons
 
 // Launch the x -> f16 prologue: block-per-row kernel where it applies.
 popcornStatus_t launch_x_to_f16(__half* x16, float* rowscale, const float* x, int64_t M, int64_t K,
-                                cudaStream_t stream) {
-    const bool vec = aligned16(x);
+                                cudaStream_t stream, RowNorm nrm = RowNorm{nullptr, 0.0f, 0}) {
+    const bool vec = aligned16(x) && (nrm.w == nullptr || aligned16(nrm.w));
     const int64_t slices = ceil_div(K / 16, kRowThreads);
     if (vec && K % 16 == 0 && K >= 1024 && slices <= 4) {
         int64_t blocks = M;
         const int64_t cap = static_cast<int64_t>(device_sm_count()) * 8;
         if (blocks > cap) blocks = cap;
         const unsigned g = static_cast<unsigned>(blocks);
-        if (slices == 1) x_to_f16_row_kernel<1><<<g, kRowThreads, 0, stream>>>(x16, rowscale, x, M, K);
-        else if (slices == 2) x_to_f16_row_kernel<2><<<g, kRowThreads, 0, stream>>>(x16, rowscale, x, M, K);
-        else x_to_f16_row_kernel<4><<<g, kRowThreads, 0, stream>>>(x16, rowscale, x, M, K);
+        if (slices == 1) x_to_f16_row_kernel<1><<<g, kRowThreads, 0, stream>>>(x16, rowscale, x, M, K, nrm);
+        else if (slices == 2) x_to_f16_row_kernel<2><<<g, kRowThreads, 0, stream>>>(x16, rowscale, x, M, K, nrm);
+        else x_to_f16_row_kernel<4><<<g, kRowThreads, 0, stream>>>(x16, rowscale, x, M, K, nrm);
         return check_launch();
     }
     int64_t blocks = ceil_div(M, 8);
     const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
     if (blocks > cap) blocks = cap;
-    x_to_f16_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x16, rowscale, x, M, K, vec ? 1 : 0);
+    x_to_f16_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x16, rowscale, x, M, K,
+                                                                      aligned16(x) ? 1 : 0, nrm);
     return check_launch();
 }
 
@@ -274,6 +347,18 @@ __device__ __forceinline__ void widen4_f16(uint32_t word, uint32_t& lo, uint32_t
 __device__ __forceinline__ uint32_t f16x2_bits(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Epilogue store: the value itself (epi = 0), or silu(g) * value (epi = 1)
+// where g is what the previous GEMM of the same call wrote there -- the gate
+// projection, so the up projection's epilogue finishes popcorn's
+// popcornSilu_f32 (g / (1 + expf(-g)), src/unary.cu:76-81) and popcornMul_f32.
+__device__ __forceinline__ void store_out(float* p, float v, int epi) {
+    if (epi) {
+        const float g = *p;
+        v = (g / (1.0f + expf(-g))) * v;
+    }
+    *p = v;
 }
 
 // Per-group formats: the converters write w * 2^e_n to tensor memory as f16
@@ -441,7 +526,7 @@ template <int BM, int FMT>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                float* __restrict__ out, const float* __restrict__ scale, const float* __restrict__ rowscale,
-               const float* __restrict__ zero, int gs, int M, int N, int K, int splits) {
+               const float* __restrict__ zero, int gs, int M, int N, int K, int splits, int epi) {
     using C = Cfg<BM, FMT>;
     constexpr int S = C::kStages;
     extern __shared__ uint8_t smem_raw[];
@@ -627,7 +712,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
                     #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         const int m = c0 + j;
-                        if (m < M) out[static_cast<int64_t>(m) * N + n] = (__uint_as_float(v[j]) * __ldg(rowscale + m)) * sc;
+                        if (m < M) {
+                            store_out(out + static_cast<int64_t>(m) * N + n,
+                                      (__uint_as_float(v[j]) * __ldg(rowscale + m)) * sc, epi);
+                        }
                     }
                 }
             }
@@ -669,7 +757,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
                     const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
                     #pragma unroll
                     for (int k = 0; k < 4; ++k) {
-                        if (m + k < M) out[static_cast<int64_t>(m + k) * N + nn] = (a4[k] * __ldg(rowscale + m + k)) * sc;
+                        if (m + k < M) {
+                            store_out(out + static_cast<int64_t>(m + k) * N + nn, (a4[k] * __ldg(rowscale + m + k)) * sc,
+                                      epi);
+                        }
                     }
                 }
             }
@@ -735,7 +826,7 @@ template <int RX, int FMT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                     float* __restrict__ out, const float* __restrict__ scale, const float* __restrict__ rowscale,
-                    const float* __restrict__ zero, int gs, int M, int N, int K) {
+                    const float* __restrict__ zero, int gs, int M, int N, int K, int epi) {
     using P = PairCfg<RX, FMT>;
     constexpr int kBK = P::kBK;
     constexpr int kSub = P::kSub;
@@ -926,7 +1017,8 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
                     for (int j = 0; j < 32; ++j) {
                         const int m = mp + c0 + j;
                         if (m < M) {
-                            out[static_cast<int64_t>(m) * N + n] = (__uint_as_float(v[j]) * __ldg(rowscale + m)) * sc;
+                            store_out(out + static_cast<int64_t>(m) * N + n,
+                                      (__uint_as_float(v[j]) * __ldg(rowscale + m)) * sc, epi);
                         }
                     }
                 }
@@ -1039,7 +1131,7 @@ int pick_splits(int slot, int64_t tiles, int64_t num_kb) {
 template <int BM, int FMT>
 popcornStatus_t launch_gemm(int slot, const CUtensorMap& tx, const CUtensorMap& tw, float* out, const float* scale,
                             const float* rowscale, const float* zero, int gs, int64_t M, int64_t N, int64_t K,
-                            cudaStream_t stream) {
+                            int epi, cudaStream_t stream) {
     using C = Cfg<BM, FMT>;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1066,7 +1158,7 @@ popcornStatus_t launch_gemm(int slot, const CUtensorMap& tx, const CUtensorMap& 
     cfg.attrs = attr;
     cfg.numAttrs = splits > 1 ? 2 : 1;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BM, FMT>, tx, tw, out, scale, rowscale, zero, gs,
-                                             static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), splits);
+                                             static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), splits, epi);
     if (e != cudaSuccess) return record_cuda(e);
     return check_launch();
 }
@@ -1105,7 +1197,7 @@ bool make_maps(PFN_cuTensorMapEncodeTiled_v12000 encode, __half* x16, const void
 template <int RX, int FMT>
 popcornStatus_t launch_pair(int slot, const CUtensorMap& tx, const CUtensorMap& tw, float* out, const float* scale,
                             const float* rowscale, const float* zero, int gs, int64_t M, int64_t N, int64_t K,
-                            cudaStream_t stream) {
+                            int epi, cudaStream_t stream) {
     using P = PairCfg<RX, FMT>;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1126,7 +1218,7 @@ popcornStatus_t launch_pair(int slot, const CUtensorMap& tx, const CUtensorMap& 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<RX, FMT>, tx, tw, out, scale, rowscale, zero,
-                                             gs, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
+                                             gs, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), epi);
     if (e != cudaSuccess) return record_cuda(e);
     return check_launch();
 }
@@ -1137,7 +1229,7 @@ popcornStatus_t launch_pair(int slot, const CUtensorMap& tx, const CUtensorMap& 
 template <int FMT>
 popcornStatus_t launch_tc_gemm(PFN_cuTensorMapEncodeTiled_v12000 encode, __half* x16, const float* rowscale,
                                float* out, const void* q, const float* scale, const float* zero, int gs, int64_t M,
-                               int64_t N, int64_t K, cudaStream_t stream) {
+                               int64_t N, int64_t K, int epi, cudaStream_t stream) {
     const int bm = pick_bm(M);
     const int64_t wcols = FMT == kFmtGroup4 ? K / 2 : K;
     const int bk = FMT == kFmtGroup4 ? 64 : 128;
@@ -1149,24 +1241,28 @@ popcornStatus_t launch_tc_gemm(PFN_cuTensorMapEncodeTiled_v12000 encode, __half*
         const int rx = bm / 2;
         if (!make_maps(encode, x16, q, M, N, K, wcols, rx, bk, &tx, &tw)) return POPCORN_ERROR_INVALID_VALUE;
         switch (rx) {
-            case 16: return launch_pair<16, FMT>(4, tx, tw, out, scale, rowscale, zero, gs, M, N, K, stream);
-            case 32: return launch_pair<32, FMT>(5, tx, tw, out, scale, rowscale, zero, gs, M, N, K, stream);
-            case 64: return launch_pair<64, FMT>(6, tx, tw, out, scale, rowscale, zero, gs, M, N, K, stream);
-            default: return launch_pair<128, FMT>(7, tx, tw, out, scale, rowscale, zero, gs, M, N, K, stream);
+            case 16: return launch_pair<16, FMT>(4, tx, tw, out, scale, rowscale, zero, gs, M, N, K, epi, stream);
+            case 32: return launch_pair<32, FMT>(5, tx, tw, out, scale, rowscale, zero, gs, M, N, K, epi, stream);
+            case 64: return launch_pair<64, FMT>(6, tx, tw, out, scale, rowscale, zero, gs, M, N, K, epi, stream);
+            default: return launch_pair<128, FMT>(7, tx, tw, out, scale, rowscale, zero, gs, M, N, K, epi, stream);
         }
     }
     if (!make_maps(encode, x16, q, M, N, K, wcols, bm, bk, &tx, &tw)) return POPCORN_ERROR_INVALID_VALUE;
     switch (bm) {
-        case 32: return launch_gemm<32, FMT>(0, tx, tw, out, scale, rowscale, zero, gs, M, N, K, stream);
-        case 64: return launch_gemm<64, FMT>(1, tx, tw, out, scale, rowscale, zero, gs, M, N, K, stream);
-        default: return launch_gemm<128, FMT>(2, tx, tw, out, scale, rowscale, zero, gs, M, N, K, stream);
+        case 32: return launch_gemm<32, FMT>(0, tx, tw, out, scale, rowscale, zero, gs, M, N, K, epi, stream);
+        case 64: return launch_gemm<64, FMT>(1, tx, tw, out, scale, rowscale, zero, gs, M, N, K, epi, stream);
+        default: return launch_gemm<128, FMT>(2, tx, tw, out, scale, rowscale, zero, gs, M, N, K, epi, stream);
     }
 }
 
 // x -> f16 prologue into stream-ordered scratch, then the GEMM.
+// x -> f16 prologue (with the optional RMSNorm), then the GEMM; with q_up a
+// second GEMM over the same activations whose epilogue multiplies by
+// silu of the first one's result (gate/up fusion).
 template <int FMT>
 popcornStatus_t tc_run(float* out, const float* x, const void* q, const float* scale, const float* zero, int gs,
-                       int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+                       int64_t M, int64_t N, int64_t K, cudaStream_t stream, RowNorm nrm = RowNorm{nullptr, 0.0f, 0},
+                       const void* q_up = nullptr, const float* s_up = nullptr) {
     PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
     if (encode == nullptr) return POPCORN_ERROR_INVALID_VALUE;
 
@@ -1182,8 +1278,13 @@ popcornStatus_t tc_run(float* out, const float* x, const void* q, const float* s
     __half* x16 = static_cast<__half*>(scratch);
     float* rowscale = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + x16_bytes);
 
-    popcornStatus_t st = launch_x_to_f16(x16, rowscale, x, M, K, stream);
-    if (st == POPCORN_SUCCESS) st = launch_tc_gemm<FMT>(encode, x16, rowscale, out, q, scale, zero, gs, M, N, K, stream);
+    popcornStatus_t st = launch_x_to_f16(x16, rowscale, x, M, K, stream, nrm);
+    if (st == POPCORN_SUCCESS) {
+        st = launch_tc_gemm<FMT>(encode, x16, rowscale, out, q, scale, zero, gs, M, N, K, 0, stream);
+    }
+    if (st == POPCORN_SUCCESS && q_up != nullptr) {
+        st = launch_tc_gemm<FMT>(encode, x16, rowscale, out, q_up, s_up, zero, gs, M, N, K, 1, stream);
+    }
     e = cudaFreeAsync(scratch, stream);
     if (st == POPCORN_SUCCESS && e != cudaSuccess) st = record_cuda(e);
     return st;
@@ -1202,6 +1303,22 @@ int tc_launch_count(int64_t, int64_t, int64_t) { return 2; }
 popcornStatus_t tc_dequant_matmul(float* out, const float* x, const int8_t* q, const float* scale, int64_t M,
                                   int64_t N, int64_t K, cudaStream_t stream) {
     return tc_run<kFmtChannel>(out, x, q, scale, nullptr, 0, M, N, K, stream);
+}
+
+cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t stream) {
+    cudaMemPool_t pool;
+    const cudaError_t e = scratch_pool(&pool);
+    if (e != cudaSuccess) return e;
+    return cudaMallocFromPoolAsync(p, bytes, pool, stream);
+}
+
+cudaError_t scratch_free(void* p, cudaStream_t stream) { return cudaFreeAsync(p, stream); }
+
+popcornStatus_t tc_dequant_matmul_fused(float* out, const float* x, const float* norm_w, float eps, bool norm,
+                                        const int8_t* q, const float* scale, const int8_t* q_up, const float* s_up,
+                                        int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+    const RowNorm nrm{norm_w, eps, norm ? 1 : 0};
+    return tc_run<kFmtChannel>(out, x, q, scale, nullptr, 0, M, N, K, stream, nrm, q_up, s_up);
 }
 
 bool tc_grouped_supported(const void* q, int64_t M, int64_t N, int64_t K, int64_t gs) {
@@ -1300,7 +1417,7 @@ extern "C" popcornStatus_t popcornDequantizeMatmulNoAlloc_i8f32(float* out, cons
     popcornStatus_t st = launch_x_to_f16(x16, rowscale, x, M, K, stream);
     if (st != POPCORN_SUCCESS) return st;
 
-    return launch_tc_gemm<kFmtChannel>(encode, x16, rowscale, out, qweight, scale, nullptr, 0, M, N, K, stream);
+    return launch_tc_gemm<kFmtChannel>(encode, x16, rowscale, out, qweight, scale, nullptr, 0, M, N, K, 0, stream);
 }
 
 namespace pcb {

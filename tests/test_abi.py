@@ -238,6 +238,27 @@ def test_int4_conventions(lib):
     assert qg(FAKE, FAKE, FAKE, FAKE, 2, 9, 3, None) == pc.POPCORN_ERROR_INVALID_VALUE
 
 
+def test_fused_conventions(lib):
+    # Every buffer but the RMSNorm weight must be non-null; sizes <= 0 are no-ops.
+    norm = lib.popcornRMSNormDequantizeMatmul_i8f32
+    glu = lib.popcornDequantizeMatmulSiluMul_i8f32
+    both = lib.popcornRMSNormDequantizeMatmulSiluMul_i8f32
+    for i in (0, 1, 3, 4):
+        args = [FAKE] * 5
+        args[i] = 0
+        assert norm(args[0], args[1], args[2], 1e-5, args[3], args[4], 1, 4, 4, None) == \
+            pc.POPCORN_ERROR_INVALID_VALUE, i
+    for i in range(6):
+        args = [FAKE] * 6
+        args[i] = 0
+        assert glu(*args, 1, 4, 4, None) == pc.POPCORN_ERROR_INVALID_VALUE, i
+        assert both(args[0], args[1], FAKE, 1e-5, *args[2:], 1, 4, 4, None) == pc.POPCORN_ERROR_INVALID_VALUE, i
+    for (M, N, K) in [(0, 4, 4), (1, 0, 4), (1, 4, 0), (-1, 4, 4)]:
+        assert norm(FAKE, FAKE, 0, 1e-5, FAKE, FAKE, M, N, K, None) == pc.POPCORN_SUCCESS
+        assert glu(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, M, N, K, None) == pc.POPCORN_SUCCESS
+        assert both(FAKE, FAKE, 0, 1e-5, FAKE, FAKE, FAKE, FAKE, M, N, K, None) == pc.POPCORN_SUCCESS
+
+
 def test_batched_size_overflow_is_rejected(lib):
     big = 1 << 62
     assert lib.popcornDequantizeMatmulBatched_i8f32(FAKE, FAKE, FAKE, FAKE, big, 4, 1, 1, None) == \
