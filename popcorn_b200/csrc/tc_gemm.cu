@@ -14,8 +14,9 @@
 //  2. tc_gemm_kernel<BM, FMT>: one CTA per 128 (weight rows) x BM (activation
 //     rows) output tile (cluster split-K when the tiles fill less than half
 //     the GPU), or tc_gemm_pair_kernel<RX, FMT>: a CTA pair per 256 x 2 RX
-//     tile with tcgen05.mma.cta_group::2. Swap-AB, so the weight tile is the
-//     MMA "A" operand; per 128-deep k-block stage:
+//     tile with tcgen05.mma.cta_group::2 (tc_gemm_pair_persist_kernel when
+//     there are more tiles than resident pairs). Swap-AB, so the weight tile
+//     is the MMA "A" operand; per 128-deep k-block stage:
 //       warp 0      TMA producer: x16 tile (128B swizzle) and the weight-code
 //                   tile [128 rows x 128 int8 (128B swizzle) or 64 bytes of
 //                   packed int4 (64B swizzle)];
@@ -799,6 +800,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
 // RX activation rows per CTA (the pair's MMA is 256 x 2*RX): 128 for
 // prefill, 16/32/64 for skinny shapes with many weight tiles, where one MMA
 // instruction now covers both CTAs' 128 weight rows.
+// Persistent: a pair walks the output tiles t = pair, pair + pairs, ...; the
+// ring's slots and barrier phases run on across tiles (a k-block counter
+// shared by all roles), so the next tile's loads and conversions proceed
+// while the epilogue of the previous one drains. The accumulator is single:
+// acc_full (multicast commit) hands it to the epilogue, acc_empty (eight
+// epilogue warps of both CTAs, on the leader) hands it back once read.
 template <int RX, int FMT = kFmtChannel>
 struct PairCfg {
     static constexpr int kBK = 128;
@@ -815,13 +822,286 @@ struct PairCfg {
     static constexpr int kTmemStages = (kTmemCols - 2 * RX) / kACols;
     static constexpr int kStages = kSmemStages < kTmemStages ? kSmemStages : kTmemStages;
     static constexpr int kAStages = kStages;
-    static constexpr int kNumBars = 4 * kStages + 2;
+    static constexpr int kNumBars = 4 * kStages + 3;
     static constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16;
     static_assert(kSmem <= 227 * 1024, "shared memory per block");
     static_assert(2 * RX + kAStages * kACols <= kTmemCols, "tensor memory holds 512 columns");
     static_assert(kXBytes % 1024 == 0, "x16 stages must stay 1024-byte aligned");
 };
 
+template <int RX, int FMT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+tc_gemm_pair_persist_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                    float* __restrict__ out, const float* __restrict__ scale, const float* __restrict__ rowscale,
+                    const float* __restrict__ zero, int gs, int M, int N, int K, int epi) {
+    using P = PairCfg<RX, FMT>;
+    constexpr int kBK = P::kBK;
+    constexpr int kSub = P::kSub;
+    constexpr int kRowsX = P::kRowsX;
+    constexpr int kXBytes = P::kXBytes;
+    constexpr int kWBytes = P::kWBytes;
+    constexpr int kACols = P::kACols;
+    constexpr int kTmemCols = P::kTmemCols;
+    constexpr int kNumBars = P::kNumBars;
+    constexpr int S = P::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* xs = smem;                                  // S x kSub x [RX][64] f16, 128B swizzle
+    uint8_t* ws = smem + S * kXBytes;                    // S x [128][kWRow] weight codes
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ws + S * kWBytes);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+
+    // full[s]: both activation halves landed (leader). wfull[s]: this CTA's
+    // weight tile landed. afull[s]: both CTAs' converters wrote A buffer s.
+    // release[s]: the MMAs of slot s finished (multicast commit to both
+    // CTAs): its tiles and A buffer may be refilled. acc_full / acc_empty:
+    // the accumulator of a tile is complete / has been read.
+    const uint32_t full0 = smem_addr(bars);
+    const uint32_t wfull0 = full0 + 8 * S;
+    const uint32_t release0 = wfull0 + 8 * S;
+    const uint32_t afull0 = release0 + 8 * S;
+    const uint32_t acc_full = afull0 + 8 * S;
+    const uint32_t acc_empty = acc_full + 8;
+    const uint32_t drain = acc_empty + 8;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = static_cast<int>(blockIdx.x >> 1);
+    const int pairs = static_cast<int>(gridDim.x >> 1);
+    const int tiles_n = (N + 2 * kTileN - 1) / (2 * kTileN);
+    const int tiles = tiles_n * ((M + 2 * kRowsX - 1) / (2 * kRowsX));
+    const int num_kb = (K + kBK - 1) / kBK;
+    unsigned int* err = &g_tc_error;
+    // Tile t: this CTA's weight rows n0 .. n0 + 127 and the pair's activation
+    // rows mp .. mp + 2*RX - 1.
+    auto tile_n0 = [&](int t) { return (t % tiles_n) * (2 * kTileN) + static_cast<int>(rank) * kTileN; };
+    auto tile_mp = [&](int t) { return (t / tiles_n) * (2 * kRowsX); };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(wfull0 + 8 * s, 1);
+            mbar_init(release0 + 8 * s, 1);
+            mbar_init(afull0 + 8 * s, 2 * 4 * kConvGroups);  // every converter warp of both CTAs
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, 2 * 4);  // the four epilogue warps of both CTAs
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (warp == kWarpTma && lane == 0) {
+        tma_prefetch_desc(&tmap_x);
+        tma_prefetch_desc(&tmap_w);
+    }
+    if (warp == kWarpMma) {
+        tmem_alloc_pair(smem_addr(tmem_slot), kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // the peer's barriers exist before anyone arrives on them
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t a_tmem0 = tmem + 2 * kRowsX;  // A buffers after the 2*RX accumulator columns
+
+    // Launched as a programmatic dependent of the x -> f16 prologue. The
+    // weights were written before the prologue ran, so the first ring of
+    // weight tiles is requested (and converted) while the prologue still
+    // runs; only the activation loads and the epilogue's row scales wait
+    // for it (griddepcontrol.wait in those threads).
+    if (warp == kWarpTma) {
+        if (lane == 0) {
+            const uint32_t full_leader0 = mapa_shared(full0, 0);
+            const int first = (pair < tiles) ? (num_kb < S ? num_kb : S) : 0;
+            for (int kb = 0; kb < first; ++kb) {
+                mbar_arrive_expect_tx(wfull0 + 8 * kb, kWBytes);
+                tma_load_2d(smem_addr(ws + kb * kWBytes), &tmap_w, kb * P::kWRow, tile_n0(pair), wfull0 + 8 * kb);
+            }
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            int g = 0;  // k-blocks issued so far (all tiles)
+            bool ok = true;
+            for (int t = pair; t < tiles && ok; t += pairs) {
+                const int n0 = tile_n0(t);
+                const int mp = tile_mp(t);
+                for (int kb = 0; kb < num_kb; ++kb, ++g) {
+                    const int s = g % S;
+                    if (g >= S && !mbar_wait_cluster(release0 + 8 * s, ((g / S) - 1) & 1, err, 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_arrive_expect_tx(full0 + 8 * s, 2 * kXBytes);
+                    #pragma unroll
+                    for (int sub = 0; sub < kSub; ++sub) {
+                        tma_load_2d_pair(smem_addr(xs + s * kXBytes + sub * kRowsX * 128), &tmap_x,
+                                         kb * kBK + sub * 64, mp + static_cast<int>(rank) * kRowsX,
+                                         full_leader0 + 8 * s);
+                    }
+                    if (g >= first) {
+                        mbar_arrive_expect_tx(wfull0 + 8 * s, kWBytes);
+                        tma_load_2d(smem_addr(ws + s * kWBytes), &tmap_w, kb * P::kWRow, n0, wfull0 + 8 * s);
+                    }
+                }
+            }
+            // Leave no copy of ours in flight: the weight tiles signal this CTA;
+            // the activation halves are covered by the drain below (the leader
+            // consumes every stage before it commits the drain).
+            for (int i = (g > S ? g - S : 0); i < g; ++i) mbar_wait(wfull0 + 8 * (i % S), (i / S) & 1, err, 64u);
+        }
+    } else if (warp == kWarpMma) {
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = idesc_f16_f32(2 * kTileN, 2 * kRowsX);
+            int g = 0;
+            int it = 0;
+            bool ok = true;
+            for (int t = pair; t < tiles && ok; t += pairs, ++it) {
+                // The previous tile's accumulator must have been read out.
+                if (it > 0 && !mbar_wait_cluster(acc_empty, (it - 1) & 1, err, 4u)) break;
+                tc_fence_after();
+                for (int kb = 0; kb < num_kb; ++kb, ++g) {
+                    const int s = g % S;
+                    if (!mbar_wait_cluster(full0 + 8 * s, (g / S) & 1, err, 2u) ||
+                        !mbar_wait_cluster(afull0 + 8 * s, (g / S) & 1, err, 4u)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    #pragma unroll
+                    for (int j = 0; j < kBK / 16; ++j) {
+                        const uint64_t bdesc =
+                            smem_desc_sw128_kmajor(smem_addr(xs + s * kXBytes + (j / 4) * kRowsX * 128));
+                        mma_f16_ts_pair(tmem, a_tmem0 + s * kACols + j * 8,
+                                        bdesc + static_cast<uint64_t>((j % 4) * 2), idesc, (kb | j) != 0 ? 1u : 0u);
+                    }
+                    mma_commit_pair(release0 + 8 * s, 0x3);
+                }
+                if (ok) mma_commit_pair(acc_full, 0x3);
+            }
+            mma_commit_pair(drain, 0x3);
+        }
+    } else if (warp < kWarpEpi0) {
+        // Converters: thread owns weight row r of this CTA's 128 = tensor-memory
+        // lane r; both groups convert every k-block, group g its codes
+        // [64 g, 64 g + 64).
+        const int quarter = warp & 3;
+        const int group = (warp - kWarpConv0) >> 2;
+        const int r = quarter * 32 + lane;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        const uint32_t afull_leader0 = mapa_shared(afull0, 0);
+        int g = 0;
+        bool ok = true;
+        for (int t = pair; t < tiles && ok; t += pairs) {
+            const int n0 = tile_n0(t);
+            float pw = 1.0f;
+            if constexpr (FMT != kFmtChannel) {
+                pw = __int_as_float((group_row_exp<FMT>(scale, zero, n0 + r, N, K / gs) + 127) << 23);
+            }
+            // Group factors one k-block ahead, their loads overlapping this
+            // block's waits and conversion.
+            float f[2] = {}, zf[2] = {};
+            if constexpr (FMT != kFmtChannel) group_factors<FMT>(scale, zero, n0 + r, N, K, gs, 0, group, pw, f, zf);
+            for (int kb = 0; kb < num_kb; ++kb, ++g) {
+                const int s = g % S;
+                float fn[2] = {}, zn[2] = {};
+                if constexpr (FMT != kFmtChannel) {
+                    if (kb + 1 < num_kb) {
+                        group_factors<FMT>(scale, zero, n0 + r, N, K, gs, kb + 1, group, pw, fn, zn);
+                    }
+                }
+                bool w_ok = mbar_wait(wfull0 + 8 * s, (g / S) & 1, err, 8u);
+                if (w_ok && g >= S) w_ok = mbar_wait_cluster(release0 + 8 * s, ((g / S) - 1) & 1, err, 16u);
+                // tcgen05.st is warp-collective: leave together or not at all.
+                if (!__all_sync(0xffffffffu, w_ok)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                convert_half<FMT>(ws + s * kWBytes, r, group, tmem + lane_addr + 2 * kRowsX + s * kACols, f, zf);
+                #pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    f[q] = fn[q];
+                    zf[q] = zn[q];
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(afull_leader0 + 8 * s);
+            }
+        }
+    } else {
+        // Epilogue: lane = weight row n of this CTA, 2*RX accumulator columns =
+        // activation rows mp .. mp + 2*RX - 1 of the pair.
+        const int quarter = warp & 3;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        const uint32_t acc_empty_leader = mapa_shared(acc_empty, 0);
+        asm volatile("griddepcontrol.wait;" ::: "memory");  // row scales come from the prologue
+        int it = 0;
+        for (int t = pair; t < tiles; t += pairs, ++it) {
+            const int n = tile_n0(t) + quarter * 32 + lane;
+            const int mp = tile_mp(t);
+            // Output scale of row n: scale[n], or 2^-e_n for a per-group format.
+            float sc = 0.0f;
+            if (n < N) {
+                if constexpr (FMT == kFmtChannel) {
+                    sc = __ldg(scale + n);
+                } else {
+                    sc = __int_as_float((127 - group_row_exp<FMT>(scale, zero, n, N, K / gs)) << 23);
+                }
+            }
+            const bool ok = mbar_wait_cluster(acc_full, it & 1, err, 32u);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc_fence_after();
+            // kChunk accumulator columns per read (64, or 32 for tiles of 32
+            // columns); the accumulator is handed back to the MMA warp as soon
+            // as its last columns are in registers.
+            constexpr int kChunk = (2 * kRowsX >= 64) ? 64 : 32;
+            const int rows_m = (M - mp < 2 * kRowsX) ? M - mp : 2 * kRowsX;  // activation rows of the tile
+            #pragma unroll 1
+            for (int c0 = 0; c0 < rows_m; c0 += kChunk) {
+                uint32_t v[kChunk];
+                tmem_ld_32x32b_x32(tmem + lane_addr + c0, *reinterpret_cast<uint32_t(*)[32]>(v));
+                if constexpr (kChunk == 64) {
+                    if (c0 + 32 < rows_m) {  // warp-uniform
+                        tmem_ld_32x32b_x32(tmem + lane_addr + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+                    }
+                }
+                tmem_wait_ld();
+                if (c0 + kChunk >= rows_m) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
+                }
+                if (n < N) {
+                    #pragma unroll
+                    for (int j = 0; j < kChunk; ++j) {
+                        if (c0 + j < rows_m) {
+                            const int m = mp + c0 + j;
+                            store_out(out + static_cast<int64_t>(m) * N + n,
+                                      (__uint_as_float(v[j]) * __ldg(rowscale + m)) * sc, epi);
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    // Every MMA of the pair must be finished before either CTA releases its
+    // tensor memory or shared memory: wait for the drain commit, then meet.
+    if (warp == kWarpMma && lane == 0) mbar_wait_cluster(drain, 0, err, 128u);
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp == kWarpMma) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, kTmemCols);
+    }
+}
+
+// One output tile per pair (grid = every tile): used when all tiles are
+// resident at once, so there is nothing to overlap between tiles and the
+// single-tile loops are the cheaper ones to issue.
 template <int RX, int FMT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
@@ -1201,14 +1481,41 @@ popcornStatus_t launch_pair(int slot, const CUtensorMap& tx, const CUtensorMap& 
     using P = PairCfg<RX, FMT>;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < kMaxDevices && !g_attr_set[dev][slot + 8 * FMT]) {
+    const bool known = dev >= 0 && dev < kMaxDevices;
+    // Both pair kernels take the same shared memory (attribute set once each).
+    static bool persist_attr[kMaxDevices][24] = {};
+    if (known && !g_attr_set[dev][slot + 8 * FMT]) {
         cudaError_t e = cudaFuncSetAttribute(tc_gemm_pair_kernel<RX, FMT>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, P::kSmem);
+        if (e == cudaSuccess && !persist_attr[dev][slot + 8 * FMT]) {
+            e = cudaFuncSetAttribute(tc_gemm_pair_persist_kernel<RX, FMT>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, P::kSmem);
+            persist_attr[dev][slot + 8 * FMT] = e == cudaSuccess;
+        }
         if (e != cudaSuccess) return record_cuda(e);
         g_attr_set[dev][slot + 8 * FMT] = true;
     }
+    // Pairs resident at once (occupancy query, cached per device and config).
+    static int resident[kMaxDevices][4][3] = {};  // [dev][log2(RX / 16)][FMT]: pairs, 0 = unknown
+    const int rxi = RX == 16 ? 0 : (RX == 32 ? 1 : (RX == 64 ? 2 : 3));
+    int pairs = known ? resident[dev][rxi][FMT] : 0;
+    if (pairs == 0) {
+        cudaLaunchConfig_t q = {};
+        q.gridDim = dim3(2);
+        q.blockDim = dim3(kThreads);
+        q.dynamicSmemBytes = P::kSmem;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, tc_gemm_pair_persist_kernel<RX, FMT>, &q) != cudaSuccess ||
+            clusters < 1) {
+            cudaGetLastError();
+            clusters = device_sm_count() / 2;
+        }
+        pairs = clusters;
+        if (known) resident[dev][rxi][FMT] = pairs;
+    }
+    const int64_t tiles_n = ceil_div(N, 2 * kTileN);
+    const int64_t tiles_m = ceil_div(M, 2 * RX);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(2 * ceil_div(N, 2 * kTileN)), static_cast<unsigned>(ceil_div(M, 2 * RX)));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = P::kSmem;
     cfg.stream = stream;
@@ -1217,8 +1524,18 @@ popcornStatus_t launch_pair(int slot, const CUtensorMap& tx, const CUtensorMap& 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<RX, FMT>, tx, tw, out, scale, rowscale, zero,
-                                             gs, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), epi);
+    cudaError_t e;
+    if (tiles_n * tiles_m > pairs) {
+        // More tiles than resident pairs: persistent pairs, so the next tile's
+        // loads and conversions overlap the previous tile's epilogue.
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+        e = cudaLaunchKernelEx(&cfg, tc_gemm_pair_persist_kernel<RX, FMT>, tx, tw, out, scale, rowscale, zero, gs,
+                               static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), epi);
+    } else {
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * tiles_n), static_cast<unsigned>(tiles_m));
+        e = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<RX, FMT>, tx, tw, out, scale, rowscale, zero, gs,
+                               static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), epi);
+    }
     if (e != cudaSuccess) return record_cuda(e);
     return check_launch();
 }
