@@ -362,6 +362,43 @@ __device__ __forceinline__ void store_out(float* p, float v, int epi) {
     *p = v;
 }
 
+// Epilogue of one 32-column accumulator chunk of weight row n:
+// out[m0 + j, n] = (v[j] * rowscale[m0 + j]) * sc for j < cnt. The chunk's
+// row scales are read first (broadcast float4 loads: every lane reads the
+// same addresses; rowscale + m0 is 16-byte aligned since m0 % 32 == 0) and
+// the epilogue mode is tested once, so the stores issue back to back
+// instead of each waiting for its own load.
+__device__ __forceinline__ void store_chunk(float* __restrict__ out, const float* __restrict__ rowscale, int m0,
+                                            int cnt, int n, int N, float sc, const uint32_t* v, int epi) {
+    float rs[32];
+    if (cnt >= 32) {
+        const float4* r4 = reinterpret_cast<const float4*>(rowscale + m0);
+        #pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float4 r = __ldg(r4 + q);
+            rs[4 * q] = r.x;
+            rs[4 * q + 1] = r.y;
+            rs[4 * q + 2] = r.z;
+            rs[4 * q + 3] = r.w;
+        }
+    } else {
+        #pragma unroll
+        for (int j = 0; j < 32; ++j) rs[j] = (j < cnt) ? __ldg(rowscale + m0 + j) : 0.0f;
+    }
+    float* base = out + static_cast<int64_t>(m0) * N + n;
+    if (epi) {
+        #pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            if (j < cnt) store_out(base + static_cast<int64_t>(j) * N, (__uint_as_float(v[j]) * rs[j]) * sc, 1);
+        }
+    } else {
+        #pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            if (j < cnt) base[static_cast<int64_t>(j) * N] = (__uint_as_float(v[j]) * rs[j]) * sc;
+        }
+    }
+}
+
 // Per-group formats: the converters write w * 2^e_n to tensor memory as f16
 // and the epilogue multiplies by 2^-e_n (exact). 2^e_n brings the largest
 // weight row n can hold -- 128 |s| for int8 codes, (15 + |z|) |s| for int4 --
@@ -710,14 +747,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
                                               __uint_as_float(v[4 * q4 + 2]), __uint_as_float(v[4 * q4 + 3]));
                     }
                 } else if (n < N) {
-                    #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int m = c0 + j;
-                        if (m < M) {
-                            store_out(out + static_cast<int64_t>(m) * N + n,
-                                      (__uint_as_float(v[j]) * __ldg(rowscale + m)) * sc, epi);
-                        }
-                    }
+                    store_chunk(out, rowscale, c0, M - c0, n, N, sc, v, epi);
                 }
             }
         }
@@ -1073,13 +1103,9 @@ tc_gemm_pair_persist_kernel(const __grid_constant__ CUtensorMap tmap_x, const __
                     if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
                 }
                 if (n < N) {
-                    #pragma unroll
-                    for (int j = 0; j < kChunk; ++j) {
-                        if (c0 + j < rows_m) {
-                            const int m = mp + c0 + j;
-                            store_out(out + static_cast<int64_t>(m) * N + n,
-                                      (__uint_as_float(v[j]) * __ldg(rowscale + m)) * sc, epi);
-                        }
+                    store_chunk(out, rowscale, mp + c0, rows_m - c0, n, N, sc, v, epi);
+                    if constexpr (kChunk == 64) {
+                        if (c0 + 32 < rows_m) store_chunk(out, rowscale, mp + c0 + 32, rows_m - c0 - 32, n, N, sc, v + 32, epi);
                     }
                 }
             }
@@ -1292,16 +1318,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tmem + lane_addr + c0, v);
                 tmem_wait_ld();
-                if (n < N) {
-                    #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int m = mp + c0 + j;
-                        if (m < M) {
-                            store_out(out + static_cast<int64_t>(m) * N + n,
-                                      (__uint_as_float(v[j]) * __ldg(rowscale + m)) * sc, epi);
-                        }
-                    }
-                }
+                if (n < N) store_chunk(out, rowscale, mp + c0, M - mp - c0, n, N, sc, v, epi);
             }
         }
     }
