@@ -79,8 +79,12 @@ struct Cfg {
     static constexpr int kWBytes = kTileN * kWRow;  // weight tile per stage
     static constexpr int kTmemCols = 512;
     static constexpr int kNumBars = 3 * kStages + 2;
-    // ring, barriers, tensor-memory slot (16 B), per-row output scales
-    static constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16 + kTileN * 4;
+    // ring, barriers, tensor-memory slot (16 B), per-row output scales, and
+    // the epilogue's [32 x 32] f32 staging tile per epilogue warp (tiles of
+    // 64 or more activation rows; a single 32-column chunk stores directly)
+    static constexpr bool kStaged = BM >= 64;
+    static constexpr int kStageBytes = kStaged ? 4 * 32 * 32 * 4 : 0;
+    static constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16 + kTileN * 4 + 16 + kStageBytes;
     // Split-K reduction buffer: [128 weight rows][BM + 4] f32 in the idle ring.
     static constexpr int kRedStride = BM + 4;
     static_assert(kXBytes % 1024 == 0, "x16 stages must stay 1024-byte aligned");
@@ -362,6 +366,46 @@ __device__ __forceinline__ void store_out(float* p, float v, int epi) {
     *p = v;
 }
 
+// Vector form of store_chunk (epi = 0) for a warp whose 32 weight rows
+// n0w .. n0w + 31 all lie below N, with 16-byte aligned output rows: the
+// chunk goes through the warp's [32 m][32 n] f32 staging tile in shared
+// memory (lane l writes its row as column l, conflict-free) and back out as
+// float4 runs along n: eight 16-byte stores per lane instead of 32 scalar
+// ones.
+__device__ __forceinline__ void store_chunk_v(float* __restrict__ out, const float* __restrict__ rowscale, int m0,
+                                              int cnt, int n0w, int N, float sc, const uint32_t* v, float* stage,
+                                              int lane) {
+    float rs[32];
+    if (cnt >= 32) {
+        const float4* r4 = reinterpret_cast<const float4*>(rowscale + m0);
+        #pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float4 r = __ldg(r4 + q);
+            rs[4 * q] = r.x;
+            rs[4 * q + 1] = r.y;
+            rs[4 * q + 2] = r.z;
+            rs[4 * q + 3] = r.w;
+        }
+    } else {
+        #pragma unroll
+        for (int j = 0; j < 32; ++j) rs[j] = (j < cnt) ? __ldg(rowscale + m0 + j) : 0.0f;
+    }
+    #pragma unroll
+    for (int j = 0; j < 32; ++j) stage[j * 32 + lane] = (__uint_as_float(v[j]) * rs[j]) * sc;
+    __syncwarp();
+    const int q = lane & 7;
+    const int mr = lane >> 3;
+    #pragma unroll
+    for (int it = 0; it < 8; ++it) {
+        const int ml = it * 4 + mr;
+        if (ml < cnt) {
+            const float4 val = *reinterpret_cast<const float4*>(stage + ml * 32 + 4 * q);
+            *reinterpret_cast<float4*>(out + static_cast<int64_t>(m0 + ml) * N + n0w + 4 * q) = val;
+        }
+    }
+    __syncwarp();  // the tile is rewritten by the next chunk
+}
+
 // Epilogue of one 32-column accumulator chunk of weight row n:
 // out[m0 + j, n] = (v[j] * rowscale[m0 + j]) * sc for j < cnt. The chunk's
 // row scales are read first (broadcast float4 loads: every lane reads the
@@ -575,6 +619,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
     uint64_t* bars = reinterpret_cast<uint64_t*>(ws + S * C::kWBytes);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
     float* rsc = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(tmem_slot) + 16);  // [128] output scales
+    float* stage = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(rsc + kTileN) + 15) & ~uintptr_t(15));
     float* red = reinterpret_cast<float*>(smem);         // split-K partial, reuses the ring
 
     // full[s]: stage s landed (TMA). afull[s]: A buffer s written (8 converter
@@ -593,6 +638,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
     const int kb0 = num_kb * rank / splits;
     const int n_kb = num_kb * (rank + 1) / splits - kb0;
     unsigned int* err = &g_tc_error;
+    // Plain epilogue into 16-byte aligned rows: stores go out as float4 runs.
+    const bool vec_out = C::kStaged && epi == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && (N & 3) == 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -746,6 +793,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
                         dst[q4] = make_float4(__uint_as_float(v[4 * q4]), __uint_as_float(v[4 * q4 + 1]),
                                               __uint_as_float(v[4 * q4 + 2]), __uint_as_float(v[4 * q4 + 3]));
                     }
+                } else if (vec_out && n0 + quarter * 32 + 32 <= N) {
+                    store_chunk_v(out, rowscale, c0, M - c0, n0 + quarter * 32, N, sc, v, stage + quarter * 1024,
+                                  lane);
                 } else if (n < N) {
                     store_chunk(out, rowscale, c0, M - c0, n, N, sc, v, epi);
                 }
@@ -853,7 +903,11 @@ struct PairCfg {
     static constexpr int kStages = kSmemStages < kTmemStages ? kSmemStages : kTmemStages;
     static constexpr int kAStages = kStages;
     static constexpr int kNumBars = 4 * kStages + 3;
-    static constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16;
+    // Epilogue [32 x 32] f32 staging tile per epilogue warp, for tiles of 64
+    // or more activation rows (a single 32-column chunk stores directly).
+    static constexpr bool kStaged = 2 * RX >= 64;
+    static constexpr int kStageBytes = kStaged ? 4 * 32 * 32 * 4 : 0;
+    static constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16 + 16 + kStageBytes;
     static_assert(kSmem <= 227 * 1024, "shared memory per block");
     static_assert(2 * RX + kAStages * kACols <= kTmemCols, "tensor memory holds 512 columns");
     static_assert(kXBytes % 1024 == 0, "x16 stages must stay 1024-byte aligned");
@@ -880,6 +934,7 @@ tc_gemm_pair_persist_kernel(const __grid_constant__ CUtensorMap tmap_x, const __
     uint8_t* ws = smem + S * kXBytes;                    // S x [128][kWRow] weight codes
     uint64_t* bars = reinterpret_cast<uint64_t*>(ws + S * kWBytes);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+    float* stage = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(tmem_slot) + 16 + 15) & ~uintptr_t(15));
 
     // full[s]: both activation halves landed (leader). wfull[s]: this CTA's
     // weight tile landed. afull[s]: both CTAs' converters wrote A buffer s.
@@ -904,6 +959,8 @@ tc_gemm_pair_persist_kernel(const __grid_constant__ CUtensorMap tmap_x, const __
     const int tiles = tiles_n * ((M + 2 * kRowsX - 1) / (2 * kRowsX));
     const int num_kb = (K + kBK - 1) / kBK;
     unsigned int* err = &g_tc_error;
+    // Plain epilogue into 16-byte aligned rows: stores go out as float4 runs.
+    const bool vec_out = P::kStaged && epi == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && (N & 3) == 0;
     // Tile t: this CTA's weight rows n0 .. n0 + 127 and the pair's activation
     // rows mp .. mp + 2*RX - 1.
     auto tile_n0 = [&](int t) { return (t % tiles_n) * (2 * kTileN) + static_cast<int>(rank) * kTileN; };
@@ -1082,31 +1139,24 @@ tc_gemm_pair_persist_kernel(const __grid_constant__ CUtensorMap tmap_x, const __
             const bool ok = mbar_wait_cluster(acc_full, it & 1, err, 32u);
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
-            // kChunk accumulator columns per read (64, or 32 for tiles of 32
-            // columns); the accumulator is handed back to the MMA warp as soon
-            // as its last columns are in registers.
-            constexpr int kChunk = (2 * kRowsX >= 64) ? 64 : 32;
+            // 32 accumulator columns per read; the accumulator is handed back
+            // to the MMA warp as soon as its last columns are in registers.
             const int rows_m = (M - mp < 2 * kRowsX) ? M - mp : 2 * kRowsX;  // activation rows of the tile
+            const int n0w = tile_n0(t) + quarter * 32;                      // the warp's first weight row
             #pragma unroll 1
-            for (int c0 = 0; c0 < rows_m; c0 += kChunk) {
-                uint32_t v[kChunk];
-                tmem_ld_32x32b_x32(tmem + lane_addr + c0, *reinterpret_cast<uint32_t(*)[32]>(v));
-                if constexpr (kChunk == 64) {
-                    if (c0 + 32 < rows_m) {  // warp-uniform
-                        tmem_ld_32x32b_x32(tmem + lane_addr + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
-                    }
-                }
+            for (int c0 = 0; c0 < rows_m; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem + lane_addr + c0, v);
                 tmem_wait_ld();
-                if (c0 + kChunk >= rows_m) {
+                if (c0 + 32 >= rows_m) {
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
                 }
-                if (n < N) {
+                if (vec_out && n0w + 32 <= N) {
+                    store_chunk_v(out, rowscale, mp + c0, rows_m - c0, n0w, N, sc, v, stage + quarter * 1024, lane);
+                } else if (n < N) {
                     store_chunk(out, rowscale, mp + c0, rows_m - c0, n, N, sc, v, epi);
-                    if constexpr (kChunk == 64) {
-                        if (c0 + 32 < rows_m) store_chunk(out, rowscale, mp + c0 + 32, rows_m - c0 - 32, n, N, sc, v + 32, epi);
-                    }
                 }
             }
         }
@@ -1149,6 +1199,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
     uint8_t* ws = smem + S * kXBytes;                    // S x [128][kWRow] weight codes
     uint64_t* bars = reinterpret_cast<uint64_t*>(ws + S * kWBytes);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+    float* stage = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(tmem_slot) + 16 + 15) & ~uintptr_t(15));
 
     // full[s]: both activation halves landed (leader). wfull[s]: this CTA's
     // weight tile landed. afull[s]: both CTAs' converters wrote A buffer s.
@@ -1169,6 +1220,8 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
     const int mp = blockIdx.y * (2 * kRowsX);                                          // pair's activation rows
     const int num_kb = (K + kBK - 1) / kBK;
     unsigned int* err = &g_tc_error;
+    // Plain epilogue into 16-byte aligned rows: stores go out as float4 runs.
+    const bool vec_out = P::kStaged && epi == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && (N & 3) == 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -1318,7 +1371,12 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tmem + lane_addr + c0, v);
                 tmem_wait_ld();
-                if (n < N) store_chunk(out, rowscale, mp + c0, M - mp - c0, n, N, sc, v, epi);
+                const int n0w = n0 + quarter * 32;  // the warp's first weight row
+                if (vec_out && n0w + 32 <= N) {
+                    store_chunk_v(out, rowscale, mp + c0, M - mp - c0, n0w, N, sc, v, stage + quarter * 1024, lane);
+                } else if (n < N) {
+                    store_chunk(out, rowscale, mp + c0, M - mp - c0, n, N, sc, v, epi);
+                }
             }
         }
     }
