@@ -64,9 +64,10 @@ WORKLOADS = {
 NCU_TRAFFIC = {
     "decode": 16826112,    # profiles/gemv_xs_decode_m1_k4096_n4096.md
     "skinny": 45422848,    # profiles/tc_gemm_skinny_m32_k4096_n11008.md
-    "prefill": 36620032,   # profiles/tc_gemm_pair_prefill_m2048_k4096_n4096.md
+    "prefill": 35509504,   # profiles/tc_gemm_pair_prefill_m2048_k4096_n4096.md
     "grouped_decode": 17335296,  # profiles/grouped_xs_decode_m1_k4096_n4096_g128.md
     "int4_decode": 9476608,      # profiles/i4_xs_decode_m1_k4096_n4096_g128.md
+    "mlp_decode": 93543168,      # profiles/fused_xs_mlp_decode_m1_k4096_n11008.md
 }
 
 
