@@ -88,7 +88,10 @@ struct Cfg {
     // Split-K reduction buffer: [128 weight rows][BM + 4] f32 in the idle ring.
     static constexpr int kRedStride = BM + 4;
     static_assert(kXBytes % 1024 == 0, "x16 stages must stay 1024-byte aligned");
-    static_assert(BM + kStages * kACols <= kTmemCols, "tensor memory holds 512 columns");
+    // Two partial accumulators: k-steps alternate between them, so
+    // consecutive MMAs of a k-block do not wait on each other's results.
+    static constexpr int kAcc = 2;
+    static_assert(kAcc * BM + kStages * kACols <= kTmemCols, "tensor memory holds 512 columns");
     static_assert(kSmem <= 227 * 1024, "shared memory per block");
     static_assert(kTileN * kRedStride * 4 <= kStages * (kXBytes + kWBytes), "reduction buffer fits the ring");
 };
@@ -364,6 +367,22 @@ __device__ __forceinline__ void store_out(float* p, float v, int epi) {
         v = (g / (1.0f + expf(-g))) * v;
     }
     *p = v;
+}
+
+// A 32-column chunk of a tile's accumulator: the sum (fixed order) of its
+// kAcc partial accumulators, `stride` columns apart.
+template <int kAcc>
+__device__ __forceinline__ void acc_ld32(uint32_t taddr, int stride, uint32_t (&v)[32]) {
+    tmem_ld_32x32b_x32(taddr, v);
+    if constexpr (kAcc == 2) {
+        uint32_t w[32];
+        tmem_ld_32x32b_x32(taddr + stride, w);
+        tmem_wait_ld();
+        #pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(w[j]));
+    } else {
+        tmem_wait_ld();
+    }
 }
 
 // Vector form of store_chunk (epi = 0) for a warp whose 32 weight rows
@@ -670,8 +689,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t acc_tmem = tmem;          // columns [0, BM)
-    const uint32_t a_tmem0 = tmem + BM;      // A buffer s at columns BM + kACols * s
+    const uint32_t acc_tmem = tmem;               // partial accumulator p at columns [p BM, (p + 1) BM)
+    const uint32_t a_tmem0 = tmem + C::kAcc * BM;  // A buffer s at columns kAcc BM + kACols s
 
     if (warp == kWarpTma) {
         if (lane == 0) {
@@ -707,8 +726,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
                     // the (j / 4)-th 64-wide atom of the activation tile.
                     const uint64_t bdesc =
                         smem_desc_sw128_kmajor(smem_addr(xs + s * C::kXBytes + (j / 4) * BM * 128));
-                    mma_f16_ts(acc_tmem, a_tmem0 + s * C::kACols + j * 8, bdesc + static_cast<uint64_t>((j % 4) * 2),
-                               idesc, (i | j) != 0 ? 1u : 0u);
+                    mma_f16_ts(acc_tmem + (j % C::kAcc) * BM, a_tmem0 + s * C::kACols + j * 8,
+                               bdesc + static_cast<uint64_t>((j % 4) * 2), idesc, (i > 0 || j >= C::kAcc) ? 1u : 0u);
                 }
                 mma_commit(release0 + 8 * s);
             }
@@ -746,7 +765,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
             // tcgen05.st below is warp-collective: leave together or not at all.
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
-            convert_half<FMT>(ws + s * C::kWBytes, r, group, tmem + lane_addr + BM + s * C::kACols, f, zf);
+            convert_half<FMT>(ws + s * C::kWBytes, r, group, tmem + lane_addr + C::kAcc * BM + s * C::kACols, f, zf);
             #pragma unroll
             for (int q = 0; q < 2; ++q) {
                 f[q] = fn[q];
@@ -783,8 +802,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
             for (int c0 = 0; c0 < BM; c0 += 32) {
                 if (c0 >= M) break;
                 uint32_t v[32];
-                tmem_ld_32x32b_x32(acc_tmem + lane_addr + c0, v);
-                tmem_wait_ld();
+                acc_ld32<C::kAcc>(acc_tmem + lane_addr + c0, BM, v);
                 if (splits > 1) {
                     // The ring is idle: every MMA has finished reading it.
                     float4* dst = reinterpret_cast<float4*>(red + row * C::kRedStride + c0);
@@ -899,7 +917,11 @@ struct PairCfg {
     // Ring slot s is also A buffer s (one release barrier frees both):
     // as many stages as both shared and tensor memory hold.
     static constexpr int kSmemStages = (RX >= 128) ? 4 : (RX >= 64 ? 6 : 8);
-    static constexpr int kTmemStages = (kTmemCols - 2 * RX) / kACols;
+    // Two partial accumulators for narrow tiles (k-steps alternate between
+    // them, so consecutive MMAs do not wait on each other's results); wide
+    // tiles keep one, their MMAs are long enough to hide the dependency.
+    static constexpr int kAcc = RX <= 32 ? 2 : 1;
+    static constexpr int kTmemStages = (kTmemCols - kAcc * 2 * RX) / kACols;
     static constexpr int kStages = kSmemStages < kTmemStages ? kSmemStages : kTmemStages;
     static constexpr int kAStages = kStages;
     static constexpr int kNumBars = 4 * kStages + 3;
@@ -909,7 +931,7 @@ struct PairCfg {
     static constexpr int kStageBytes = kStaged ? 4 * 32 * 32 * 4 : 0;
     static constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16 + 16 + kStageBytes;
     static_assert(kSmem <= 227 * 1024, "shared memory per block");
-    static_assert(2 * RX + kAStages * kACols <= kTmemCols, "tensor memory holds 512 columns");
+    static_assert(kAcc * 2 * RX + kAStages * kACols <= kTmemCols, "tensor memory holds 512 columns");
     static_assert(kXBytes % 1024 == 0, "x16 stages must stay 1024-byte aligned");
 };
 
@@ -991,7 +1013,7 @@ tc_gemm_pair_persist_kernel(const __grid_constant__ CUtensorMap tmap_x, const __
     cluster_sync();  // the peer's barriers exist before anyone arrives on them
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t a_tmem0 = tmem + 2 * kRowsX;  // A buffers after the 2*RX accumulator columns
+    const uint32_t a_tmem0 = tmem + P::kAcc * 2 * kRowsX;  // A buffers after the accumulator columns
 
     // Launched as a programmatic dependent of the x -> f16 prologue. The
     // weights were written before the prologue ran, so the first ring of
@@ -1058,8 +1080,9 @@ tc_gemm_pair_persist_kernel(const __grid_constant__ CUtensorMap tmap_x, const __
                     for (int j = 0; j < kBK / 16; ++j) {
                         const uint64_t bdesc =
                             smem_desc_sw128_kmajor(smem_addr(xs + s * kXBytes + (j / 4) * kRowsX * 128));
-                        mma_f16_ts_pair(tmem, a_tmem0 + s * kACols + j * 8,
-                                        bdesc + static_cast<uint64_t>((j % 4) * 2), idesc, (kb | j) != 0 ? 1u : 0u);
+                        mma_f16_ts_pair(tmem + (j % P::kAcc) * 2 * kRowsX, a_tmem0 + s * kACols + j * 8,
+                                        bdesc + static_cast<uint64_t>((j % 4) * 2), idesc,
+                                        (kb > 0 || j >= P::kAcc) ? 1u : 0u);
                     }
                     mma_commit_pair(release0 + 8 * s, 0x3);
                 }
@@ -1104,7 +1127,8 @@ tc_gemm_pair_persist_kernel(const __grid_constant__ CUtensorMap tmap_x, const __
                     break;
                 }
                 tc_fence_after();
-                convert_half<FMT>(ws + s * kWBytes, r, group, tmem + lane_addr + 2 * kRowsX + s * kACols, f, zf);
+                convert_half<FMT>(ws + s * kWBytes, r, group, tmem + lane_addr + P::kAcc * 2 * kRowsX + s * kACols, f,
+                                  zf);
                 #pragma unroll
                 for (int q = 0; q < 2; ++q) {
                     f[q] = fn[q];
@@ -1146,8 +1170,7 @@ tc_gemm_pair_persist_kernel(const __grid_constant__ CUtensorMap tmap_x, const __
             #pragma unroll 1
             for (int c0 = 0; c0 < rows_m; c0 += 32) {
                 uint32_t v[32];
-                tmem_ld_32x32b_x32(tmem + lane_addr + c0, v);
-                tmem_wait_ld();
+                acc_ld32<P::kAcc>(tmem + lane_addr + c0, 2 * kRowsX, v);
                 if (c0 + 32 >= rows_m) {
                     tc_fence_before();
                     __syncwarp();
@@ -1247,7 +1270,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
     cluster_sync();  // the peer's barriers exist before anyone arrives on them
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t a_tmem0 = tmem + 2 * kRowsX;  // A buffers after the 2*RX accumulator columns
+    const uint32_t a_tmem0 = tmem + P::kAcc * 2 * kRowsX;  // A buffers after the accumulator columns
 
     // Launched as a programmatic dependent of the x -> f16 prologue. The
     // weights were written before the prologue ran, so the first ring of
@@ -1296,8 +1319,9 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
                 #pragma unroll
                 for (int j = 0; j < kBK / 16; ++j) {
                     const uint64_t bdesc = smem_desc_sw128_kmajor(smem_addr(xs + s * kXBytes + (j / 4) * kRowsX * 128));
-                    mma_f16_ts_pair(tmem, a_tmem0 + a * kACols + j * 8, bdesc + static_cast<uint64_t>((j % 4) * 2),
-                                    idesc, (kb | j) != 0 ? 1u : 0u);
+                    mma_f16_ts_pair(tmem + (j % P::kAcc) * 2 * kRowsX, a_tmem0 + a * kACols + j * 8,
+                                    bdesc + static_cast<uint64_t>((j % 4) * 2), idesc,
+                                    (kb > 0 || j >= P::kAcc) ? 1u : 0u);
                 }
                 mma_commit_pair(release0 + 8 * s, 0x3);
             }
@@ -1335,7 +1359,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
             // tcgen05.st is warp-collective: leave together or not at all.
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();
-            convert_half<FMT>(ws + s * kWBytes, r, group, tmem + lane_addr + 2 * kRowsX + a * kACols, f, zf);
+            convert_half<FMT>(ws + s * kWBytes, r, group, tmem + lane_addr + P::kAcc * 2 * kRowsX + a * kACols, f, zf);
             #pragma unroll
             for (int q = 0; q < 2; ++q) {
                 f[q] = fn[q];
@@ -1369,8 +1393,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
             for (int c0 = 0; c0 < 2 * kRowsX; c0 += 32) {
                 if (mp + c0 >= M) break;
                 uint32_t v[32];
-                tmem_ld_32x32b_x32(tmem + lane_addr + c0, v);
-                tmem_wait_ld();
+                acc_ld32<P::kAcc>(tmem + lane_addr + c0, 2 * kRowsX, v);
                 const int n0w = n0 + quarter * 32;  // the warp's first weight row
                 if (vec_out && n0w + 32 <= N) {
                     store_chunk_v(out, rowscale, mp + c0, M - mp - c0, n0w, N, sc, v, stage + quarter * 1024, lane);
