@@ -92,13 +92,14 @@ int popcornDequantizeMatmulLaunchCount(
  * counterpart in the reference; popcorn's ABI has no scratch-free variant.
  *
  * It allocates nothing: its scratch is one fixed device array inside this
- * library (16 MiB for f16 activations + 64 KiB for row scales) that every
- * GPU loading the library holds until the process exits. Limits: K % 16 == 0,
+ * library (16 MiB for the converted activations, 64 KiB for row scales and
+ * 10 MiB for split-K partial tiles) that every GPU loading the library holds
+ * until the process exits. Limits: K % 16 == 0,
  * 16-byte aligned qweight, M <= 16384 and M*K*2 rounded up to 256 bytes
  * <= 16 MiB (for example M = 2048 with K = 4096); anything larger, or a shape
  * the tensor path cannot run, returns POPCORN_ERROR_INVALID_VALUE without
- * launching. Results equal popcornDequantizeMatmulPath_i8f32 with
- * POPCORN_MATMUL_PATH_TENSOR_F16.
+ * launching. It runs the same kernels, so its results equal
+ * popcornDequantizeMatmulPath_i8f32 with POPCORN_MATMUL_PATH_TENSOR_F16.
  *
  * The first call on a device also looks up the array's device address and
  * sets kernel attributes for that device; make that first call before any

@@ -126,6 +126,18 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
         : "memory");
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::i8 (signed 8-bit A and
+// B, s32 accumulate), single CTA. K = 32 per instruction.
+__device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05 op this thread issued so far is done.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -186,6 +198,15 @@ __device__ __forceinline__ uint64_t smem_desc_sw128_kmajor(uint32_t saddr) {
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
     return (1u << 4)                                    // D format: f32
            | (0u << 7) | (0u << 10)                     // A, B format: f16
+           | (static_cast<uint32_t>(n >> 3) << 17)      // N / 8
+           | (static_cast<uint32_t>(m >> 4) << 24);     // M / 16
+}
+
+// Instruction descriptor, kind::i8 with signed 8-bit A and B, s32
+// accumulate (no saturation), both K-major, MMA shape M x N.
+__host__ __device__ constexpr uint32_t idesc_i8_s32(int m, int n) {
+    return (2u << 4)                                    // D format: s32
+           | (1u << 7) | (1u << 10)                     // A, B format: signed 8-bit
            | (static_cast<uint32_t>(n >> 3) << 17)      // N / 8
            | (static_cast<uint32_t>(m >> 4) << 24);     // M / 16
 }

@@ -1,5 +1,11 @@
 // tcgen05 tensor-core dequant-matmul path: out[m, n] = scale[n] * sum_k x[m, k] * q[n, k].
 //
+// Per-channel int8 weights with 4 < M <= 128 take the int8 path at the end
+// of the device code (x_to_i8_*_kernel + tc_i8_kernel): activations as two
+// signed 8-bit digits of a 16-bit fixed-point row, tcgen05.mma.kind::i8 on
+// the raw weight codes, exact int32 sums. Everything else (M > 128, and the
+// per-group int8 / int4 formats at any M) takes the f16 path described here.
+//
 // Same arithmetic contract as popcorn's dequantizeMatmulKernel_i8f32
 // (src/quantize.cu:18-84) except that activations enter the tensor cores as
 // f16: int8 codes are exact in f16, each activation row m is first scaled by
@@ -338,6 +344,260 @@ popcornStatus_t launch_x_to_f16(__half* x16, float* rowscale, const float* x, in
     return check_launch();
 }
 
+// ------------------------------------------- int8 digit prologue (M <= 128)
+// For the int8 tensor path, activation row m becomes the 16-bit fixed-point
+// row X[m, k] = rint(x[m, k] * 32512 / a_m), a_m = max_k |x[m, k]|, so
+// |X| <= 32512 and x[m, k] = X[m, k] * f_m up to half a step, f_m = a_m / 32512.
+// X is stored as two signed 8-bit digits X = 256 hi + lo, hi = (X + 128) >> 8
+// in [-127, 127] and lo in [-128, 127]: hi digits of all rows in plane 0, lo
+// digits in plane 1 of xd [2, M, K]. f_m is stored as a mantissa in [1, 2)
+// (rowfactor[m]) and an exact power of two (rowpow[m]); the epilogue forms
+// ((acc * mantissa) * scale[n]) * power, which overflows or underflows only
+// where the result itself does. Rows with a NaN
+// get f_m = NaN (every output of the row is NaN, as in popcorn's sum). Rows
+// with infinities get f_m = inf and X = +-1 at the infinite entries, 0
+// elsewhere: with one infinity each output is +-inf with the sign of x * w,
+// or NaN where that code is 0 -- popcorn's result exactly; with several,
+// every output is non-finite as popcorn's, but +-inf where popcorn's mixed
+// signs give NaN. An all-zero row gets f_m = 0. Rows with a_m < 2^-100 are
+// scaled by 2^100 (exact) before the division so 32512 / a stays finite.
+struct DigitRow {
+    float pre;   // exact power-of-two pre-scale
+    float mult;  // 32512 / (a_m * pre)
+    int mode;    // 0 finite, 1 infinities (no NaN), 2 NaN
+    float fm;    // f_m = fm * pw: mantissa in [1, 2) (or NaN, inf, 0 for special rows)
+    float pw;    //   and an exact power of two (0 below the smallest denormal)
+};
+
+__device__ __forceinline__ DigitRow digit_row(float a, bool has_nan) {
+    DigitRow d{1.0f, 0.0f, 0, 0.0f, 1.0f};
+    if (has_nan) {
+        d.mode = 2;
+        d.fm = __int_as_float(0x7fc00000);
+    } else if (a > 3.402823466e38f) {
+        d.mode = 1;
+        d.fm = __int_as_float(0x7f800000);
+    } else if (a > 0.0f) {
+        const bool tiny = a < 0x1p-100f;
+        d.pre = tiny ? 0x1p100f : 1.0f;
+        const float ap = a * d.pre;
+        d.mult = 32512.0f / ap;
+        // ap / 32512 lies in [2^-64, 2^114): a normal float, split exactly.
+        const uint32_t b = __float_as_uint(ap / 32512.0f);
+        d.fm = __uint_as_float((b & 0x807FFFFFu) | (127u << 23));
+        const int e = static_cast<int>((b >> 23) & 0xFFu) - 127 - (tiny ? 100 : 0);
+        d.pw = e >= -126 ? __uint_as_float(static_cast<uint32_t>(e + 127) << 23)
+                         : (e >= -149 ? __uint_as_float(1u << (e + 149)) : 0.0f);
+    }
+    return d;
+}
+
+__device__ __forceinline__ int digit_value(float v, const DigitRow& d) {
+    if (d.mode == 1) return (v == __int_as_float(0x7f800000)) ? 1 : ((v == __int_as_float(0xff800000)) ? -1 : 0);
+    if (d.mode == 2) return 0;
+    int X = __float2int_rn((v * d.pre) * d.mult);
+    X = X > 32512 ? 32512 : (X < -32512 ? -32512 : X);
+    return X;
+}
+
+// Four values -> their hi and lo digit bytes, k order.
+__device__ __forceinline__ void digits4(float a, float b, float c, float e, const DigitRow& d, uint32_t& hi,
+                                        uint32_t& lo) {
+    const int X[4] = {digit_value(a, d), digit_value(b, d), digit_value(c, d), digit_value(e, d)};
+    hi = 0;
+    lo = 0;
+    #pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int h = (X[i] + 128) >> 8;
+        const int l = X[i] - h * 256;
+        hi |= (static_cast<uint32_t>(h) & 0xFFu) << (8 * i);
+        lo |= (static_cast<uint32_t>(l) & 0xFFu) << (8 * i);
+    }
+}
+
+// One block per row, the row held in registers (U 16-float slices per
+// thread, K <= 16 * 256 * U); needs K % 16 == 0 and 16-byte aligned x (and
+// norm weights).
+template <int U>
+__global__ void __launch_bounds__(kRowThreads)
+x_to_i8_row_kernel(int8_t* __restrict__ xd, float* __restrict__ rowfactor, float* __restrict__ rowpow,
+                   const float* __restrict__ x, int64_t M, int64_t K, RowNorm nrm) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the GEMM waits for this grid
+    __shared__ float red[2][kRowThreads / 32];
+    __shared__ float ssq[2][kRowThreads / 32];
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int64_t units = K >> 4;
+    int parity = 0;
+    for (int64_t row = blockIdx.x; row < M; row += gridDim.x, parity ^= 1) {
+        const float4* r4 = reinterpret_cast<const float4*>(x + row * K);
+        float4 v[U][4];
+        #pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t unit = tid + static_cast<int64_t>(u) * kRowThreads;
+            #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                v[u][c] = (unit < units) ? __ldg(r4 + unit * 4 + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+        }
+        if (nrm.on) {
+            float ss = 0.0f;
+            #pragma unroll
+            for (int u = 0; u < U; ++u)
+                #pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    ss = fmaf(v[u][c].x, v[u][c].x, ss);
+                    ss = fmaf(v[u][c].y, v[u][c].y, ss);
+                    ss = fmaf(v[u][c].z, v[u][c].z, ss);
+                    ss = fmaf(v[u][c].w, v[u][c].w, ss);
+                }
+            #pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+            if (lane == 0) ssq[parity][warp] = ss;
+            __syncthreads();
+            float total = 0.0f;
+            #pragma unroll
+            for (int w = 0; w < kRowThreads / 32; ++w) total += ssq[parity][w];
+            const float inv = row_inv_rms(total, K, nrm.eps);
+            #pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int64_t unit = tid + static_cast<int64_t>(u) * kRowThreads;
+                #pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    float4 a = v[u][c];
+                    a.x *= inv;
+                    a.y *= inv;
+                    a.z *= inv;
+                    a.w *= inv;
+                    if (nrm.w != nullptr && unit < units) {
+                        const float4 g = __ldg(reinterpret_cast<const float4*>(nrm.w) + unit * 4 + c);
+                        a.x *= g.x;
+                        a.y *= g.y;
+                        a.z *= g.z;
+                        a.w *= g.w;
+                    }
+                    v[u][c] = a;
+                }
+            }
+        }
+        float m = 0.0f;
+        int nan_seen = 0;
+        #pragma unroll
+        for (int u = 0; u < U; ++u)
+            #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float4 a = v[u][c];
+                m = absmax_step(absmax_step(absmax_step(absmax_step(m, a.x), a.y), a.z), a.w);
+                nan_seen |= (a.x != a.x) | (a.y != a.y) | (a.z != a.z) | (a.w != a.w);
+            }
+        #pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float other = __shfl_xor_sync(0xffffffffu, m, off);
+            m = (other > m) ? other : m;
+        }
+        if (lane == 0) red[parity][warp] = m;
+        const bool has_nan = __syncthreads_or(nan_seen) != 0;
+        m = red[parity][0];
+        #pragma unroll
+        for (int w = 1; w < kRowThreads / 32; ++w) {
+            const float other = red[parity][w];
+            m = (other > m) ? other : m;
+        }
+        const DigitRow d = digit_row(m, has_nan);
+        if (tid == 0) {
+            rowfactor[row] = d.fm;
+            rowpow[row] = d.pw;
+        }
+        uint4* hi8 = reinterpret_cast<uint4*>(xd + row * K);
+        uint4* lo8 = reinterpret_cast<uint4*>(xd + (M + row) * K);
+        #pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t unit = tid + static_cast<int64_t>(u) * kRowThreads;
+            if (unit < units) {
+                uint32_t h[4], l[4];
+                #pragma unroll
+                for (int c = 0; c < 4; ++c) digits4(v[u][c].x, v[u][c].y, v[u][c].z, v[u][c].w, d, h[c], l[c]);
+                hi8[unit] = make_uint4(h[0], h[1], h[2], h[3]);
+                lo8[unit] = make_uint4(l[0], l[1], l[2], l[3]);
+            }
+        }
+    }
+}
+
+// Any K (multiple of 16) and alignment of x: one warp per row, two passes
+// over the row (the second from L2).
+__global__ void __launch_bounds__(256)
+x_to_i8_kernel(int8_t* __restrict__ xd, float* __restrict__ rowfactor, float* __restrict__ rowpow,
+               const float* __restrict__ x, int64_t M, int64_t K, RowNorm nrm) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); row < M;
+         row += nwarps) {
+        const float* r = x + row * K;
+        float inv = 1.0f;
+        if (nrm.on) {
+            float ss = 0.0f;
+            for (int64_t k = lane; k < K; k += 32) {
+                const float v = __ldg(r + k);
+                ss = fmaf(v, v, ss);
+            }
+            #pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+            inv = row_inv_rms(ss, K, nrm.eps);
+        }
+        auto val = [&](int64_t k) {
+            float v = __ldg(r + k);
+            if (!nrm.on) return v;
+            v = v * inv;
+            return nrm.w != nullptr ? v * __ldg(nrm.w + k) : v;
+        };
+        float m = 0.0f;
+        int nan_seen = 0;
+        for (int64_t k = lane; k < K; k += 32) {
+            const float v = val(k);
+            m = absmax_step(m, v);
+            nan_seen |= (v != v);
+        }
+        #pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float other = __shfl_xor_sync(0xffffffffu, m, off);
+            m = (other > m) ? other : m;
+        }
+        const bool has_nan = __any_sync(0xffffffffu, nan_seen) != 0;
+        const DigitRow d = digit_row(m, has_nan);
+        if (lane == 0) {
+            rowfactor[row] = d.fm;
+            rowpow[row] = d.pw;
+        }
+        uint32_t* hi4 = reinterpret_cast<uint32_t*>(xd + row * K);
+        uint32_t* lo4 = reinterpret_cast<uint32_t*>(xd + (M + row) * K);
+        for (int64_t c = lane; c < (K >> 2); c += 32) {
+            uint32_t h, l;
+            digits4(val(4 * c), val(4 * c + 1), val(4 * c + 2), val(4 * c + 3), d, h, l);
+            hi4[c] = h;
+            lo4[c] = l;
+        }
+    }
+}
+
+popcornStatus_t launch_x_to_i8(int8_t* xd, float* rowfactor, float* rowpow, const float* x, int64_t M, int64_t K,
+                               cudaStream_t stream, RowNorm nrm) {
+    const bool vec = aligned16(x) && (nrm.w == nullptr || aligned16(nrm.w));
+    const int64_t slices = ceil_div(K / 16, kRowThreads);
+    if (vec && K % 16 == 0 && slices <= 4) {
+        const unsigned g = static_cast<unsigned>(M);  // M <= 128 on this path
+        if (slices == 1) x_to_i8_row_kernel<1><<<g, kRowThreads, 0, stream>>>(xd, rowfactor, rowpow, x, M, K, nrm);
+        else if (slices == 2) x_to_i8_row_kernel<2><<<g, kRowThreads, 0, stream>>>(xd, rowfactor, rowpow, x, M, K, nrm);
+        else x_to_i8_row_kernel<4><<<g, kRowThreads, 0, stream>>>(xd, rowfactor, rowpow, x, M, K, nrm);
+        return check_launch();
+    }
+    x_to_i8_kernel<<<static_cast<unsigned>(ceil_div(M, 8)), 256, 0, stream>>>(xd, rowfactor, rowpow, x, M, K,
+                                                                         nrm);
+    return check_launch();
+}
+
 // Four int8 codes (one word) -> two f16x2 words, exact:
 // (code ^ 0x80) in the low byte of f16 0x6400 gives 1024 + 128 + code;
 // subtracting 1152 leaves the code.
@@ -617,6 +877,67 @@ __device__ __forceinline__ void convert_half(const uint8_t* tile, int r, int g, 
     tmem_st_32x32b_x32(taddr + g * 32, h);
 }
 
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(cluster_addr));
+    return v;
+}
+
+// Split-K fix-up of rank `rank` of a CS-CTA cluster: weight rows
+// [rank * rows, (rank + 1) * rows) of the tile, mq groups of four activation
+// rows each, read from every rank's partial at `red_base` (row stride
+// `red_stride` floats) and summed in rank order 0..CS-1. One unit = one weight
+// row x four activation rows; each of the 128 threads takes units et,
+// et + 128, ... two at a time, with all 2 x CS remote loads issued before
+// the first sum (a distributed-shared-memory load costs several hundred
+// cycles; issued one at a time they dominated the kernel).
+template <int CS>
+__device__ __forceinline__ void split_reduce(uint32_t red_base, int red_stride, int rank, int rows, int mq, int et,
+                                             int n0, int M, int N, const float* rsc,
+                                             const float* __restrict__ rowscale, float* __restrict__ out, int epi) {
+    const int total = rows * mq;
+    for (int u0 = et; u0 < total; u0 += 256) {
+        float4 v[2][CS];
+        #pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int unit = (u0 + h * 128 < total) ? u0 + h * 128 : u0;
+            const int rl = rank * rows + unit % rows;
+            const uint32_t off = static_cast<uint32_t>((rl * red_stride + 4 * (unit / rows)) * 4);
+            #pragma unroll
+            for (int p = 0; p < CS; ++p) v[h][p] = ld_dsmem_f4(mapa_shared(red_base + off, static_cast<uint32_t>(p)));
+        }
+        #pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int unit = u0 + h * 128;
+            if (unit >= total) break;
+            const int rl = rank * rows + unit % rows;  // weight row within the tile
+            const int m = 4 * (unit / rows);
+            float4 acc = v[h][0];
+            #pragma unroll
+            for (int p = 1; p < CS; ++p) {
+                acc.x += v[h][p].x;
+                acc.y += v[h][p].y;
+                acc.z += v[h][p].z;
+                acc.w += v[h][p].w;
+            }
+            const int nn = n0 + rl;
+            if (nn < N) {
+                const float sc = rsc[rl];
+                const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+                #pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    if (m + k < M) {
+                        store_out(out + static_cast<int64_t>(m + k) * N + nn, (a4[k] * __ldg(rowscale + m + k)) * sc,
+                                  epi);
+                    }
+                }
+            }
+        }
+    }
+}
+
 // Split-K over a cluster: with `splits` = C > 1 the C CTAs of a cluster
 // (consecutive blockIdx.x) share one 128-row tile, rank r taking k-blocks
 // [num_kb * r / C, num_kb * (r + 1) / C). Each rank copies its accumulator
@@ -831,37 +1152,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant
             const int rows = kTileN / splits;
             const int mq = ((M < BM ? M : BM) + 3) / 4;  // 4-column groups the epilogue wrote
             const uint32_t red_base = smem_addr(red);
-            for (int unit = et; unit < rows * mq; unit += 128) {
-                const int rl = rank * rows + unit % rows;  // weight row within the tile
-                const int m = 4 * (unit / rows);
-                const uint32_t off = static_cast<uint32_t>((rl * C::kRedStride + m) * 4);
-                float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                for (int p = 0; p < splits; ++p) {
-                    float4 v;
-                    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-                                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                                 : "r"(mapa_shared(red_base + off, static_cast<uint32_t>(p))));
-                    if (p == 0) {
-                        acc = v;
-                    } else {
-                        acc.x += v.x;
-                        acc.y += v.y;
-                        acc.z += v.z;
-                        acc.w += v.w;
-                    }
-                }
-                const int nn = n0 + rl;
-                if (nn < N) {
-                    const float sc = rsc[rl];
-                    const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
-                    #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        if (m + k < M) {
-                            store_out(out + static_cast<int64_t>(m + k) * N + nn, (a4[k] * __ldg(rowscale + m + k)) * sc,
-                                      epi);
-                        }
-                    }
-                }
+            if (splits == 2) {
+                split_reduce<2>(red_base, C::kRedStride, rank, rows, mq, et, n0, M, N, rsc, rowscale, out, epi);
+            } else if (splits == 4) {
+                split_reduce<4>(red_base, C::kRedStride, rank, rows, mq, et, n0, M, N, rsc, rowscale, out, epi);
+            } else {
+                split_reduce<8>(red_base, C::kRedStride, rank, rows, mq, et, n0, M, N, rsc, rowscale, out, epi);
             }
         }
         // No rank may leave while another still reads its shared memory.
@@ -1417,6 +1713,254 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
     }
 }
 
+// ---------------------------------------------- int8 tensor path (M <= 128)
+// Per-channel int8 weights, M <= 128 activation rows: the weight codes go
+// from TMA straight into tcgen05.mma.kind::i8 as the A operand (shared
+// memory, 128B swizzle), with no conversion. The B operand of a k-block is
+// the [2 BM x 128] int8 tile of the prologue's digit planes (hi digits of
+// the BM rows, then their lo digits), so each M=128, N=2 BM, K=32
+// instruction adds the exact int32 dot products of both digits. The
+// epilogue forms ((256 hi + lo) * mantissa_m) * scale[n] * 2^e_m in f32.
+//
+// Bounds: |code * digit| <= 128 * 128, so the int32 sums cannot wrap for
+// K <= 131071 (the path is taken for K <= 65536).
+//
+// Warp roles (6 warps): 0 TMA producer, 1 MMA issuer (and tensor-memory
+// owner), 2-5 epilogue (warp w reads tensor-memory lanes 32 (w % 4) ..).
+// Split-K over a cluster of C CTAs when the 128-row tiles fill less than
+// half the GPU: each rank writes its f32 partial tile [BM][128] to global
+// scratch (L2), and after a cluster barrier rank r sums weight rows
+// [128 r / C, 128 (r + 1) / C) over the C partials in rank order.
+constexpr int kI8Threads = 192;
+constexpr int kI8WarpEpi0 = 2;
+
+template <int BM>
+struct CfgI8 {
+    static constexpr int kBK = 128;                  // k-block depth (int8 elements = bytes)
+    static constexpr int kN = 2 * BM;                // MMA N: hi and lo digit rows
+    static constexpr int kXBytes = kN * kBK;         // digit tile per stage
+    static constexpr int kWBytes = kTileN * kBK;     // weight tile per stage
+    static constexpr int kStages = BM >= 128 ? 4 : (BM >= 64 ? 6 : 8);
+    static constexpr int kAcc = 2;                   // k-steps alternate between two accumulators
+    static constexpr int kTmemCols = kAcc * kN;      // 128, 256 or 512
+    static constexpr int kNumBars = 2 * kStages + 2;
+    static constexpr bool kStaged = BM >= 64;
+    static constexpr int kStageBytes = kStaged ? 4 * 32 * 32 * 4 : 0;
+    static constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16 + 16 + kStageBytes;
+    static_assert(kXBytes % 1024 == 0 && kWBytes % 1024 == 0, "stages stay 1024-byte aligned");
+    static_assert(kTmemCols == 128 || kTmemCols == 256 || kTmemCols == 512, "tensor-memory allocation");
+    static_assert(kSmem <= 227 * 1024, "shared memory per block");
+};
+
+template <int BM>
+__global__ void __launch_bounds__(kI8Threads, 1)
+tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+             float* __restrict__ out, const float* __restrict__ scale, const float* __restrict__ rowfactor,
+             const float* __restrict__ rowpow, float* __restrict__ part, int M, int N, int K, int splits, int epi) {
+    using C = CfgI8<BM>;
+    constexpr int S = C::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* xs = smem;                                  // S x [2 BM][128] digits, 128B swizzle
+    uint8_t* ws = smem + S * C::kXBytes;                 // S x [128][128] weight codes, 128B swizzle
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ws + S * C::kWBytes);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+    float* stage = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(tmem_slot + 4) + 15) & ~uintptr_t(15));
+
+    // full[s]: stage s landed. release[s]: the MMAs reading stage s finished.
+    const uint32_t full0 = smem_addr(bars);
+    const uint32_t release0 = full0 + 8 * S;
+    const uint32_t acc_full = release0 + 8 * S;
+    const uint32_t drain = acc_full + 8;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int rank = static_cast<int>(blockIdx.x) % splits;
+    const int n0 = (static_cast<int>(blockIdx.x) / splits) * kTileN;
+    const int num_kb = (K + C::kBK - 1) / C::kBK;
+    const int kb0 = num_kb * rank / splits;
+    const int n_kb = num_kb * (rank + 1) / splits - kb0;
+    unsigned int* err = &g_tc_error;
+    const bool vec_out = C::kStaged && epi == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && (N & 3) == 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(release0 + 8 * s, 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmap_x);
+        tma_prefetch_desc(&tmap_w);
+        // Weights were written before the prologue ran: warm L2 with this
+        // CTA's first tiles while the prologue finishes.
+        for (int i = 0; i < S && i < n_kb; ++i) tma_prefetch_l2_2d(&tmap_w, (kb0 + i) * C::kBK, n0);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_addr(tmem_slot), C::kTmemCols);
+        tmem_relinquish();
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;  // accumulator p at columns [p 2BM, (p + 1) 2BM): hi at +0, lo at +BM
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int i = 0; i < n_kb; ++i) {
+                const int s = i % S;
+                if (i >= S && !mbar_wait(release0 + 8 * s, ((i / S) - 1) & 1, err, 1u)) break;
+                const int kb = kb0 + i;
+                mbar_arrive_expect_tx(full0 + 8 * s, C::kXBytes + C::kWBytes);
+                tma_load_2d(smem_addr(xs + s * C::kXBytes), &tmap_x, kb * C::kBK, 0, full0 + 8 * s);
+                tma_load_2d(smem_addr(xs + s * C::kXBytes + BM * C::kBK), &tmap_x, kb * C::kBK, M, full0 + 8 * s);
+                tma_load_2d(smem_addr(ws + s * C::kWBytes), &tmap_w, kb * C::kBK, n0, full0 + 8 * s);
+            }
+            // Nothing of ours may still be landing in shared memory at exit.
+            for (int i = (n_kb > S ? n_kb - S : 0); i < n_kb; ++i) {
+                mbar_wait(full0 + 8 * (i % S), (i / S) & 1, err, 64u);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_i8_s32(kTileN, C::kN);
+            for (int i = 0; i < n_kb; ++i) {
+                const int s = i % S;
+                if (!mbar_wait(full0 + 8 * s, (i / S) & 1, err, 2u)) break;
+                tc_fence_after();
+                const uint64_t adesc = smem_desc_sw128_kmajor(smem_addr(ws + s * C::kWBytes));
+                const uint64_t bdesc = smem_desc_sw128_kmajor(smem_addr(xs + s * C::kXBytes));
+                #pragma unroll
+                for (int j = 0; j < C::kBK / 32; ++j) {
+                    // K step of 32 int8 = 32 bytes inside the 128-byte swizzle rows.
+                    mma_i8_ss(tmem + (j % C::kAcc) * C::kN, adesc + static_cast<uint64_t>(2 * j),
+                              bdesc + static_cast<uint64_t>(2 * j), idesc, (i > 0 || j >= C::kAcc) ? 1u : 0u);
+                }
+                mma_commit(release0 + 8 * s);
+            }
+            mma_commit(acc_full);
+            // Every MMA must be finished before tensor memory is released.
+            mma_commit(drain);
+            mbar_wait(drain, 0, err, 128u);
+        }
+    } else {
+        // Epilogue: lane = weight row n, 32 activation rows per chunk.
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const int n = n0 + row;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        const float sc = n < N ? __ldg(scale + n) : 0.0f;
+        const bool ok = mbar_wait(acc_full, 0, err, 32u) && n_kb > 0;
+        if (__all_sync(0xffffffffu, ok)) {
+            tc_fence_after();
+            #pragma unroll 1
+            for (int c0 = 0; c0 < BM; c0 += 32) {
+                if (c0 >= M) break;
+                uint32_t h0[32], h1[32];
+                tmem_ld_32x32b_x32(tmem + lane_addr + c0, h0);
+                tmem_ld_32x32b_x32(tmem + lane_addr + C::kN + c0, h1);
+                tmem_wait_ld();
+                #pragma unroll
+                for (int j = 0; j < 32; ++j) h0[j] = static_cast<uint32_t>(static_cast<int>(h0[j]) + static_cast<int>(h1[j]));
+                uint32_t l0[32];
+                tmem_ld_32x32b_x32(tmem + lane_addr + BM + c0, l0);
+                tmem_ld_32x32b_x32(tmem + lane_addr + C::kN + BM + c0, h1);
+                tmem_wait_ld();
+                uint32_t v[32];
+                #pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int lo = static_cast<int>(l0[j]) + static_cast<int>(h1[j]);
+                    v[j] = __float_as_uint(fmaf(256.0f, static_cast<float>(static_cast<int>(h0[j])),
+                                                static_cast<float>(lo)));
+                }
+                if (splits == 1) {
+                    // (acc * mantissa_m) * scale[n] here; the stores multiply by 2^e_m.
+                    float fm[32];
+                    if (M - c0 >= 32) {
+                        const float4* f4 = reinterpret_cast<const float4*>(rowfactor + c0);
+                        #pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const float4 f = __ldg(f4 + q);
+                            fm[4 * q] = f.x;
+                            fm[4 * q + 1] = f.y;
+                            fm[4 * q + 2] = f.z;
+                            fm[4 * q + 3] = f.w;
+                        }
+                    } else {
+                        #pragma unroll
+                        for (int j = 0; j < 32; ++j) fm[j] = (c0 + j < M) ? __ldg(rowfactor + c0 + j) : 0.0f;
+                    }
+                    #pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = __float_as_uint((__uint_as_float(v[j]) * fm[j]) * sc);
+                }
+                if (splits > 1) {
+                    // Partial tile of this rank: [BM activation rows][128 weight rows].
+                    float* dst = part + (static_cast<size_t>(blockIdx.x) * BM + c0) * kTileN + row;
+                    #pragma unroll
+                    for (int j = 0; j < 32; ++j) dst[j * kTileN] = __uint_as_float(v[j]);
+                } else if (vec_out && n0 + quarter * 32 + 32 <= N) {
+                    store_chunk_v(out, rowpow, c0, M - c0, n0 + quarter * 32, N, 1.0f, v, stage + quarter * 1024,
+                                  lane);
+                } else if (n < N) {
+                    store_chunk(out, rowpow, c0, M - c0, n, N, 1.0f, v, epi);
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (splits > 1) {
+        // Every rank's partial is in global memory (release/acquire at
+        // cluster scope orders the stores before the loads below).
+        cluster_sync();
+        if (warp >= kI8WarpEpi0) {
+            const int et = threadIdx.x - kI8WarpEpi0 * 32;  // 0..127
+            const int rows = kTileN / splits;
+            const int mq = ((M < BM ? M : BM) + 3) / 4;
+            const int tile = static_cast<int>(blockIdx.x) / splits;
+            for (int unit = et; unit < rows * mq; unit += 128) {
+                const int rl = rank * rows + unit % rows;  // weight row within the tile
+                const int m = 4 * (unit / rows);
+                float p4[8][4];
+                #pragma unroll
+                for (int p = 0; p < 8; ++p) {
+                    if (p < splits) {
+                        const float* src = part + (static_cast<size_t>(tile * splits + p) * BM + m) * kTileN + rl;
+                        #pragma unroll
+                        for (int k = 0; k < 4; ++k) p4[p][k] = __ldcg(src + k * kTileN);
+                    }
+                }
+                const int nn = n0 + rl;
+                if (nn < N) {
+                    const float s_n = __ldg(scale + nn);
+                    #pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        float acc = p4[0][k];
+                        #pragma unroll
+                        for (int p = 1; p < 8; ++p) {
+                            if (p < splits) acc += p4[p][k];
+                        }
+                        if (m + k < M) {
+                            store_out(out + static_cast<int64_t>(m + k) * N + nn,
+                                      ((acc * __ldg(rowfactor + m + k)) * s_n) * __ldg(rowpow + m + k), epi);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, C::kTmemCols);
+    }
+}
+
 // ------------------------------------------------------------------ host side
 constexpr int kMaxDevices = 64;
 
@@ -1670,6 +2214,193 @@ popcornStatus_t launch_tc_gemm(PFN_cuTensorMapEncodeTiled_v12000 encode, __half*
     }
 }
 
+// ---------------------------------------------------- int8 path, host side
+bool g_i8_attr_set[kMaxDevices][3] = {};
+
+template <int BM>
+int i8_slot() {
+    return BM == 32 ? 0 : (BM == 64 ? 1 : 2);
+}
+
+// Cluster size for the int8 path's split-K: the largest C in {8, 4, 2}
+// that keeps every CTA of the grid resident at once and leaves each rank
+// >= 4 k-blocks; 1 when the tiles alone fill half the GPU.
+template <int BM>
+int pick_splits_i8(int64_t tiles, int64_t num_kb) {
+    using C = CfgI8<BM>;
+    static int cache[kMaxDevices][3][3] = {};  // [dev][slot][log2 C - 1]: 0 unknown, 1 no, 2 + clusters
+    const int64_t sms = device_sm_count();
+    if (tiles * 2 > sms) return 1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    for (int c = 8; c >= 2; c >>= 1) {
+        if (tiles * c > sms || num_kb < 4 * c) continue;
+        const int li = c == 8 ? 2 : (c == 4 ? 1 : 0);
+        int* known = (dev >= 0 && dev < kMaxDevices) ? &cache[dev][i8_slot<BM>()][li] : nullptr;
+        int clusters = 0;
+        if (known == nullptr || *known == 0) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(static_cast<unsigned>(c));
+            cfg.blockDim = dim3(kI8Threads);
+            cfg.dynamicSmemBytes = C::kSmem;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = static_cast<unsigned>(c);
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            if (cudaOccupancyMaxActiveClusters(&clusters, tc_i8_kernel<BM>, &cfg) != cudaSuccess) {
+                cudaGetLastError();
+                clusters = 0;
+            }
+            if (known != nullptr) *known = clusters > 0 ? 2 + clusters : 1;
+        } else {
+            clusters = *known >= 2 ? *known - 2 : 0;
+        }
+        if (clusters >= tiles) return c;
+    }
+    return 1;
+}
+
+template <int BM>
+popcornStatus_t i8_set_attr() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < kMaxDevices && !g_i8_attr_set[dev][i8_slot<BM>()]) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(tc_i8_kernel<BM>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgI8<BM>::kSmem);
+        if (e != cudaSuccess) return record_cuda(e);
+        g_i8_attr_set[dev][i8_slot<BM>()] = true;
+    }
+    return POPCORN_SUCCESS;
+}
+
+template <int BM>
+popcornStatus_t launch_i8(PFN_cuTensorMapEncodeTiled_v12000 encode, const int8_t* xd, const float* rowfactor,
+                          const float* rowpow, float* part, int splits, float* out, const void* q, const float* scale, int64_t M,
+                          int64_t N, int64_t K, int epi, cudaStream_t stream) {
+    using C = CfgI8<BM>;
+    popcornStatus_t st = i8_set_attr<BM>();
+    if (st != POPCORN_SUCCESS) return st;
+    // Digit planes xd [2 M, K] in [BM x 128] boxes; weight codes [N, K] in
+    // [128 x 128] boxes; both 128-byte swizzled, zero fill past the edges.
+    CUtensorMap tx, tw;
+    const cuuint64_t xdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(2 * M)};
+    const cuuint64_t xstride[1] = {static_cast<cuuint64_t>(K)};
+    const cuuint32_t xbox[2] = {static_cast<cuuint32_t>(C::kBK), static_cast<cuuint32_t>(BM)};
+    const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+    const cuuint64_t wstride[1] = {static_cast<cuuint64_t>(K)};
+    const cuuint32_t wbox[2] = {static_cast<cuuint32_t>(C::kBK), kTileN};
+    const cuuint32_t estride[2] = {1, 1};
+    if (encode(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(xd), xdims, xstride, xbox, estride,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+        encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(q), wdims, wstride, wbox, estride,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+        return POPCORN_ERROR_INVALID_VALUE;
+    }
+    const int64_t tiles = ceil_div(N, kTileN);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(tiles * splits));
+    cfg.blockDim = dim3(kI8Threads);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(splits);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = splits > 1 ? 2 : 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_i8_kernel<BM>, tx, tw, out, scale, rowfactor, rowpow, part,
+                                             static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), splits,
+                                             epi);
+    if (e != cudaSuccess) return record_cuda(e);
+    return check_launch();
+}
+
+// The int8 path applies to per-channel weights with 4 < M <= 128 and
+// K <= 65536 (int32 sums cannot wrap).
+bool i8_path(int64_t M, int64_t K) { return M <= 128 && K <= 65536; }
+
+template <int BM>
+int i8_splits(int64_t N, int64_t K) {
+    return pick_splits_i8<BM>(ceil_div(N, kTileN), ceil_div(K, CfgI8<BM>::kBK));
+}
+
+// Launch plan of one int8-path call: activation tile height, split-K
+// cluster size and the scratch it needs -- digit planes [2, M, K] int8, row
+// mantissas and powers [M] f32 each, split-K partials [tiles * splits][BM][128]
+// f32 -- each region 256-byte aligned.
+struct I8Plan {
+    int bm;
+    int splits;
+    size_t xd_bytes;
+    size_t rf_bytes;
+    size_t part_bytes;
+    size_t total() const { return xd_bytes + 2 * rf_bytes + part_bytes; }
+};
+
+I8Plan i8_plan(int64_t M, int64_t N, int64_t K) {
+    I8Plan p;
+    p.bm = pick_bm(M);
+    p.splits = p.bm == 32 ? i8_splits<32>(N, K) : (p.bm == 64 ? i8_splits<64>(N, K) : i8_splits<128>(N, K));
+    p.xd_bytes = (static_cast<size_t>(2 * M) * K + 255) & ~size_t(255);
+    p.rf_bytes = (static_cast<size_t>(M) * 4 + 255) & ~size_t(255);
+    p.part_bytes =
+        p.splits > 1 ? static_cast<size_t>(ceil_div(N, kTileN)) * p.splits * p.bm * kTileN * sizeof(float) : 0;
+    return p;
+}
+
+// Digit prologue, then the GEMM (and, with q_up, the up-projection GEMM whose
+// epilogue multiplies by silu of the first result), with the plan's scratch
+// regions at xd, rowfactor, rowpow and part.
+popcornStatus_t i8_launch_all(const I8Plan& p, PFN_cuTensorMapEncodeTiled_v12000 encode, int8_t* xd,
+                              float* rowfactor, float* rowpow, float* part, float* out, const float* x,
+                              const int8_t* q, const float* scale, int64_t M, int64_t N, int64_t K,
+                              cudaStream_t stream, RowNorm nrm, const int8_t* q_up, const float* s_up) {
+    auto gemm = [&](const int8_t* qq, const float* ss, int epi) {
+        if (p.bm == 32) {
+            return launch_i8<32>(encode, xd, rowfactor, rowpow, part, p.splits, out, qq, ss, M, N, K, epi, stream);
+        }
+        if (p.bm == 64) {
+            return launch_i8<64>(encode, xd, rowfactor, rowpow, part, p.splits, out, qq, ss, M, N, K, epi, stream);
+        }
+        return launch_i8<128>(encode, xd, rowfactor, rowpow, part, p.splits, out, qq, ss, M, N, K, epi, stream);
+    };
+    popcornStatus_t st = launch_x_to_i8(xd, rowfactor, rowpow, x, M, K, stream, nrm);
+    if (st == POPCORN_SUCCESS) st = gemm(q, scale, 0);
+    if (st == POPCORN_SUCCESS && q_up != nullptr) st = gemm(q_up, s_up, 1);
+    return st;
+}
+
+// The int8 path with its scratch from the stream-ordered pool.
+popcornStatus_t tc_run_i8(float* out, const float* x, const int8_t* q, const float* scale, int64_t M, int64_t N,
+                          int64_t K, cudaStream_t stream, RowNorm nrm, const int8_t* q_up, const float* s_up) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = encode_fn();
+    if (encode == nullptr) return POPCORN_ERROR_INVALID_VALUE;
+    const I8Plan p = i8_plan(M, N, K);
+    cudaMemPool_t pool;
+    cudaError_t e = scratch_pool(&pool);
+    if (e != cudaSuccess) return record_cuda(e);
+    void* scratch = nullptr;
+    e = cudaMallocFromPoolAsync(&scratch, p.total(), pool, stream);
+    if (e != cudaSuccess) return record_cuda(e);
+    uint8_t* base = static_cast<uint8_t*>(scratch);
+    popcornStatus_t st = i8_launch_all(
+        p, encode, reinterpret_cast<int8_t*>(base), reinterpret_cast<float*>(base + p.xd_bytes),
+        reinterpret_cast<float*>(base + p.xd_bytes + p.rf_bytes),
+        p.splits > 1 ? reinterpret_cast<float*>(base + p.xd_bytes + 2 * p.rf_bytes) : nullptr, out, x, q, scale, M,
+        N, K, stream, nrm, q_up, s_up);
+    e = cudaFreeAsync(scratch, stream);
+    if (st == POPCORN_SUCCESS && e != cudaSuccess) st = record_cuda(e);
+    return st;
+}
+
 // x -> f16 prologue into stream-ordered scratch, then the GEMM.
 // x -> f16 prologue (with the optional RMSNorm), then the GEMM; with q_up a
 // second GEMM over the same activations whose epilogue multiplies by
@@ -1717,6 +2448,7 @@ int tc_launch_count(int64_t, int64_t, int64_t) { return 2; }
 
 popcornStatus_t tc_dequant_matmul(float* out, const float* x, const int8_t* q, const float* scale, int64_t M,
                                   int64_t N, int64_t K, cudaStream_t stream) {
+    if (i8_path(M, K)) return tc_run_i8(out, x, q, scale, M, N, K, stream, RowNorm{nullptr, 0.0f, 0}, nullptr, nullptr);
     return tc_run<kFmtChannel>(out, x, q, scale, nullptr, 0, M, N, K, stream);
 }
 
@@ -1733,6 +2465,7 @@ popcornStatus_t tc_dequant_matmul_fused(float* out, const float* x, const float*
                                         const int8_t* q, const float* scale, const int8_t* q_up, const float* s_up,
                                         int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
     const RowNorm nrm{norm_w, eps, norm ? 1 : 0};
+    if (i8_path(M, K)) return tc_run_i8(out, x, q, scale, M, N, K, stream, nrm, q_up, s_up);
     return tc_run<kFmtChannel>(out, x, q, scale, nullptr, 0, M, N, K, stream, nrm, q_up, s_up);
 }
 
@@ -1762,11 +2495,11 @@ popcornStatus_t tc_dequant_matmul_grouped(WeightFormat fmt, float* out, const fl
 // service that accounts for every byte, or an inference server that reserves
 // almost all of HBM for its KV cache), or a real-time loop that forbids any
 // allocation after initialisation so it can never fail or stall mid-run. For
-// them, popcornDequantizeMatmulNoAlloc_i8f32 runs the same two kernels as the
+// them, popcornDequantizeMatmulNoAlloc_i8f32 runs the same kernels as the
 // tensor path with its scratch in the fixed array below instead of the pool.
 //
 // The array is a file-scope device variable: every GPU that loads this
-// library holds it (16 MiB + 64 KiB) until the process exits. In host code
+// library holds it (26 MiB + 64 KiB) until the process exits. In host code
 // its name is only a host-side stand-in, not a device address, so the entry
 // point looks up the real address with cudaGetSymbolAddress once per device
 // (with that device current) and passes that pointer to the kernels.
@@ -1774,10 +2507,12 @@ popcornStatus_t tc_dequant_matmul_grouped(WeightFormat fmt, float* out, const fl
 namespace pcb {
 namespace {
 
-constexpr size_t kNoAllocX16Bytes = size_t(16) << 20;  // f16 activations
-constexpr size_t kNoAllocRowBytes = size_t(64) << 10;  // f32 row scales
+constexpr size_t kNoAllocX16Bytes = size_t(16) << 20;   // f16 activations, or int8 digit planes
+constexpr size_t kNoAllocRowBytes = size_t(64) << 10;   // f32 row scales (row mantissas and powers)
+constexpr size_t kNoAllocPartBytes = size_t(10) << 20;  // split-K partials of the int8 path
 
-static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocX16Bytes + kNoAllocRowBytes];
+static __device__ __align__(256) unsigned char
+    g_noalloc_scratch[kNoAllocX16Bytes + kNoAllocRowBytes + kNoAllocPartBytes];
 
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[kMaxDevices] = {};
@@ -1826,9 +2561,22 @@ extern "C" popcornStatus_t popcornDequantizeMatmulNoAlloc_i8f32(float* out, cons
     __half* x16 = static_cast<__half*>(scratch);
     float* rowscale = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + kNoAllocX16Bytes);
 
-    // The prologue writes every x16 element and row scale the GEMM reads (tile
-    // edges past M or K are zero-filled by TMA, not read from the array), so
+    // The prologue writes every activation element and row scale the GEMM
+    // reads (tile edges past M or K are zero-filled by TMA, not read from the
+    // array), and every split-K partial is written before it is read, so
     // nothing left in the array by an earlier call needs clearing.
+    if (i8_path(M, K)) {
+        const I8Plan p = i8_plan(M, N, K);
+        if (p.xd_bytes > kNoAllocX16Bytes || 2 * p.rf_bytes > kNoAllocRowBytes || p.part_bytes > kNoAllocPartBytes) {
+            return POPCORN_ERROR_INVALID_VALUE;
+        }
+        uint8_t* base = static_cast<uint8_t*>(scratch);
+        float* rows = reinterpret_cast<float*>(base + kNoAllocX16Bytes);
+        return i8_launch_all(p, encode, reinterpret_cast<int8_t*>(base), rows,
+                             reinterpret_cast<float*>(base + kNoAllocX16Bytes + p.rf_bytes),
+                             reinterpret_cast<float*>(base + kNoAllocX16Bytes + kNoAllocRowBytes), out, x, qweight,
+                             scale, M, N, K, stream, RowNorm{nullptr, 0.0f, 0}, nullptr, nullptr);
+    }
     popcornStatus_t st = launch_x_to_f16(x16, rowscale, x, M, K, stream);
     if (st != POPCORN_SUCCESS) return st;
 

@@ -342,15 +342,16 @@ def test_tensor_path_shapes(cuda, M, N, K):
     ref = oracle.dequant_matmul(x, q, s, fused=True, threads=8)
     err = oracle.normwise_rel_err(got, ref)
     assert err <= TOL_TENSOR, err
-    # f16 activations: expect ~1e-4, far inside the tolerance.
+    # int8 digit activations (M <= 128) ~4e-5, f16 activations (M > 128)
+    # ~1e-4: both far inside the tolerance.
     assert err <= 5e-4, err
 
 
 @pytest.mark.parametrize("M,N,K", [(5, 9600, 512), (16, 9601, 256), (33, 9500, 1024), (64, 9728, 2048),
                                    (100, 10000, 1024), (128, 12288, 4096), (130, 9600, 512)])
 def test_tensor_path_pairs_for_many_weight_tiles(cuda, M, N, K):
-    # More 128-row weight tiles than half the SMs: CTA pairs (cta_group::2)
-    # with 16/32/64/128 activation rows per CTA, odd M and N tails included.
+    # More 128-row weight tiles than half the SMs: one CTA per tile on the
+    # int8 path (M <= 128), CTA pairs (cta_group::2) above; odd M and N tails.
     import torch
 
     x, q, s = random_case(M, N, K, 7 + M + N + K)
@@ -359,6 +360,93 @@ def test_tensor_path_pairs_for_many_weight_tiles(cuda, M, N, K):
     ref = oracle.dequant_matmul(x, q, s, fused=True, threads=8)
     err = oracle.normwise_rel_err(got, ref)
     assert err <= 5e-4, err
+
+
+# ---------------------------------------------------------------------------
+# The int8 tensor path (per-channel weights, 4 < M <= 128): activations as two
+# signed 8-bit digits of a 16-bit fixed-point row, tcgen05.mma.kind::i8 on the
+# raw weight codes, split-K partials summed through L2 when tiles are few.
+# ---------------------------------------------------------------------------
+TOL_I8 = 2e-4  # normwise; the 16-bit rows give ~4e-5
+
+
+@pytest.mark.parametrize("M,N,K", [
+    (5, 4096, 4096),      # 32 tiles: cluster split-K, BM = 32
+    (32, 4096, 4096),
+    (64, 4096, 11008),    # split-K with ragged k-block shares, K tail
+    (128, 4096, 4096),    # BM = 128
+    (100, 2000, 8192),    # 16 tiles: 8-way split, N tail
+    (17, 11008, 4096),    # 86 tiles, no split
+    (128, 12288, 4096),
+    (65, 300, 16),        # a single, mostly zero-filled k-block
+])
+def test_int8_tensor_path_shapes(cuda, M, N, K):
+    import torch
+
+    x, q, s = random_case(M, N, K, 11 * M + N + K)
+    got = abi_matmul(torch, cuda, x, q, s)
+    assert pc.device_errors() == 0
+    ref = oracle.dequant_matmul(x, q, s, fused=True, threads=8)
+    assert oracle.normwise_rel_err(got, ref) <= TOL_I8
+
+
+@pytest.mark.parametrize("M,K,x_off", [(48, 20480, 0), (33, 4096, 1), (9, 2064, 3)])
+def test_int8_tensor_path_prologue_forms(cuda, M, K, x_off):
+    # K beyond the row-in-registers prologue and unaligned activations: the
+    # warp-per-row digit prologue.
+    import torch
+
+    N = 1024
+    x, q, s = random_case(M, N, K, 5 + M + K)
+    got = abi_matmul(torch, cuda, x, q, s, x_offset=x_off)
+    assert pc.device_errors() == 0
+    assert oracle.normwise_rel_err(got, oracle.dequant_matmul(x, q, s, fused=True, threads=8)) <= TOL_I8
+
+
+def test_int8_tensor_path_special_rows(cuda):
+    # Magnitudes from 1e-33 (pre-scaled by 2^100) to 1e35, an all-zero row, a
+    # NaN row, rows with one or two infinities of the same sign.
+    import torch
+
+    M, N, K = 12, 4096, 4096
+    x, q, s = random_case(M, N, K, 91)
+    x = x.copy()
+    x[0] *= 1e-33
+    x[1] *= 1e35
+    x[2] = 0.0
+    x[3, 5] = np.nan
+    x[4, 7] = np.inf
+    x[5, 9] = -np.inf
+    x[6, 11] = np.inf
+    x[6, 4000] = np.inf
+    x[7] *= 2.0 ** -100
+    got = abi_matmul(torch, cuda, x, q, s)
+    assert pc.device_errors() == 0
+    ref = oracle.dequant_matmul(x, q, s, fused=True, threads=8)
+    for m in (0, 1, 7, 8, 9, 10, 11):
+        assert oracle.normwise_rel_err(got[m], ref[m]) <= TOL_I8, m
+    assert np.all(got[2] == 0.0)
+    assert np.all(np.isnan(got[3]))
+    for m in (4, 5):
+        # one infinity: +-inf with popcorn's sign, NaN exactly where popcorn's
+        # sum is NaN (the code at the infinite entry is 0)
+        assert np.array_equal(np.isnan(got[m]), np.isnan(ref[m])), m
+        inf = np.isinf(ref[m])
+        assert np.array_equal(got[m][inf], ref[m][inf]), m
+    # two infinities: every output non-finite, as popcorn's (which is NaN
+    # wherever the two terms' signs differ)
+    assert np.all(~np.isfinite(got[6])) and np.all(~np.isfinite(ref[6]))
+
+
+def test_int8_tensor_path_is_deterministic(cuda):
+    # Split-K partials are summed in rank order: repeated calls agree bitwise.
+    import torch
+
+    x, q, s = random_case(96, 4096, 11008, 17)
+    a = abi_matmul(torch, cuda, x, q, s)
+    b = abi_matmul(torch, cuda, x, q, s)
+    assert pc.device_errors() == 0
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
 def test_f32_path_fixed_point_edges(cuda):
