@@ -1746,7 +1746,9 @@ struct CfgI8 {
     static constexpr int kNumBars = 2 * kStages + 2;
     static constexpr bool kStaged = BM >= 64;
     static constexpr int kStageBytes = kStaged ? 4 * 32 * 32 * 4 : 0;
-    static constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16 + 16 + kStageBytes;
+    // ring, barriers, tensor-memory slot, staging tiles, row factors [2][BM]
+    static constexpr int kSmem =
+        1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16 + 16 + kStageBytes + 2 * BM * 4;
     static_assert(kXBytes % 1024 == 0 && kWBytes % 1024 == 0, "stages stay 1024-byte aligned");
     static_assert(kTmemCols == 128 || kTmemCols == 256 || kTmemCols == 512, "tensor-memory allocation");
     static_assert(kSmem <= 227 * 1024, "shared memory per block");
@@ -1803,6 +1805,7 @@ tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__
         tmem_alloc(smem_addr(tmem_slot), C::kTmemCols);
         tmem_relinquish();
     }
+    float* rf_s = stage + C::kStageBytes / 4;  // row factors: [BM] mantissas, then [BM] powers
     asm volatile("griddepcontrol.wait;" ::: "memory");
     tc_fence_before();
     __syncthreads();
@@ -1854,6 +1857,15 @@ tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__
         const int n = n0 + row;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
         const float sc = n < N ? __ldg(scale + n) : 0.0f;
+        // This CTA's row factors, once, into shared memory while the k-loop
+        // runs (named barrier 1: the four epilogue warps only). Loading them
+        // before the block-wide barrier above instead delayed the first
+        // digit tile.
+        for (int i = threadIdx.x - kI8WarpEpi0 * 32; i < BM; i += 128) {
+            rf_s[i] = i < M ? __ldg(rowfactor + i) : 0.0f;
+            rf_s[BM + i] = i < M ? __ldg(rowpow + i) : 0.0f;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
         const bool ok = mbar_wait(acc_full, 0, err, 32u) && n_kb > 0;
         if (__all_sync(0xffffffffu, ok)) {
             tc_fence_after();
@@ -1877,36 +1889,48 @@ tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__
                     v[j] = __float_as_uint(fmaf(256.0f, static_cast<float>(static_cast<int>(h0[j])),
                                                 static_cast<float>(lo)));
                 }
-                if (splits == 1) {
-                    // (acc * mantissa_m) * scale[n] here; the stores multiply by 2^e_m.
-                    float fm[32];
-                    if (M - c0 >= 32) {
-                        const float4* f4 = reinterpret_cast<const float4*>(rowfactor + c0);
-                        #pragma unroll
-                        for (int q = 0; q < 8; ++q) {
-                            const float4 f = __ldg(f4 + q);
-                            fm[4 * q] = f.x;
-                            fm[4 * q + 1] = f.y;
-                            fm[4 * q + 2] = f.z;
-                            fm[4 * q + 3] = f.w;
-                        }
-                    } else {
-                        #pragma unroll
-                        for (int j = 0; j < 32; ++j) fm[j] = (c0 + j < M) ? __ldg(rowfactor + c0 + j) : 0.0f;
-                    }
-                    #pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = __float_as_uint((__uint_as_float(v[j]) * fm[j]) * sc);
-                }
+                const int cnt = M - c0;
                 if (splits > 1) {
                     // Partial tile of this rank: [BM activation rows][128 weight rows].
                     float* dst = part + (static_cast<size_t>(blockIdx.x) * BM + c0) * kTileN + row;
                     #pragma unroll
                     for (int j = 0; j < 32; ++j) dst[j * kTileN] = __uint_as_float(v[j]);
-                } else if (vec_out && n0 + quarter * 32 + 32 <= N) {
-                    store_chunk_v(out, rowpow, c0, M - c0, n0 + quarter * 32, N, 1.0f, v, stage + quarter * 1024,
-                                  lane);
+                    continue;
+                }
+                // ((acc * mantissa_m) * scale[n]) * 2^e_m, row factors from shared memory.
+                float o[32];
+                #pragma unroll
+                for (int j = 0; j < 32; ++j) o[j] = ((__uint_as_float(v[j]) * rf_s[c0 + j]) * sc) * rf_s[BM + c0 + j];
+                if (vec_out && n0 + quarter * 32 + 32 <= N) {
+                    // [32 m][32 n] staging tile of this warp, out as float4 runs along n.
+                    float* st = stage + quarter * 1024;
+                    #pragma unroll
+                    for (int j = 0; j < 32; ++j) st[j * 32 + lane] = o[j];
+                    __syncwarp();
+                    const int q4 = lane & 7;
+                    const int mr = lane >> 3;
+                    #pragma unroll
+                    for (int it = 0; it < 8; ++it) {
+                        const int ml = it * 4 + mr;
+                        if (ml < cnt) {
+                            *reinterpret_cast<float4*>(out + static_cast<int64_t>(c0 + ml) * N + n0 + quarter * 32 +
+                                                       4 * q4) = *reinterpret_cast<const float4*>(st + ml * 32 + 4 * q4);
+                        }
+                    }
+                    __syncwarp();
                 } else if (n < N) {
-                    store_chunk(out, rowpow, c0, M - c0, n, N, 1.0f, v, epi);
+                    float* base = out + static_cast<int64_t>(c0) * N + n;
+                    if (epi) {
+                        #pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (j < cnt) store_out(base + static_cast<int64_t>(j) * N, o[j], 1);
+                        }
+                    } else {
+                        #pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (j < cnt) base[static_cast<int64_t>(j) * N] = o[j];
+                        }
+                    }
                 }
             }
         }
@@ -2222,6 +2246,19 @@ int i8_slot() {
     return BM == 32 ? 0 : (BM == 64 ? 1 : 2);
 }
 
+template <int BM>
+popcornStatus_t i8_set_attr() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < kMaxDevices && !g_i8_attr_set[dev][i8_slot<BM>()]) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(tc_i8_kernel<BM>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgI8<BM>::kSmem);
+        if (e != cudaSuccess) return record_cuda(e);
+        g_i8_attr_set[dev][i8_slot<BM>()] = true;
+    }
+    return POPCORN_SUCCESS;
+}
+
 // Cluster size for the int8 path's split-K: the largest C in {8, 4, 2}
 // that keeps every CTA of the grid resident at once and leaves each rank
 // >= 4 k-blocks; 1 when the tiles alone fill half the GPU.
@@ -2231,6 +2268,9 @@ int pick_splits_i8(int64_t tiles, int64_t num_kb) {
     static int cache[kMaxDevices][3][3] = {};  // [dev][slot][log2 C - 1]: 0 unknown, 1 no, 2 + clusters
     const int64_t sms = device_sm_count();
     if (tiles * 2 > sms) return 1;
+    // The occupancy query needs the kernel's shared-memory size allowed first
+    // (without it the query fails and "no split" would be cached for good).
+    if (i8_set_attr<BM>() != POPCORN_SUCCESS) return 1;
     int dev = 0;
     cudaGetDevice(&dev);
     for (int c = 8; c >= 2; c >>= 1) {
@@ -2261,19 +2301,6 @@ int pick_splits_i8(int64_t tiles, int64_t num_kb) {
         if (clusters >= tiles) return c;
     }
     return 1;
-}
-
-template <int BM>
-popcornStatus_t i8_set_attr() {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < kMaxDevices && !g_i8_attr_set[dev][i8_slot<BM>()]) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(tc_i8_kernel<BM>, cudaFuncAttributeMaxDynamicSharedMemorySize, CfgI8<BM>::kSmem);
-        if (e != cudaSuccess) return record_cuda(e);
-        g_i8_attr_set[dev][i8_slot<BM>()] = true;
-    }
-    return POPCORN_SUCCESS;
 }
 
 template <int BM>
