@@ -63,7 +63,7 @@ WORKLOADS = {
 # produced each figure is in the profiles/ summary named beside it.
 NCU_TRAFFIC = {
     "decode": 16826112,    # profiles/gemv_xs_decode_m1_k4096_n4096.md
-    "skinny": 45422848,    # profiles/tc_gemm_skinny_m32_k4096_n11008.md
+    "skinny": 45440256,    # profiles/tc_i8_skinny_m32_k4096_n11008.md
     "prefill": 35509504,   # profiles/tc_gemm_pair_prefill_m2048_k4096_n4096.md
     "grouped_decode": 17335296,  # profiles/grouped_xs_decode_m1_k4096_n4096_g128.md
     "int4_decode": 9476608,      # profiles/i4_xs_decode_m1_k4096_n4096_g128.md
@@ -439,6 +439,18 @@ def time_e2e(torch, setup, steps, warmup, dist_on):
     return ms, M * K * 4, M * N * 4
 
 
+def compute_dtype(path, M, K, grouped):
+    """Arithmetic of the path a workload takes: f32 on the CUDA-core path;
+    on tensor cores, per-channel int8 weights with M <= 128 (K <= 65536) run
+    tcgen05 kind::i8 on activations held as 16-bit fixed point in two int8
+    digits, everything else f16 x f16 with f32 accumulation."""
+    if "tensor" not in path:
+        return "f32"
+    if not grouped and M <= 128 and K <= 65536:
+        return "s8x(2 s8 digits)->s32"
+    return "f16xf16->f32"
+
+
 def max_over_ranks(torch, value, dist_on, device):
     if not dist_on:
         return value
@@ -638,7 +650,7 @@ def run_ours(args):
         "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None,
-        "dtype": "f32" if setup.path() == "simt_f32" else "f16xf16->f32",
+        "dtype": compute_dtype(setup.path(), wl["M"], wl["K"], bool(wl.get("group_size"))),
         "data": "synthetic: X ~ N(0,1), W ~ N(0,0.02) (torch.randn, fixed seed), int8 per-row via popcornQuantize_f32i8",
         "config": {
             "workload": f"{args.workload} M={wl['M']} K={wl['K']} N={wl['N']}",
