@@ -56,9 +56,10 @@ const char* popcornGetLastCudaErrorString(void);
  * src/quantize.cu:86-112). x is row-major [M, K] f32, qweight is row-major
  * [N, K] int8 (one row per output channel), scale is [N] f32 and out is
  * row-major [M, N] f32. Accumulation is f32. Small problems and M <= 4 run on
- * an f32 CUDA-core path; large problems run on the tcgen05 tensor-core path,
- * whose activations are rounded to f16 after a per-row power-of-two
- * rescaling (normwise relative error well below 2e-3).
+ * an f32 CUDA-core path; large problems run on the tcgen05 tensor-core path:
+ * up to 128 activation rows as 16-bit fixed point per row (two int8 digits,
+ * int8 tensor cores, exact int32 sums), more rows rounded to f16 after a
+ * per-row power-of-two rescaling (normwise relative error well below 2e-3).
  */
 popcornStatus_t popcornDequantizeMatmul_i8f32(
     float* out,

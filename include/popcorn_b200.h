@@ -21,11 +21,15 @@ typedef enum {
      * product is accumulated in f32 (max relative error ~1e-6 normwise).
      * Runs any shape and any alignment. */
     POPCORN_MATMUL_PATH_SIMT_F32 = 1,
-    /* tcgen05 tensor-core path: codes become f16 (exact), each activation row
-     * is rescaled by a power of two and rounded to f16, products accumulate
-     * in f32 in tensor memory (max relative error ~2e-4 normwise). Needs
+    /* tcgen05 tensor-core path. Up to 128 activation rows (K <= 65536): each
+     * row becomes 16-bit fixed point (rint(x * 32512 / max|x|)) held as two
+     * int8 digits, the int8 codes multiply them on the int8 tensor cores with
+     * exact int32 sums (~4e-5 normwise). More rows: codes become f16 (exact),
+     * each activation row is rescaled by a power of two and rounded to f16,
+     * products accumulate in f32 in tensor memory (~2e-4 normwise). Needs
      * K % 16 == 0 and a 16-byte aligned qweight. Takes stream-ordered scratch
-     * of M*K*2 + M*4 bytes from a library-private memory pool. */
+     * (about M*K*2 bytes, plus up to 10 MB of split-K partials) from a
+     * library-private memory pool. */
     POPCORN_MATMUL_PATH_TENSOR_F16 = 2,
 } popcornMatmulPath_t;
 

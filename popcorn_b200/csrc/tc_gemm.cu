@@ -1685,16 +1685,17 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_con
         const bool ok = mbar_wait_cluster(acc_full, 0, err, 32u);
         if (__all_sync(0xffffffffu, ok)) {
             tc_fence_after();
+            // Activation rows of this tile: 2*RX, or fewer in the last tile row.
+            const int rows_m = (M - mp < 2 * kRowsX) ? M - mp : 2 * kRowsX;
             #pragma unroll 1
-            for (int c0 = 0; c0 < 2 * kRowsX; c0 += 32) {
-                if (mp + c0 >= M) break;
+            for (int c0 = 0; c0 < rows_m; c0 += 32) {
                 uint32_t v[32];
                 acc_ld32<P::kAcc>(tmem + lane_addr + c0, 2 * kRowsX, v);
                 const int n0w = n0 + quarter * 32;  // the warp's first weight row
                 if (vec_out && n0w + 32 <= N) {
-                    store_chunk_v(out, rowscale, mp + c0, M - mp - c0, n0w, N, sc, v, stage + quarter * 1024, lane);
+                    store_chunk_v(out, rowscale, mp + c0, rows_m - c0, n0w, N, sc, v, stage + quarter * 1024, lane);
                 } else if (n < N) {
-                    store_chunk(out, rowscale, mp + c0, M - mp - c0, n, N, sc, v, epi);
+                    store_chunk(out, rowscale, mp + c0, rows_m - c0, n, N, sc, v, epi);
                 }
             }
         }

@@ -525,6 +525,38 @@ def test_tensor_path_prefill_full_size(cuda):
     assert err <= TOL_TENSOR, err
 
 
+@pytest.mark.parametrize("fmt", ["channel", "group8", "int4"])
+def test_tensor_path_ragged_prefill_all_formats(cuda, fmt):
+    # M=2000, N=4096: persistent CTA pairs over 128 tiles whose last tile row
+    # holds 208 of 256 activation rows, every weight format, against a
+    # float64 product of the dequantized weights.
+    import torch
+
+    g = torch.Generator(device=cuda)
+    g.manual_seed(21)
+    M, N, K, gs = 2000, 4096, 1024, 128
+    x = torch.randn((M, K), generator=g, device=cuda)
+    w = torch.randn((N, K), generator=g, device=cuda) * 0.02
+    if fmt == "channel":
+        q, s = pc.quantize(w)
+        y = pc.dequantize_matmul(x, q, s)
+        wd = q.double() * s.double()[:, None]
+    elif fmt == "group8":
+        q, s = pc.quantize_grouped(w, gs)
+        y = pc.dequantize_matmul_grouped(x, q, s, gs)
+        wd = q.double() * s.double().repeat_interleave(gs, dim=1)
+    else:
+        q, s, z = pc.quantize_grouped_i4(w, gs)
+        y = pc.dequantize_matmul_grouped_i4(x, q, s, z, gs)
+        codes = torch.stack(((q & 15), (q >> 4)), dim=-1).reshape(N, K).double()
+        wd = (codes - z.double().repeat_interleave(gs, dim=1)) * s.double().repeat_interleave(gs, dim=1)
+    ref = x.double() @ wd.T
+    torch.cuda.synchronize()
+    assert pc.device_errors() == 0
+    err = float((y.double() - ref).abs().max() / ref.abs().max())
+    assert err <= TOL_TENSOR, err
+
+
 def test_tensor_path_skinny_full_size(cuda):
     import torch
 
