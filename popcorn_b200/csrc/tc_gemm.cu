@@ -1878,7 +1878,9 @@ tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__
                 tmem_ld_32x32b_x32(tmem + lane_addr + C::kN + c0, h1);
                 tmem_wait_ld();
                 #pragma unroll
-                for (int j = 0; j < 32; ++j) h0[j] = static_cast<uint32_t>(static_cast<int>(h0[j]) + static_cast<int>(h1[j]));
+                for (int j = 0; j < 32; ++j) {
+                    h0[j] = static_cast<uint32_t>(static_cast<int>(h0[j]) + static_cast<int>(h1[j]));
+                }
                 uint32_t l0[32];
                 tmem_ld_32x32b_x32(tmem + lane_addr + BM + c0, l0);
                 tmem_ld_32x32b_x32(tmem + lane_addr + C::kN + BM + c0, h1);
@@ -1914,8 +1916,8 @@ tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__
                     for (int it = 0; it < 8; ++it) {
                         const int ml = it * 4 + mr;
                         if (ml < cnt) {
-                            *reinterpret_cast<float4*>(out + static_cast<int64_t>(c0 + ml) * N + n0 + quarter * 32 +
-                                                       4 * q4) = *reinterpret_cast<const float4*>(st + ml * 32 + 4 * q4);
+                            float* dst = out + static_cast<int64_t>(c0 + ml) * N + n0 + quarter * 32 + 4 * q4;
+                            *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(st + ml * 32 + 4 * q4);
                         }
                     }
                     __syncwarp();
@@ -2306,8 +2308,8 @@ int pick_splits_i8(int64_t tiles, int64_t num_kb) {
 
 template <int BM>
 popcornStatus_t launch_i8(PFN_cuTensorMapEncodeTiled_v12000 encode, const int8_t* xd, const float* rowfactor,
-                          const float* rowpow, float* part, int splits, float* out, const void* q, const float* scale, int64_t M,
-                          int64_t N, int64_t K, int epi, cudaStream_t stream) {
+                          const float* rowpow, float* part, int splits, float* out, const void* q,
+                          const float* scale, int64_t M, int64_t N, int64_t K, int epi, cudaStream_t stream) {
     using C = CfgI8<BM>;
     popcornStatus_t st = i8_set_attr<BM>();
     if (st != POPCORN_SUCCESS) return st;
