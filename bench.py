@@ -62,7 +62,7 @@ WORKLOADS = {
 # the dominant kernel from one ncu capture of that workload; the command that
 # produced each figure is in the profiles/ summary named beside it.
 NCU_TRAFFIC = {
-    "decode": 16826112,    # profiles/gemv_xs_decode_m1_k4096_n4096.md
+    "decode": 16836864,    # profiles/gemv_xs_decode_m1_k4096_n4096.md
     "skinny": 45440256,    # profiles/tc_i8_skinny_m32_k4096_n11008.md
     "prefill": 35509504,   # profiles/tc_gemm_pair_prefill_m2048_k4096_n4096.md
     "grouped_decode": 17335296,  # profiles/grouped_xs_decode_m1_k4096_n4096_g128.md
