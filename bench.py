@@ -488,8 +488,22 @@ def roofline(wl, ms_per_launch, peaks, workload_name):
             "traffic": NCU_TRAFFIC.get(workload_name)}
 
 
+def _time_host(run, budget_s):
+    """Repeat `run` for about `budget_s` seconds of wall-clock (at least once,
+    at most 200 times, after one untimed call); returns (reps, seconds per call)."""
+    t0 = time.perf_counter()
+    run()
+    one = time.perf_counter() - t0
+    reps = max(1, min(200, int(budget_s / max(one, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        run()
+    return reps, (time.perf_counter() - t0) / reps
+
+
 def cpu_baseline(torch, setup, wl):
-    """popcorn's own CPU loop (oracle/_ref), all host threads, bounded sample."""
+    """popcorn's own CPU loop (oracle/_ref) on all host threads, bounded
+    sample, plus the same loop on one core."""
     import oracle
 
     threads = host_threads()
@@ -501,28 +515,24 @@ def cpu_baseline(torch, setup, wl):
     s = setup.s[0].cpu().numpy()
     rows = q.shape[0]
 
-    def run():
+    def run(nt):
         if use_ref:
-            oracle.ref_dequant_matmul(x, q, s, threads=threads)
+            oracle.ref_dequant_matmul(x, q, s, threads=nt)
         else:
-            oracle.dequant_matmul(x, q, s, threads=threads)
+            oracle.dequant_matmul(x, q, s, threads=nt)
 
-    t0 = time.perf_counter()
-    run()
-    one = time.perf_counter() - t0
-    reps = max(1, min(200, int(2.0 / max(one, 1e-6))))
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        run()
-    dt = (time.perf_counter() - t0) / reps
-    wbytes = rows * K
-    if wl["unit"] == "GB/s":
-        value = wbytes / dt / 1e9
-    else:
-        value = 2.0 * M * rows * K / dt / 1e12
-    return {"value": round(value, 4), "unit": wl["unit"], "cores": threads, "kind": kind,
+    def rate(dt):
+        if wl["unit"] == "GB/s":
+            return rows * K / dt / 1e9
+        return 2.0 * M * rows * K / dt / 1e12
+
+    reps, dt = _time_host(lambda: run(threads), 2.0)
+    reps1, dt1 = _time_host(lambda: run(1), 1.0)
+    return {"value": round(rate(dt), 4), "unit": wl["unit"], "cores": threads, "kind": kind,
             "sample": f"{reps} full calls M={M} K={K} N={rows} (one weight set), {dt*1e3:.2f} ms each, "
-                      f"wall-clock, {threads} threads"}
+                      f"wall-clock, {threads} threads",
+            "single_core": {"value": round(rate(dt1), 4), "unit": wl["unit"], "cores": 1,
+                            "sample": f"{reps1} full calls, {dt1*1e3:.2f} ms each, one thread"}}
 
 
 def stack_shards(torch, pc, dims, layers, rank, world, device, seed):

@@ -116,3 +116,25 @@ def test_clock_summary_without_nvml():
     s.ok = False
     out = s.summary(0, 1, 0, 1)
     assert out["sm_mhz"] is None and out["reasons"] == ["nvml unavailable"]
+
+
+def test_cpu_baseline_runs_on_host_tensors():
+    # The CPU baseline leg on a small case: popcorn's own loop (or the oracle
+    # port) on all threads and on one core, reported in the workload's unit.
+    import types
+
+    import numpy as np
+    import torch
+
+    import oracle
+
+    M, N, K = 1, 256, 512
+    x = torch.from_numpy(oracle.fill_normal(M * K, 0, 1.0).reshape(M, K))
+    q, s = oracle.quantize(oracle.fill_normal(N * K, 1, 0.02).reshape(N, K))
+    setup = types.SimpleNamespace(x=[x], q=[torch.from_numpy(q)], s=[torch.from_numpy(s)])
+    wl = dict(M=M, K=K, N=N, unit="GB/s", bound="hbm")
+    out = bench.cpu_baseline(torch, setup, wl)
+    assert out["unit"] == "GB/s" and out["value"] > 0 and out["cores"] >= 1
+    assert out["kind"] == ("reference" if oracle.have_ref_loops() else "port")
+    assert out["single_core"]["cores"] == 1 and out["single_core"]["value"] > 0
+    assert np.isfinite(out["value"]) and np.isfinite(out["single_core"]["value"])
