@@ -56,6 +56,13 @@ WORKLOADS = {
     # (popcornRMSNormDequantizeMatmulSiluMul_i8f32); algorithmic bytes = both
     # int8 weight matrices. The unfused sequence is timed beside it.
     "mlp_decode": dict(M=1, K=4096, N=11008, unit="GB/s", bound="hbm", mlp=True),
+    # The weight-side kernels around the matmul at the decode layer's size:
+    # popcornQuantize_f32i8 (bytes 5*N*K + 4*N: read f32, write codes and
+    # scales) and popcornDequantize_i8f32 (bytes N*K + 4*N + 4*N*K: read
+    # codes and scales, write f32).
+    "quantize": dict(M=0, K=4096, N=4096, unit="GB/s", bound="hbm", op="quantize"),
+    "dequantize": dict(M=0, K=4096, N=4096, unit="GB/s", bound="hbm", op="dequantize"),
+    "dequantize_bf16": dict(M=0, K=4096, N=4096, unit="GB/s", bound="hbm", op="dequantize", out_bytes=2),
 }
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of
@@ -79,7 +86,7 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
     p.add_argument("--extras", default="skinny,prefill,grouped_decode,int4_decode,grouped_prefill,int4_prefill,"
-                                       "mlp_decode",
+                                       "mlp_decode,quantize,dequantize,dequantize_bf16",
                    help="comma-separated extra single-GPU workloads reported beside the headline (N=1 only)")
     p.add_argument("--stack", default="1,128",
                    help="M values of the 32-layer 7B-shaped linear stack timed at every N ('none' to skip)")
@@ -206,22 +213,30 @@ class Setup:
         self.sets = max(2, math.ceil(pool_bytes / per_set))
         if wl["bound"] == "tensor":
             self.sets = min(self.sets, 4)
+        # Every rank draws the same full matrices and inputs (seeds do not
+        # depend on the rank) and keeps its row shard, so the N-sharded job
+        # computes exactly what one GPU computes over the full weights.
         g = torch.Generator(device=device)
-        g.manual_seed(1234 + rank)
+        lo, hi = rank * self.Nl, (rank + 1) * self.Nl
         self.q, self.s, self.z, self.x, self.out = [], [], [], [], []
+        self.q_full = self.s_full = None
         for i in range(self.sets):
             # W ~ N(0, 0.02) f32 quantized (per row, per group or int4 per
             # group) by this library's quantizer.
-            w = torch.randn((self.Nl, K), generator=g, device=device) * 0.02
+            g.manual_seed(1234 + i)
+            w = torch.randn((N, K), generator=g, device=device) * 0.02
             if self.bits == 4:
                 q, s, z = pc.quantize_grouped_i4(w, self.gs)
-                self.z.append(z)
+                self.z.append(z[lo:hi].contiguous())
             else:
                 q, s = pc.quantize_grouped(w, self.gs) if self.gs else pc.quantize(w)
             del w
-            self.q.append(q)
-            self.s.append(s)
+            if i == 0 and world > 1 and not self.gs:
+                self.q_full, self.s_full = q, s
+            self.q.append(q[lo:hi].contiguous())
+            self.s.append(s[lo:hi].contiguous())
             if wl["bound"] == "tensor" or i == 0:
+                g.manual_seed(99 + i)
                 self.x.append(torch.randn((M, K), generator=g, device=device))
             self.out.append(torch.empty((M, self.Nl), dtype=torch.float32, device=device))
         self.gathered = torch.empty((world * M * self.Nl,), dtype=torch.float32, device=device)
@@ -265,6 +280,28 @@ class Setup:
                                f"{self.lib.popcornGetLastCudaErrorString().decode()}")
         if self.world > 1:
             self.torch.distributed.all_gather_into_tensor(self.gathered, self.out[j].view(-1), group=group)
+
+    def tp_parity(self, stream_handle):
+        """After one sharded step on weight set 0: the gathered [M, N] output
+        against a single-GPU popcornDequantizeMatmul_i8f32 over the full
+        weights on this rank (bit-exact expected: same per-row arithmetic)."""
+        torch = self.torch
+        self.step(0, stream_handle)
+        if self.fused is not None:
+            got = self.full.clone()
+        else:
+            parts = self.gathered.view(self.world, self.M, self.Nl)
+            got = torch.cat([parts[r] for r in range(self.world)], dim=1)
+        ref = torch.empty((self.M, self.N), dtype=torch.float32, device=got.device)
+        st = self.lib.popcornDequantizeMatmul_i8f32(ref.data_ptr(), self.x[0].data_ptr(), self.q_full.data_ptr(),
+                                                    self.s_full.data_ptr(), self.M, self.N, self.K, stream_handle)
+        if st != 0:
+            raise RuntimeError(f"single-GPU reference call failed: {st}")
+        torch.cuda.synchronize()
+        err = float((got.double() - ref.double()).abs().max() / ref.double().abs().max())
+        bitexact = bool(torch.equal(got.view(torch.int32), ref.view(torch.int32)))
+        return {"what": "gathered output vs one GPU over the full weights (same x, set 0)",
+                "max_err": err, "bitexact": bitexact, "ok": bitexact}
 
     def grouped_tensor(self):
         """Per-group formats take the tensor-core path (prologue + GEMM) above
@@ -338,6 +375,54 @@ class MlpSetup:
         return "fused rmsnorm + gate/up + silu*mul" if self.fused else "unfused sequence"
 
 
+LEAD_IN_CYCLES = 2_000_000  # ~1 ms of GPU time at 1.9 GHz
+
+
+def lead_in(torch):
+    """Keep the stream busy (a spin kernel of ~1 ms) while the host enqueues
+    the start event, the graph and the end event, so the events bracket the K
+    steps themselves and not the host's submission latency."""
+    torch.cuda._sleep(LEAD_IN_CYCLES)
+
+
+class OpSetup:
+    """popcornQuantize_f32i8 or popcornDequantize_i8f32 on [N, K], rotating
+    over enough independent buffers that every step reads and writes HBM."""
+
+    def __init__(self, torch, pc, wl, device, pool_bytes):
+        N, K = wl["N"], wl["K"]
+        self.op, self.N, self.K = wl["op"], N, K
+        self.bf16 = wl.get("out_bytes", 4) == 2
+        self.sets = max(2, math.ceil(pool_bytes / weight_bytes(wl)))
+        g = torch.Generator(device=device)
+        g.manual_seed(555)
+        self.w, self.q, self.s = [], [], []
+        for _ in range(self.sets):
+            w = torch.randn((N, K), generator=g, device=device) * 0.02
+            q, sc = pc.quantize(w)
+            self.w.append(w.to(torch.bfloat16) if self.bf16 else w)
+            self.q.append(q)
+            self.s.append(sc)
+        self.lib = pc.load_library()
+        torch.cuda.synchronize()
+
+    def step(self, i, stream_handle, group=None):
+        j = i % self.sets
+        if self.op == "quantize":
+            st = self.lib.popcornQuantize_f32i8(self.q[j].data_ptr(), self.s[j].data_ptr(), self.w[j].data_ptr(),
+                                                self.N, self.K, stream_handle)
+        else:
+            fn = self.lib.popcornDequantize_i8bf16 if self.bf16 else self.lib.popcornDequantize_i8f32
+            st = fn(self.w[j].data_ptr(), self.q[j].data_ptr(), self.s[j].data_ptr(), self.N, self.K, stream_handle)
+        if st != 0:
+            raise RuntimeError(f"{self.op} call failed: {st}")
+
+    def path(self):
+        if self.op == "quantize":
+            return "popcornQuantize_f32i8"
+        return "popcornDequantize_i8bf16 (bf16 out)" if self.bf16 else "popcornDequantize_i8f32 (f32 out)"
+
+
 def time_graph(torch, setup, steps, warmup, soak_s, sampler, dist_on):
     """Warm up, soak, then time exactly `steps` steps from one CUDA graph."""
     stream = torch.cuda.Stream()
@@ -377,6 +462,7 @@ def time_graph(torch, setup, steps, warmup, soak_s, sampler, dist_on):
     torch.cuda.synchronize()
     t_timed0 = time.perf_counter()
     with torch.cuda.stream(stream):
+        lead_in(torch)
         start.record(stream)
         graph.replay()
         end.record(stream)
@@ -390,35 +476,56 @@ def time_graph(torch, setup, steps, warmup, soak_s, sampler, dist_on):
     return ms, clocks
 
 
+def _cudart():
+    """The CUDA runtime torch has loaded (for per-step copies without torch's
+    dispatch overhead)."""
+    import ctypes
+
+    rt = ctypes.CDLL("libcudart.so.12")
+    rt.cudaMemcpyAsync.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
+    rt.cudaMemcpyAsync.restype = ctypes.c_int
+    rt.cudaStreamSynchronize.argtypes = [ctypes.c_void_p]
+    rt.cudaStreamSynchronize.restype = ctypes.c_int
+    return rt
+
+
 def time_e2e(torch, setup, steps, warmup, dist_on):
-    """Same steps through the C ABI with host buffers: pinned H2D of x, the
-    call, pinned D2H of the (gathered) result, every step, stream-synchronized."""
+    """Same steps through the C ABI with host buffers, every step: pinned H2D
+    of x (cudaMemcpyAsync), the library call, pinned D2H of the (gathered)
+    result, and a stream synchronize before the host reads it."""
     M, K, N = setup.M, setup.K, setup.N
     stream = torch.cuda.Stream()
+    sh = stream.cuda_stream
+    rt = _cudart()
+    h2d, d2h = 1, 2  # cudaMemcpyHostToDevice, cudaMemcpyDeviceToHost
     x_host = torch.randn((M, K)).pin_memory()
     y_host = torch.empty((M * N,), dtype=torch.float32).pin_memory()
     x_dev = torch.empty((M, K), dtype=torch.float32, device=setup.x[0].device)
+    xb, yb = M * K * 4, M * N * 4
+    lib = setup.lib
 
     def one(i):
         j = i % setup.sets
-        x_dev.copy_(x_host, non_blocking=True)
+        if rt.cudaMemcpyAsync(x_dev.data_ptr(), x_host.data_ptr(), xb, h2d, sh) != 0:
+            raise RuntimeError("H2D copy failed")
         if setup.fused is not None:
-            st = setup.fused.all_gather(setup.full, x_dev, setup.q[j], setup.s[j], setup.n_offset, stream.cuda_stream)
+            st = setup.fused.all_gather(setup.full, x_dev, setup.q[j], setup.s[j], setup.n_offset, sh)
             if st != 0:
                 raise RuntimeError("popcornDequantizeMatmulAllGather_i8f32 failed in e2e loop")
-            y_host.copy_(setup.full.view(-1), non_blocking=True)
-            stream.synchronize()
-            return
-        st = setup.lib.popcornDequantizeMatmul_i8f32(setup.out[j].data_ptr(), x_dev.data_ptr(), setup.q[j].data_ptr(),
-                                                     setup.s[j].data_ptr(), M, setup.Nl, K, stream.cuda_stream)
-        if st != 0:
-            raise RuntimeError("popcornDequantizeMatmul_i8f32 failed in e2e loop")
-        if setup.world > 1:
-            torch.distributed.all_gather_into_tensor(setup.gathered, setup.out[j].view(-1))
-            y_host.copy_(setup.gathered, non_blocking=True)
+            src = setup.full
         else:
-            y_host.copy_(setup.out[j].view(-1), non_blocking=True)
-        stream.synchronize()
+            st = lib.popcornDequantizeMatmul_i8f32(setup.out[j].data_ptr(), x_dev.data_ptr(), setup.q[j].data_ptr(),
+                                                   setup.s[j].data_ptr(), M, setup.Nl, K, sh)
+            if st != 0:
+                raise RuntimeError("popcornDequantizeMatmul_i8f32 failed in e2e loop")
+            src = setup.out[j]
+            if setup.world > 1:
+                torch.distributed.all_gather_into_tensor(setup.gathered, setup.out[j].view(-1))
+                src = setup.gathered
+        if rt.cudaMemcpyAsync(y_host.data_ptr(), src.data_ptr(), yb, d2h, sh) != 0:
+            raise RuntimeError("D2H copy failed")
+        if rt.cudaStreamSynchronize(sh) != 0:
+            raise RuntimeError("stream synchronize failed")
 
     with torch.cuda.stream(stream):
         for i in range(warmup):
@@ -436,15 +543,19 @@ def time_e2e(torch, setup, steps, warmup, dist_on):
     if dist_on:
         torch.distributed.barrier()
     ms = start.elapsed_time(end)
-    return ms, M * K * 4, M * N * 4
+    return ms, xb, yb
 
 
 def compute_dtype(path, M, K, grouped):
-    """Arithmetic of the path a workload takes: f32 on the CUDA-core path;
-    on tensor cores, per-channel int8 weights with M <= 128 (K <= 65536) run
-    tcgen05 kind::i8 on activations held as 16-bit fixed point in two int8
-    digits, everything else f16 x f16 with f32 accumulation."""
+    """Arithmetic of the path a workload takes. CUDA cores at M = 1 (per
+    channel): each thread's 16-column slice of x as 30-bit fixed point, int8
+    codes, exact dp2a int32 sums, then f32; other CUDA-core cases f32. Tensor
+    cores: per-channel int8 weights with M <= 128 (K <= 65536) run tcgen05
+    kind::i8 on activations held as 16-bit fixed point in two int8 digits,
+    everything else f16 x f16 with f32 accumulation."""
     if "tensor" not in path:
+        if M == 1 and not grouped:
+            return "s30 fixed-point x s8 (dp2a) -> s32/f32"
         return "f32"
     if not grouped and M <= 128 and K <= 65536:
         return "s8x(2 s8 digits)->s32"
@@ -461,7 +572,13 @@ def max_over_ranks(torch, value, dist_on, device):
 
 def weight_bytes(wl):
     """Algorithmic bytes of one call: the codes (int8, or int4 packed two per
-    byte), plus the scales (and int4 zero points) of a grouped layout."""
+    byte), plus the scales (and int4 zero points) of a grouped layout; for
+    the quantizer and dequantizer every byte read and written."""
+    op = wl.get("op")
+    if op == "quantize":
+        return 5 * wl["N"] * wl["K"] + 4 * wl["N"]
+    if op == "dequantize":
+        return wl["N"] * wl["K"] + 4 * wl["N"] + wl.get("out_bytes", 4) * wl["N"] * wl["K"]
     if wl.get("mlp"):
         return 2 * wl["N"] * wl["K"]
     gs = wl.get("group_size")
@@ -535,42 +652,66 @@ def cpu_baseline(torch, setup, wl):
                             "sample": f"{reps1} full calls, {dt1*1e3:.2f} ms each, one thread"}}
 
 
-def stack_shards(torch, pc, dims, layers, rank, world, device, seed):
-    """This rank's shards of `layers` random layers, generated in place.
+def stack_shards(torch, pc, dims, layers, rank, world, device, seed, keep_full=0):
+    """This rank's shards of `layers` random layers, and the full quantized
+    weights of the first `keep_full` layers.
 
-    Each shard is drawn directly (W ~ N(0, 0.02) f32, quantized per row of the
-    shard by popcornQuantize_f32i8); the full matrices never exist.
-    """
-    from popcorn_b200.tp import STACK_PARTS, shard_bounds, stack_part_shape
+    Every matrix is drawn whole from a seed of its own (layer, part) that does
+    not depend on the rank (W ~ N(0, 0.02) f32, quantized per row by
+    popcornQuantize_f32i8), so the ranks' shards are slices of one model:
+    rows of qkv, gate and up (column-parallel), columns of o and down
+    (row-parallel, with the full per-row scale)."""
+    from popcorn_b200.tp import STACK_PARTS, shard_stack_layer, stack_part_shape
 
     g = torch.Generator(device=device)
-    g.manual_seed(seed + 7919 * rank)
-    out = []
-    for _ in range(layers):
-        layer = {}
-        for part in STACK_PARTS:
+    out, full_layers = [], []
+    for li in range(layers):
+        full = {}
+        for pi, part in enumerate(STACK_PARTS):
             N, K = stack_part_shape(dims, part)
-            if part in ("o", "down"):
-                lo, hi = shard_bounds(K, world, rank)
-                shape = (N, hi - lo)
-            else:
-                lo, hi = shard_bounds(N, world, rank)
-                shape = (hi - lo, K)
-            w = torch.randn(shape, generator=g, device=device) * 0.02
-            layer[part] = pc.quantize(w)
+            g.manual_seed(seed + 16 * li + pi)
+            w = torch.randn((N, K), generator=g, device=device) * 0.02
+            full[part] = pc.quantize(w)
             del w
-        out.append(layer)
-    return out
+        out.append(shard_stack_layer(full, rank, world))
+        if li < keep_full:
+            full_layers.append(full)
+        del full
+    return out, full_layers
+
+
+def stack_reference(torch, pc, full_layers, x, world, dims):
+    """The same layers unsharded on this GPU (single-GPU library calls),
+    wired as the sharded stack wires them: the o projection reads, for each
+    rank r, the first o-slice-width columns of r's qkv rows; down reads
+    silu(gate) * up."""
+    from popcorn_b200.tp import shard_bounds
+
+    h = x
+    for w in full_layers:
+        a = pc.dequantize_matmul(h, *w["qkv"])
+        cols = []
+        for r in range(world):
+            qlo, _ = shard_bounds(dims["qkv"], world, r)
+            olo, ohi = shard_bounds(dims["hidden"], world, r)
+            cols.append(a[:, qlo:qlo + (ohi - olo)])
+        h1 = pc.dequantize_matmul(torch.cat(cols, dim=1).contiguous(), *w["o"])
+        glu = pc.dequantize_matmul_silu_mul(h1, *w["gate"], *w["up"])
+        h = pc.dequantize_matmul(glu, *w["down"])
+    return h
 
 
 def time_stack(torch, pc, M, layers, rank, world, device, peaks, dist_on):
     """One pass of the 32-layer stack = one step; K passes from one CUDA graph."""
     from popcorn_b200.tp import STACK_7B, LinearStack, PeerGroup
 
-    shards = stack_shards(torch, pc, STACK_7B, layers, rank, world, device, 4242)
+    check_layers = 2 if world > 1 else 0
+    shards, full_layers = stack_shards(torch, pc, STACK_7B, layers, rank, world, device, 4242, check_layers)
     peer = PeerGroup(M, STACK_7B["hidden"], device) if (world > 1 and M <= 4) else None
     stack = LinearStack(shards, M, STACK_7B, device, peer=peer)
-    x = torch.randn((M, STACK_7B["hidden"]), device=device)
+    gx = torch.Generator(device=device)
+    gx.manual_seed(77 + M)
+    x = torch.randn((M, STACK_7B["hidden"]), generator=gx, device=device)
     stream = torch.cuda.Stream()
     passes = 8
     with torch.cuda.stream(stream):
@@ -590,6 +731,7 @@ def time_stack(torch, pc, M, layers, rank, world, device, peaks, dist_on):
         torch.distributed.barrier()
     torch.cuda.synchronize()
     with torch.cuda.stream(stream):
+        lead_in(torch)
         start.record(stream)
         graph.replay()
         end.record(stream)
@@ -597,6 +739,20 @@ def time_stack(torch, pc, M, layers, rank, world, device, peaks, dist_on):
     ms = max_over_ranks(torch, start.elapsed_time(end), dist_on, device) / passes
     errs = pc.device_errors()
     del graph
+    parity = None
+    if check_layers:
+        # The first layers of the sharded stack (same shards, same collectives)
+        # against the same layers unsharded on this GPU.
+        head = LinearStack(shards[:check_layers], M, STACK_7B, device, peer=peer)
+        with torch.cuda.stream(stream):
+            got = head(x).clone()
+            ref = stack_reference(torch, pc, full_layers, x, world, STACK_7B)
+        torch.cuda.synchronize()
+        err = float((got.double() - ref.double()).abs().max() / ref.double().abs().max())
+        tol = 1e-5 if M <= 4 else 2e-3
+        parity = {"what": f"first {check_layers} layers vs the same layers unsharded on one GPU",
+                  "max_err": err, "tol": tol, "ok": bool(err <= tol) and pc.device_errors() == 0}
+        del head, full_layers
     wbytes = stack.weight_bytes()
     if dist_on:
         t = torch.tensor([wbytes], dtype=torch.int64, device=device)
@@ -613,6 +769,8 @@ def time_stack(torch, pc, M, layers, rank, world, device, peaks, dist_on):
                                 "fused into the GEMV (tagged NVLink peer stores)" if stack.peer is not None
                                 else "NCCL all-reduce"),
            "device_error_bits": errs}
+    if parity is not None:
+        res["tp_parity"] = parity
     if M > 1:
         res["tflops"] = round(2.0 * M * wbytes / (ms * 1e-3) / 1e12, 2)
     del stack, shards, peer
@@ -648,6 +806,15 @@ def run_ours(args):
     ms_step = ms / args.steps
     value = throughput(wl, ms_step)
     launches = setup.launches_per_step()
+    tp_parity = None
+    if dist_on:
+        stream = torch.cuda.Stream()
+        with torch.cuda.stream(stream):
+            tp_parity = setup.tp_parity(stream.cuda_stream)
+        flag = torch.tensor([0 if tp_parity["ok"] else 1], dtype=torch.int32, device=device)
+        torch.distributed.all_reduce(flag)
+        tp_parity["ranks_failing"] = int(flag.item())
+        tp_parity["ok"] = tp_parity["ok"] and tp_parity["ranks_failing"] == 0
 
     line = {
         "metric": METRIC,
@@ -671,13 +838,17 @@ def run_ours(args):
             "path": setup.path(),
             "l2": f"weights rotate over {setup.sets} sets "
                   f"({setup.sets * setup.Nl * wl['K'] / 1e6:.0f} MB per rank > 2x L2 {l2 / 1e6:.0f} MB)",
-            "timing": "K steps replayed from one CUDA graph, CUDA events, max over ranks",
+            "timing": "K steps replayed from one CUDA graph; CUDA events on the launching stream bracket exactly "
+                      "those K steps (a ~1 ms spin kernel ahead of the start event keeps host submission latency "
+                      "out); max over ranks",
         },
         "gpu_launches": launches * args.steps,
         "roofline": roofline(dict(wl, N=setup.Nl), ms_step, peaks, args.workload) if world == 1 else
         roofline(wl, ms_step, dict(peaks, hbm=peaks["hbm"] * world, tc=peaks["tc"] * world), args.workload),
         "clocks": clocks,
     }
+    if tp_parity is not None:
+        line["tp_parity"] = tp_parity
 
     if not args.no_e2e:
         e2e_steps = min(args.steps, 2000)
@@ -686,18 +857,21 @@ def run_ours(args):
         line["e2e"] = {"value": round(throughput(wl, ems / e2e_steps), 2), "unit": wl["unit"],
                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                        "ms_per_step": round(ems / e2e_steps, 6),
-                       "how": "pinned H2D of x + " + ("popcornDequantizeMatmulAllGather_i8f32"
-                                                        if setup.fused is not None else
-                                                        "popcornDequantizeMatmul_i8f32"
-                                                        + (" + NCCL all-gather" if world > 1 else ""))
+                       "how": "pinned H2D of x (cudaMemcpyAsync) + " + (
+                           "popcornDequantizeMatmulAllGather_i8f32" if setup.fused is not None else
+                           "popcornDequantizeMatmul_i8f32" + (" + NCCL all-gather" if world > 1 else ""))
                               + " via ctypes + pinned D2H of the full y, stream-synchronized every step"}
 
     if world == 1 and rank == 0:
         extras = {}
         for name in [e for e in args.extras.split(",") if e in WORKLOADS and e != args.workload]:
             ewl = WORKLOADS[name]
-            es = MlpSetup(torch, pc, ewl, device, pool) if ewl.get("mlp") else Setup(torch, pc, ewl, 0, 1, device,
-                                                                                       pool)
+            if ewl.get("mlp"):
+                es = MlpSetup(torch, pc, ewl, device, pool)
+            elif ewl.get("op"):
+                es = OpSetup(torch, pc, ewl, device, pool)
+            else:
+                es = Setup(torch, pc, ewl, 0, 1, device, pool)
             esteps = 200 if ewl["bound"] == "hbm" else 20
             ems, _ = time_graph(torch, es, esteps, 3, 0.0, None, False)
             eval_ = throughput(ewl, ems / esteps)
@@ -723,9 +897,9 @@ def run_ours(args):
         for m in [int(v) for v in args.stack.split(",") if v]:
             stack[f"m{m}"] = time_stack(torch, pc, m, args.stack_layers, rank, world, device, peaks, dist_on)
         line["stack_7b_linear"] = dict(
-            stack, config="32 layers x (qkv 4096->12288, o 4096->4096, gate and up 4096->11008, down 11008->4096), "
-                          "column-parallel qkv/gate/up, row-parallel o/down, one pass per step from a CUDA graph, "
-                          "max over ranks" if args.stack_layers == 32 else f"{args.stack_layers} layers")
+            stack, config="32 layers x (qkv 4096->12288, o 4096->4096, gate and up 4096->11008 with silu(gate)*up in "
+                          "one fused call, down 11008->4096), column-parallel qkv/gate/up, row-parallel o/down, one "
+                          "pass per step from a CUDA graph, max over ranks" if args.stack_layers == 32 else f"{args.stack_layers} layers")
 
     if rank == 0:
         print(json.dumps(line), flush=True)

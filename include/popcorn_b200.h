@@ -50,6 +50,21 @@ popcornStatus_t popcornDequantize_i8f32(
 );
 
 /*
+ * The same expansion with bf16 output, for callers that keep expanded
+ * weights in bf16 (half the bytes of f32): out[n, k] holds the bf16 bit
+ * pattern of (float)qweight[n, k] * scale[n] -- the f32 product above,
+ * rounded once to nearest even. Bit-exact.
+ */
+popcornStatus_t popcornDequantize_i8bf16(
+    uint16_t* out,
+    const int8_t* qweight,
+    const float* scale,
+    int64_t N,
+    int64_t K,
+    cudaStream_t stream
+);
+
+/*
  * popcornDequantizeMatmul_i8f32 with the kernel path chosen by the caller.
  * Returns POPCORN_ERROR_INVALID_VALUE when `path` cannot run this shape or
  * these pointers (for example the tensor path with K % 16 != 0).

@@ -45,6 +45,7 @@ def _load():
         lib.oracle_dequant_matmul_i8_mt.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _int]
         lib.oracle_quantize_i8.argtypes = [_vp, _vp, _vp, _i64, _i64, _int]
         lib.oracle_dequantize_i8.argtypes = [_vp, _vp, _vp, _i64, _i64]
+        lib.oracle_dequantize_i8_bf16.argtypes = [_vp, _vp, _vp, _i64, _i64]
         lib.oracle_fill_normal.argtypes = [_vp, _i64, ctypes.c_uint64, ctypes.c_float]
         lib.oracle_dequant_matmul_grouped_i8.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int]
         lib.oracle_quantize_grouped_i8.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _int]
@@ -53,7 +54,7 @@ def _load():
         lib.oracle_rmsnorm.argtypes = [_vp, _vp, _vp, _i64, _i64, ctypes.c_float, _int]
         lib.oracle_silu.argtypes = [_vp, _vp, _i64]
         for f in (lib.oracle_rmsnorm, lib.oracle_silu, lib.oracle_dequant_matmul_i8, lib.oracle_dequant_matmul_i8_mt, lib.oracle_quantize_i8,
-                  lib.oracle_dequantize_i8, lib.oracle_fill_normal, lib.oracle_dequant_matmul_grouped_i8,
+                  lib.oracle_dequantize_i8, lib.oracle_dequantize_i8_bf16, lib.oracle_fill_normal, lib.oracle_dequant_matmul_grouped_i8,
                   lib.oracle_quantize_grouped_i8, lib.oracle_dequant_matmul_grouped_i4,
                   lib.oracle_quantize_grouped_i4):
             f.restype = None
@@ -185,6 +186,16 @@ def dequantize(q, scale) -> np.ndarray:
     return out
 
 
+def dequantize_bf16(q, scale) -> np.ndarray:
+    """bf16 bit patterns (uint16) of (float)q[n,k] * scale[n], rounded to nearest even."""
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    scale = np.ascontiguousarray(scale, dtype=np.float32)
+    N, K = q.shape
+    out = np.empty((N, K), dtype=np.uint16)
+    _load().oracle_dequantize_i8_bf16(_ptr(out), _ptr(q), _ptr(scale), N, K)
+    return out
+
+
 def normwise_rel_err(got, ref) -> float:
     """max|got - ref| / max|ref| (the matmul parity metric)."""
     got = np.asarray(got, dtype=np.float64)
@@ -199,6 +210,17 @@ def normwise_rel_err(got, ref) -> float:
 # ---------------------------------------------------------------------------
 # Reference builds (oracle/_ref), present where the reference was compiled.
 # ---------------------------------------------------------------------------
+def reference_checkout():
+    """The popcorn checkout that _ref was built from (recorded by
+    ``make -C oracle ref``), or None when it is not on this machine."""
+    try:
+        with open(os.path.join(_HERE, "_ref", "source_dir")) as f:
+            path = f.read().strip()
+    except OSError:
+        return None
+    return path if os.path.isdir(path) else None
+
+
 def have_ref_loops() -> bool:
     return os.path.exists(REF_LOOPS_LIB)
 

@@ -9,6 +9,7 @@
 #include "oracle.h"
 
 #include <math.h>
+#include <string.h>
 #include <pthread.h>
 #include <stdlib.h>
 
@@ -383,6 +384,24 @@ void oracle_dequantize_i8(float* out, const int8_t* q, const float* scale, int64
     for (int64_t n = 0; n < N; n++) {
         const float sc = scale[n];
         for (int64_t k = 0; k < K; k++) out[n * K + k] = (float)q[n * K + k] * sc;
+    }
+}
+
+/* f32 -> bf16 bit pattern, round to nearest, ties to even (IEEE-754 binary32
+ * truncated to its upper 16 bits after adding half an ulp of the result plus
+ * the tie bit); NaN keeps its sign and becomes a quiet NaN. */
+static uint16_t f32_to_bf16_rne(float f) {
+    uint32_t b;
+    memcpy(&b, &f, 4);
+    if ((b & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((b >> 16) | 0x0040u);
+    b += 0x7FFFu + ((b >> 16) & 1u);
+    return (uint16_t)(b >> 16);
+}
+
+void oracle_dequantize_i8_bf16(uint16_t* out, const int8_t* q, const float* scale, int64_t N, int64_t K) {
+    for (int64_t n = 0; n < N; n++) {
+        const float sc = scale[n];
+        for (int64_t k = 0; k < K; k++) out[n * K + k] = f32_to_bf16_rne((float)q[n * K + k] * sc);
     }
 }
 

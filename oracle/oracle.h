@@ -85,6 +85,10 @@ void oracle_silu(float* out, const float* in, int64_t n);
 /* out[n,k] = (float)q[n,k] * scale[n]. */
 void oracle_dequantize_i8(float* out, const int8_t* q, const float* scale, int64_t N, int64_t K);
 
+/* The same f32 product rounded once to bf16 (nearest, ties to even); out
+ * holds the bf16 bit patterns. */
+void oracle_dequantize_i8_bf16(uint16_t* out, const int8_t* q, const float* scale, int64_t N, int64_t K);
+
 /* Deterministic synthetic data: SplitMix64 stream (Steele, Lea & Flood 2014)
  * feeding an Irwin-Hall(12) normal approximation, sum of twelve 24-bit
  * uniforms minus 6, scaled by sigma. Integer and exactly-rounded float

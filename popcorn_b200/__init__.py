@@ -48,6 +48,7 @@ ABI_SYMBOLS = (
 )
 EXT_SYMBOLS = (
     "popcornDequantize_i8f32",
+    "popcornDequantize_i8bf16",
     "popcornDequantizeMatmulPath_i8f32",
     "popcornDequantizeMatmulSelectPath",
     "popcornDequantizeMatmulLaunchCount",
@@ -58,6 +59,9 @@ EXT_SYMBOLS = (
     "popcornRMSNormDequantizeMatmul_i8f32",
     "popcornDequantizeMatmulSiluMul_i8f32",
     "popcornRMSNormDequantizeMatmulSiluMul_i8f32",
+    "popcornDequantizeMatmulColumnParallel_i8f32",
+    "popcornDequantizeMatmulRowParallel_i8f32",
+    "popcornGetLastNcclError",
 )
 
 TP_MAX_RANKS = 8
@@ -90,6 +94,7 @@ _SIGNATURES = {
     "popcornDequantizeMatmulGrouped_i4f32": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "popcornQuantizeGrouped_f32i4": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "popcornDequantize_i8f32": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
+    "popcornDequantize_i8bf16": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "popcornDequantizeMatmulPath_i8f32": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "popcornDequantizeMatmulSelectPath": (_int, [_vp, _vp, _i64, _i64, _i64]),
     "popcornDequantizeMatmulLaunchCount": (_int, [_vp, _vp, _i64, _i64, _i64, _int]),
@@ -101,6 +106,9 @@ _SIGNATURES = {
     "popcornDequantizeMatmulSiluMul_i8f32": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "popcornRMSNormDequantizeMatmulSiluMul_i8f32": (_int, [_vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp, _vp, _i64,
                                                            _i64, _i64, _vp]),
+    "popcornDequantizeMatmulColumnParallel_i8f32": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "popcornDequantizeMatmulRowParallel_i8f32": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "popcornGetLastNcclError": (_int, []),
 }
 
 _lib = None
@@ -182,6 +190,10 @@ def popcornQuantizeGrouped_f32i4(out, scale, zero, inp, N, K, group_size, stream
 
 def popcornDequantize_i8f32(out, qweight, scale, N, K, stream=0) -> int:
     return load_library().popcornDequantize_i8f32(out, qweight, scale, N, K, stream)
+
+
+def popcornDequantize_i8bf16(out, qweight, scale, N, K, stream=0) -> int:
+    return load_library().popcornDequantize_i8bf16(out, qweight, scale, N, K, stream)
 
 
 def popcornDequantizeMatmulPath_i8f32(out, x, qweight, scale, M, N, K, path, stream=0) -> int:
@@ -372,16 +384,21 @@ def dequantize_matmul_silu_mul(x, q_gate, s_gate, q_up, s_up, norm_weight=None, 
     return out
 
 
-def dequantize(qweight, scale, out=None, stream=None):
-    """f32 [N, K] = qweight[N, K] * scale[N, None]."""
+def dequantize(qweight, scale, out=None, stream=None, dtype=None):
+    """[N, K] = qweight[N, K] * scale[N, None] in f32, or rounded to bf16 with dtype=torch.bfloat16."""
     import torch
 
     N, K = qweight.shape
+    dtype = dtype or (out.dtype if out is not None else torch.float32)
+    if dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("dequantize writes float32 or bfloat16")
     if out is None:
-        out = torch.empty((N, K), dtype=torch.float32, device=qweight.device)
+        out = torch.empty((N, K), dtype=dtype, device=qweight.device)
     st = _stream_handle(stream)
-    _check(
-        popcornDequantize_i8f32(out.data_ptr(), qweight.data_ptr(), scale.data_ptr(), N, K, st),
-        "popcornDequantize_i8f32",
-    )
+    if dtype == torch.bfloat16:
+        _check(popcornDequantize_i8bf16(out.data_ptr(), qweight.data_ptr(), scale.data_ptr(), N, K, st),
+               "popcornDequantize_i8bf16")
+    else:
+        _check(popcornDequantize_i8f32(out.data_ptr(), qweight.data_ptr(), scale.data_ptr(), N, K, st),
+               "popcornDequantize_i8f32")
     return out

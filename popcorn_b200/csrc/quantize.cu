@@ -13,6 +13,8 @@
 // holds it in registers between the max and the quantize step; otherwise one
 // warp per row makes two passes (the second served by L2).
 // Traffic per element: 4 B read from HBM, 1 B written; plus 4 B per row.
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 
 namespace pcb {
@@ -205,6 +207,47 @@ dequantize_kernel(float* __restrict__ out, const int8_t* __restrict__ q,
     }
 }
 
+// The bf16 form: the same f32 product, rounded once to bf16 (nearest even,
+// cvt.rn.bf16x2.f32); each thread expands 16 codes into two 16-byte stores.
+template <bool kVec>
+__global__ void __launch_bounds__(256)
+dequantize_bf16_kernel(uint16_t* __restrict__ out, const int8_t* __restrict__ q,
+                       const float* __restrict__ scale, int64_t N, int64_t K) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (kVec) {
+        const int64_t per_row = K >> 4;
+        const int64_t total = N * per_row;
+        for (; t < total; t += stride) {
+            const int64_t row = t / per_row;
+            const float sc = __ldg(scale + row);
+            const uint4 packed = __ldg(reinterpret_cast<const uint4*>(q) + t);
+            const uint32_t w[4] = {packed.x, packed.y, packed.z, packed.w};
+            uint32_t o[8];
+            #pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float a = static_cast<float>(static_cast<int8_t>(w[j] & 0xffu)) * sc;
+                const float b = static_cast<float>(static_cast<int8_t>((w[j] >> 8) & 0xffu)) * sc;
+                const float c = static_cast<float>(static_cast<int8_t>((w[j] >> 16) & 0xffu)) * sc;
+                const float d = static_cast<float>(static_cast<int8_t>(w[j] >> 24)) * sc;
+                const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b);  // a in the low half
+                const __nv_bfloat162 hi = __floats2bfloat162_rn(c, d);
+                o[2 * j] = *reinterpret_cast<const uint32_t*>(&lo);
+                o[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&hi);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(out) + t * 2;
+            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+    } else {
+        const int64_t total = N * K;
+        for (; t < total; t += stride) {
+            const __nv_bfloat16 v = __float2bfloat16_rn(static_cast<float>(q[t]) * __ldg(scale + t / K));
+            out[t] = *reinterpret_cast<const uint16_t*>(&v);
+        }
+    }
+}
+
 int grid_for(int64_t work_items, int threads) {
     const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
     int64_t g = ceil_div(work_items, threads);
@@ -260,6 +303,21 @@ extern "C" popcornStatus_t popcornDequantize_i8f32(float* out, const int8_t* qwe
         dequantize_kernel<true><<<grid_for(N * (K / 16), 256), 256, 0, stream>>>(out, qweight, scale, N, K);
     } else {
         dequantize_kernel<false><<<grid_for(N * K, 256), 256, 0, stream>>>(out, qweight, scale, N, K);
+    }
+    return check_launch();
+}
+
+extern "C" popcornStatus_t popcornDequantize_i8bf16(uint16_t* out, const int8_t* qweight, const float* scale,
+                                                    int64_t N, int64_t K, cudaStream_t stream) {
+    using namespace pcb;
+    if (out == nullptr || qweight == nullptr || scale == nullptr) return POPCORN_ERROR_INVALID_VALUE;
+    if (N <= 0 || K <= 0) return POPCORN_SUCCESS;
+
+    const bool vec = (K % 16 == 0) && aligned16(qweight) && aligned16(out);
+    if (vec) {
+        dequantize_bf16_kernel<true><<<grid_for(N * (K / 16), 256), 256, 0, stream>>>(out, qweight, scale, N, K);
+    } else {
+        dequantize_bf16_kernel<false><<<grid_for(N * K, 256), 256, 0, stream>>>(out, qweight, scale, N, K);
     }
     return check_launch();
 }

@@ -160,6 +160,63 @@ class PeerGroup:
             q.shape[1], stream_handle)
 
 
+class NcclComm:
+    """An NCCL communicator of its own over the ranks of ``group``, for the C
+    entry points of include/popcorn_tp_nccl.h (which take an ncclComm_t, as a
+    cgo caller holding its own communicator would pass). Rank 0's unique id
+    travels through torch.distributed; ncclCommInitRank runs on ``device``.
+    Uses the libnccl.so.2 already loaded in the process (torch's)."""
+
+    class _UniqueId(ctypes.Structure):
+        _fields_ = [("internal", ctypes.c_char * 128)]
+
+    def __init__(self, device: torch.device, group: Optional[dist.ProcessGroup] = None):
+        self.group = group or dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        nccl = ctypes.CDLL("libnccl.so.2")
+        nccl.ncclGetUniqueId.argtypes = [ctypes.POINTER(self._UniqueId)]
+        nccl.ncclCommInitRank.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, self._UniqueId,
+                                          ctypes.c_int]
+        nccl.ncclCommDestroy.argtypes = [ctypes.c_void_p]
+        uid = self._UniqueId()
+        if self.rank == 0 and nccl.ncclGetUniqueId(ctypes.byref(uid)) != 0:
+            raise RuntimeError("ncclGetUniqueId failed")
+        box = [bytes(uid.internal) if self.rank == 0 else None]
+        dist.broadcast_object_list(box, src=dist.get_global_rank(self.group, 0), group=self.group)
+        ctypes.memmove(ctypes.addressof(uid), box[0], 128)
+        self.comm = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            rc = nccl.ncclCommInitRank(ctypes.byref(self.comm), self.world, uid, self.rank)
+        if rc != 0:
+            raise RuntimeError(f"ncclCommInitRank failed: {rc}")
+        self._nccl = nccl
+
+    def destroy(self) -> None:
+        if self.comm:
+            self._nccl.ncclCommDestroy(self.comm)
+            self.comm = ctypes.c_void_p()
+
+    def column_parallel(self, out: torch.Tensor, work: Optional[torch.Tensor], x: torch.Tensor, q: torch.Tensor,
+                        s: torch.Tensor) -> None:
+        """out [M, N] <- the full column-parallel output; q [N / P, K] is this rank's shard."""
+        M, N = out.shape
+        st = load_library().popcornDequantizeMatmulColumnParallel_i8f32(
+            self.comm, out.data_ptr(), None if work is None else work.data_ptr(), x.data_ptr(), q.data_ptr(),
+            s.data_ptr(), M, N, q.shape[1], torch.cuda.current_stream().cuda_stream)
+        if st != POPCORN_SUCCESS:
+            raise PopcornError(st, "popcornDequantizeMatmulColumnParallel_i8f32")
+
+    def row_parallel(self, out: torch.Tensor, x: torch.Tensor, q: torch.Tensor, s: torch.Tensor) -> None:
+        """out [M, N] <- sum over ranks of x_r @ (q_r * s).T; x [M, K_r], q [N, K_r]."""
+        M, N = out.shape
+        st = load_library().popcornDequantizeMatmulRowParallel_i8f32(
+            self.comm, out.data_ptr(), x.data_ptr(), q.data_ptr(), s.data_ptr(), M, N, q.shape[1],
+            torch.cuda.current_stream().cuda_stream)
+        if st != POPCORN_SUCCESS:
+            raise PopcornError(st, "popcornDequantizeMatmulRowParallel_i8f32")
+
+
 class FusedColumnParallelLinear:
     """Column-parallel decode layer whose all-gather is fused into the GEMV.
 
@@ -256,13 +313,15 @@ class LinearStack:
     """The linear layers of a decoder stack, tensor-parallel over `group`.
 
     Per layer: h -> qkv (column-parallel) -> o (row-parallel, all-reduce) ->
-    gate and up (column-parallel) -> down (row-parallel, all-reduce) -> h.
-    Attention and the SiLU(gate) * up product lie outside the dequant-matmul
-    path; in their place the o projection reads the first columns of the
-    rank's qkv output and the down projection reads the rank's gate output,
-    so every weight byte of every layer is streamed once per pass and every
-    collective of a Megatron-style stack happens, with nothing else between
-    the calls. Column-parallel outputs stay sharded (no all-gather).
+    silu(gate) * up (column-parallel, one fused call) -> down (row-parallel,
+    all-reduce) -> h. Attention lies outside the dequant-matmul path; in its
+    place the o projection reads the first columns of the rank's qkv output.
+    The gated MLP is the real one: gate and up share their row shards, so
+    popcornDequantizeMatmulSiluMul_i8f32 forms silu(g) * u on each rank's
+    channels and down reads that product. Every weight byte of every layer is
+    streamed once per pass and every collective of a Megatron-style stack
+    happens, with nothing else between the calls. Column-parallel outputs
+    stay sharded (no all-gather).
 
     Row-parallel sums use the fused popcornDequantizeMatmulAllReduce_i8f32
     when a PeerGroup is given and M <= 4, else the library call followed by an
@@ -295,7 +354,6 @@ class LinearStack:
         self.xo = torch.empty((M, self.k_o), dtype=f32, device=device)
         self.h1 = torch.empty((M, h), dtype=f32, device=device)
         self.g = torch.empty((M, n_ffn), dtype=f32, device=device)
-        self.u = torch.empty((M, n_ffn), dtype=f32, device=device)
         self.h2 = torch.empty((M, h), dtype=f32, device=device)
         self._lib = None if local_matmul is not None else load_library()
 
@@ -308,6 +366,20 @@ class LinearStack:
                                                      torch.cuda.current_stream().cuda_stream)
         if st != POPCORN_SUCCESS:
             raise PopcornError(st, "popcornDequantizeMatmul_i8f32")
+
+    def _glu(self, out: torch.Tensor, x: torch.Tensor, gate: tuple, up: tuple) -> None:
+        """out = silu(x @ W_gate^T) * (x @ W_up^T) on this rank's channels."""
+        (qg, sg), (qu, su) = gate, up
+        if self.local_matmul is not None:
+            g = self.local_matmul(x, qg, sg)
+            u = self.local_matmul(x, qu, su)
+            out.copy_(g / (1.0 + torch.exp(-g)) * u)  # popcorn's SiLU: g / (1 + exp(-g))
+            return
+        st = self._lib.popcornDequantizeMatmulSiluMul_i8f32(out.data_ptr(), x.data_ptr(), qg.data_ptr(), sg.data_ptr(),
+                                                            qu.data_ptr(), su.data_ptr(), out.shape[0], qg.shape[0],
+                                                            qg.shape[1], torch.cuda.current_stream().cuda_stream)
+        if st != POPCORN_SUCCESS:
+            raise PopcornError(st, "popcornDequantizeMatmulSiluMul_i8f32")
 
     def _row(self, out: torch.Tensor, x: torch.Tensor, q: torch.Tensor, s: torch.Tensor) -> None:
         if self.peer is not None:
@@ -330,8 +402,7 @@ class LinearStack:
                 self.xo.copy_(self.a[:, : self.k_o])
                 xo = self.xo
             self._row(self.h1, xo, *w["o"])
-            self._mm(self.g, self.h1, *w["gate"])
-            self._mm(self.u, self.h1, *w["up"])
+            self._glu(self.g, self.h1, w["gate"], w["up"])
             self._row(self.h2, self.g, *w["down"])
             h = self.h2
         return h
@@ -343,14 +414,19 @@ class LinearStack:
         return sum(q.numel() for w in self.layers for (q, _) in w.values())
 
     def launches_per_pass(self) -> int:
-        """Library kernel launches per pass (NCCL and copies not counted)."""
+        """Library kernel launches per pass (NCCL and copies not counted): one
+        per decode-size call; the fused gate/up call on tensor cores is the
+        shared activation prologue plus the two GEMMs."""
         if self._lib is None:
             return 0
         n = 0
         M = self.M
         for w in self.layers:
-            for part in STACK_PARTS:
+            for part in ("qkv", "o", "down"):
                 q = w[part][0]
                 n += self._lib.popcornDequantizeMatmulLaunchCount(0x10000, q.data_ptr(), M, q.shape[0],
                                                                   q.shape[1], 0)
+            q = w["gate"][0]
+            tensor = self._lib.popcornDequantizeMatmulSelectPath(0x10000, q.data_ptr(), M, q.shape[0], q.shape[1]) == 2
+            n += 3 if (M > 4 and tensor) else 1
         return n

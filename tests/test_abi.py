@@ -16,7 +16,8 @@ import pytest
 import popcorn_b200 as pc
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADERS = [os.path.join(ROOT, "include", h) for h in ("popcorn.h", "popcorn_b200.h", "popcorn_tp.h")]
+HEADERS = [os.path.join(ROOT, "include", h)
+           for h in ("popcorn.h", "popcorn_b200.h", "popcorn_tp.h", "popcorn_tp_nccl.h")]
 
 
 def declared_functions():
@@ -32,11 +33,41 @@ def test_header_declarations_are_the_python_symbol_list():
     assert declared_functions() == sorted(pc.ABI_SYMBOLS + pc.EXT_SYMBOLS)
 
 
+def _normalised(path):
+    text = re.sub(r"/\*.*?\*/", "", open(path).read(), flags=re.S)
+    text = re.sub(r"//[^\n]*", "", text)
+    return " ".join(text.split())
+
+
+def _prototype(norm, name):
+    m = re.search(r"(?:const\s+)?\w+\*? \*?" + name + r" ?\([^;]*\);", norm)
+    return None if m is None else re.sub(r"\s*([(),;*])\s*", r"\1", m.group(0))
+
+
+def test_popcorn_h_matches_the_reference_header():
+    # Read popcorn's own include/popcorn.h where its checkout is on this
+    # machine: every hot-path prototype and the status enum must be the same
+    # declaration, token for token.
+    import oracle
+
+    ref_dir = oracle.reference_checkout()
+    ref_h = os.path.join(ref_dir, "include", "popcorn.h") if ref_dir else None
+    if ref_h is None or not os.path.isfile(ref_h):
+        pytest.skip("reference checkout not on this machine")
+    ours, theirs = _normalised(HEADERS[0]), _normalised(ref_h)
+    for name in pc.ABI_SYMBOLS:
+        want = _prototype(theirs, name)
+        assert want is not None, name
+        assert _prototype(ours, name) == want, name
+    enum = re.compile(r"typedef enum \{[^}]*\} popcornStatus_t;")
+    assert enum.search(ours).group(0) == enum.search(theirs).group(0)
+
+
 def test_popcorn_h_keeps_the_reference_signatures():
     # The exact C prototypes popcorn declares for this path
-    # (include/popcorn.h:11-27, :464-473, :491-501, :527-534), whitespace-normalised.
-    text = re.sub(r"/\*.*?\*/", "", open(HEADERS[0]).read(), flags=re.S)
-    norm = " ".join(text.split())
+    # (include/popcorn.h:11-27, :464-473, :491-501, :527-534), whitespace-normalised;
+    # the test above checks them against the reference header itself.
+    norm = _normalised(HEADERS[0])
     for proto in [
         "POPCORN_SUCCESS = 0, POPCORN_ERROR_INVALID_VALUE = 1, POPCORN_ERROR_CUDA = 2, } popcornStatus_t;",
         "const char* popcornGetErrorString(popcornStatus_t status);",
@@ -77,12 +108,15 @@ def test_static_archive_exports_every_declared_symbol():
         assert name in defined, name
 
 
-def test_library_is_sm100a_only():
-    out = subprocess.run(["cuobjdump", "--list-elf", pc.LIB_PATH], capture_output=True, text=True)
-    if out.returncode != 0:
-        pytest.skip("cuobjdump unavailable")
-    archs = set(re.findall(r"sm_(\d+a?)", out.stdout))
-    assert archs == {"100a"}, archs
+def test_library_builds_for_sm100a_only():
+    # The library's Makefile compiles and links every object for one target,
+    # sm_100a, and nothing else (no other -gencode, no -arch shortcut).
+    text = open(os.path.join(ROOT, "popcorn_b200", "Makefile")).read()
+    assert re.findall(r"-gencode\s+(\S+)", text) == ["arch=compute_100a,code=sm_100a"]
+    assert "-arch" not in text
+    for rule in ("$(NVCC) $(NVCCFLAGS) -c", "$(NVCC) $(ARCH) -shared"):
+        assert rule in text, rule
+    assert "ARCH      := -gencode" in text and "$(ARCH)" in text.split("NVCCFLAGS :=")[1].split("\n")[0]
 
 
 def test_error_strings(lib):
@@ -106,6 +140,7 @@ def test_null_pointers_are_invalid_before_sizes(lib):
     for args in [(0, FAKE, FAKE), (FAKE, 0, FAKE), (FAKE, FAKE, 0)]:
         assert lib.popcornQuantize_f32i8(*args, 1, 4, None) == pc.POPCORN_ERROR_INVALID_VALUE
         assert lib.popcornDequantize_i8f32(*args, 1, 4, None) == pc.POPCORN_ERROR_INVALID_VALUE
+        assert lib.popcornDequantize_i8bf16(*args, 1, 4, None) == pc.POPCORN_ERROR_INVALID_VALUE
 
 
 @pytest.mark.parametrize("sizes", [(0, 1, 1), (1, 0, 1), (1, 1, 0), (-1, 5, 5), (5, -3, 5), (5, 5, -9)])
@@ -117,6 +152,7 @@ def test_nonpositive_sizes_are_noops(lib, sizes):
     if N <= 0 or K <= 0:
         assert lib.popcornQuantize_f32i8(FAKE, FAKE, FAKE, N, K, None) == pc.POPCORN_SUCCESS
         assert lib.popcornDequantize_i8f32(FAKE, FAKE, FAKE, N, K, None) == pc.POPCORN_SUCCESS
+        assert lib.popcornDequantize_i8bf16(FAKE, FAKE, FAKE, N, K, None) == pc.POPCORN_SUCCESS
     assert pc.launch_count(FAKE, FAKE, M, N, K) == 0
 
 
@@ -277,3 +313,21 @@ def test_path_selection_rules():
     assert pc.select_path(a16, a16 + 8, 2048, 4096, 4096) == pc.PATH_SIMT_F32
     assert pc.select_path(a16, a16, 2048, 4096, 4100) == pc.PATH_SIMT_F32
     assert pc.launch_count(a16, a16, 1, 4096, 4096) == 1
+
+
+def test_nccl_layer_argument_checks(lib):
+    # Checks that return before the communicator is used: null buffers (or a
+    # null communicator) -> invalid, sizes <= 0 -> no-op, and a column-parallel
+    # call with M > 1 needs its work buffer.
+    col = lib.popcornDequantizeMatmulColumnParallel_i8f32
+    row = lib.popcornDequantizeMatmulRowParallel_i8f32
+    for i in range(5):
+        args = [FAKE] * 5  # comm, out, x, qweight, scale
+        args[i] = 0
+        assert col(args[0], args[1], FAKE, *args[2:], 1, 8, 16, None) == pc.POPCORN_ERROR_INVALID_VALUE, i
+        assert row(*args, 1, 8, 16, None) == pc.POPCORN_ERROR_INVALID_VALUE, i
+    for (M, N, K) in [(0, 8, 16), (1, 0, 16), (1, 8, 0), (-1, 8, 16)]:
+        assert col(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, M, N, K, None) == pc.POPCORN_SUCCESS
+        assert row(FAKE, FAKE, FAKE, FAKE, FAKE, M, N, K, None) == pc.POPCORN_SUCCESS
+    assert col(FAKE, FAKE, 0, FAKE, FAKE, FAKE, 2, 8, 16, None) == pc.POPCORN_ERROR_INVALID_VALUE
+    assert lib.popcornGetLastNcclError() == 0

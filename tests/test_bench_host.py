@@ -67,11 +67,21 @@ def test_traffic_figures_name_existing_profiles():
 
 
 def test_compute_dtype_routes():
-    assert bench.compute_dtype("simt_f32", 1, 4096, False) == "f32"
+    # M = 1 per channel: fixed-point activations times int8 codes on dp2a.
+    assert bench.compute_dtype("simt_f32", 1, 4096, False) == "s30 fixed-point x s8 (dp2a) -> s32/f32"
+    assert bench.compute_dtype("simt_f32", 2, 4096, False) == "f32"
+    assert bench.compute_dtype("simt_f32", 1, 4096, True) == "f32"
     assert bench.compute_dtype("tensor_f16", 32, 4096, False).startswith("s8")
     assert bench.compute_dtype("tensor_f16", 128, 65536, False).startswith("s8")
     assert bench.compute_dtype("tensor_f16", 129, 4096, False) == "f16xf16->f32"
     assert bench.compute_dtype("tensor_f16", 32, 4096, True) == "f16xf16->f32"
+
+
+def test_quantize_and_dequantize_bytes():
+    # 5*N*K + 4*N for the quantizer; N*K + 4*N + 4*N*K (f32 out) for the dequantizer.
+    assert bench.weight_bytes(bench.WORKLOADS["quantize"]) == 5 * 4096 * 4096 + 4 * 4096
+    assert bench.weight_bytes(bench.WORKLOADS["dequantize"]) == 4096 * 4096 + 4 * 4096 + 4 * 4096 * 4096
+    assert bench.weight_bytes(dict(bench.WORKLOADS["dequantize"], out_bytes=2)) == 4096 * 4096 * 3 + 4 * 4096
 
 
 def test_measured_peaks_read_from_file():

@@ -286,6 +286,27 @@ def test_dequantize_bitexact(cuda, N, K):
     np.testing.assert_array_equal(got.view(np.uint32), oracle.dequantize(q, s).view(np.uint32))
 
 
+@pytest.mark.parametrize("N,K", [(1, 1), (3, 5), (64, 4096), (130, 4112), (7, 100), (4096, 4096)])
+def test_dequantize_bf16_bitexact(cuda, N, K):
+    # bf16 output: the f32 product rounded once to nearest even, bit for bit;
+    # scales spanning many binades (ties and bf16 subnormals included).
+    import torch
+
+    w = oracle.fill_normal(N * K, N + 2 * K, 0.02).reshape(N, K)
+    q, s = oracle.quantize(w)
+    s = (s * np.exp2(np.arange(N) % 200 - 100).astype(np.float32)).astype(np.float32)
+    s[0] = 0.0
+    out = Guarded(torch, cuda, N * K, torch.int16, -12345)
+    qd, sd = dev(q, torch, cuda), dev(s, torch, cuda)
+    assert pc.popcornDequantize_i8bf16(out.ptr(), qd.data_ptr(), sd.data_ptr(), N, K, None) == pc.POPCORN_SUCCESS
+    torch.cuda.synchronize()
+    got = out.check().reshape(N, K).view(np.uint16)
+    np.testing.assert_array_equal(got, oracle.dequantize_bf16(q, s))
+    y = pc.dequantize(qd, sd, dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(y.view(torch.int16).cpu().numpy().view(np.uint16), oracle.dequantize_bf16(q, s))
+
+
 def test_runs_on_caller_stream(cuda):
     import torch
 
@@ -455,7 +476,7 @@ def test_f32_path_fixed_point_edges(cuda):
     # Check both, and rows mixing them, against the oracle.
     import torch
 
-    N, K = 1024, 4096
+    N, K = 2048, 4096  # above the sequential kernel's 2^22 multiply-adds
     x, q, s = random_case(1, N, K, 31)
     ref = oracle.dequant_matmul(x, q, s, fused=True, threads=8)
     for scale in (1.0, 2.0 ** -80, 2.0 ** -95, 2.0 ** 95, 2.0 ** 105):
@@ -599,9 +620,14 @@ def test_tensor_path_back_to_back_calls_reuse_scratch(cuda):
 @pytest.mark.parametrize("M,N,K", [
     (1, 4096, 4096), (1, 1100, 4096), (1, 1000, 8192), (1, 777, 16384), (1, 1031, 11008),
     (1, 5000, 1024), (2, 4096, 4096), (2, 999, 8192), (3, 2000, 4096), (4, 4097, 4096), (4, 300, 4096),
+    # M = 1 shapes of the bulk-copy decode kernel: more rows than one CTA per
+    # SM can own (extra CTAs), fewer rows than SMs, every rows-per-stage and
+    # slices-per-thread variant, K with partial 4 KB slices.
+    (1, 40000, 1024), (1, 300, 16384), (1, 2100, 2048), (1, 9000, 512), (1, 4000, 1376), (1, 1000, 5504),
+    (1, 400, 12288), (1, 2000, 16384), (1, 3, 1 << 21),
 ])
 def test_bulk_gemv_variants(cuda, M, N, K):
-    # Every template variant of the bulk-staged decode GEMV (f32 path, M <= 4).
+    # Every template variant of the decode GEMVs (f32 path, M <= 4).
     import torch
 
     assert M * N * K > (1 << 22)

@@ -304,3 +304,21 @@ def test_int4_oracle_equals_reference_loops_random(shape):
         qr, sr, zr = oracle.quantize_grouped_i4(w, gs)
     np.testing.assert_array_equal(oracle.ref_dequant_matmul_grouped_i4(x, qr, sr, zr, gs),
                                   oracle.dequant_matmul_grouped_i4(x, qr, sr, zr, gs, threads=2))
+
+
+def test_bf16_dequantize_rounds_to_nearest_even():
+    # The oracle's bf16 expansion equals torch's own f32 -> bf16 conversion
+    # (round to nearest, ties to even) of the f32 product, including exact
+    # ties, values that round up into the next binade, subnormals and zeros.
+    import torch
+
+    N, K = 64, 256
+    q, s = oracle.quantize(oracle.fill_normal(N * K, 3, 0.02).reshape(N, K))
+    s = (s * np.exp2(np.arange(N) % 64 * 4 - 130).astype(np.float32)).astype(np.float32)
+    s[1] = 1.0 + 2.0 ** -8   # q * s lands on bf16 ties for many q
+    s[2] = 1.0 - 2.0 ** -9
+    s[3] = 0.0
+    got = oracle.dequantize_bf16(q, s)
+    f32 = oracle.dequantize(q, s)
+    want = torch.from_numpy(f32).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    np.testing.assert_array_equal(got, want)
