@@ -1,21 +1,31 @@
 // Status strings and the per-thread CUDA error record
 // (popcorn src/common.cuh:16-27, src/unary.cu:89-110).
+//
+// The record is popcorn's own: the C++17 inline thread_local variable
+// __popcorn_last_cuda_error of popcorn's src/common.cuh, declared here with
+// the same name and type. An inline variable is one object per program, so
+// when this library is linked together with popcorn's other operators
+// (unary.o, binary.o, ...) both write the same per-thread record, and
+// popcornGetLastCudaError reports the last failure of either library. The
+// three functions below are weak definitions for the same reason: popcorn's
+// unary.o defines them too, and its (identical) strong definitions win
+// without a duplicate-symbol error.
 #include "common.cuh"
+
+// One record per host thread, as in popcorn: a cgo caller has to query it from
+// the OS thread that made the failing call.
+inline thread_local cudaError_t __popcorn_last_cuda_error = cudaSuccess;
 
 namespace pcb {
 
 namespace {
-// One record per host thread, as in popcorn: a cgo caller has to query it from
-// the OS thread that made the failing call.
-thread_local cudaError_t t_last_cuda_error = cudaSuccess;
-
 constexpr int kMaxDevices = 64;
 int g_sm_count[kMaxDevices] = {0};
 }  // namespace
 
 popcornStatus_t record_cuda(cudaError_t err) {
     if (err != cudaSuccess) {
-        t_last_cuda_error = err;
+        ::__popcorn_last_cuda_error = err;
         return POPCORN_ERROR_CUDA;
     }
     return POPCORN_SUCCESS;
@@ -38,7 +48,7 @@ int device_sm_count() {
 
 }  // namespace pcb
 
-extern "C" const char* popcornGetErrorString(popcornStatus_t status) {
+extern "C" __attribute__((weak)) const char* popcornGetErrorString(popcornStatus_t status) {
     switch (status) {
         case POPCORN_SUCCESS:
             return "success";
@@ -51,8 +61,8 @@ extern "C" const char* popcornGetErrorString(popcornStatus_t status) {
     }
 }
 
-extern "C" cudaError_t popcornGetLastCudaError(void) { return pcb::t_last_cuda_error; }
+extern "C" __attribute__((weak)) cudaError_t popcornGetLastCudaError(void) { return ::__popcorn_last_cuda_error; }
 
-extern "C" const char* popcornGetLastCudaErrorString(void) {
-    return cudaGetErrorString(pcb::t_last_cuda_error);
+extern "C" __attribute__((weak)) const char* popcornGetLastCudaErrorString(void) {
+    return cudaGetErrorString(::__popcorn_last_cuda_error);
 }

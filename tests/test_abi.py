@@ -103,7 +103,7 @@ def test_static_archive_exports_every_declared_symbol():
     archive = os.path.join(ROOT, "lib", "libpopcorn.a")
     assert os.path.exists(archive), "lib/libpopcorn.a not built"
     out = subprocess.run(["nm", "-g", "--defined-only", archive], capture_output=True, text=True, check=True).stdout
-    defined = set(re.findall(r" T (\w+)$", out, flags=re.M))
+    defined = set(re.findall(r" [TW] (\w+)$", out, flags=re.M))
     for name in declared_functions():
         assert name in defined, name
 

@@ -26,7 +26,7 @@ def _build(tmp_path):
 def test_consumer_links_against_the_archive(tmp_path):
     binary = _build(tmp_path)
     syms = subprocess.run(["nm", str(binary)], capture_output=True, text=True, check=True).stdout
-    defined = set(re.findall(r" T (popcorn\w+)$", syms, flags=re.M))
+    defined = set(re.findall(r" [TW] (popcorn\w+)$", syms, flags=re.M))
     called = set(re.findall(r"\b(popcorn\w+)\(", open(os.path.join(ROOT, "tests", "consumer",
                                                                    "consumer_linear.c")).read()))
     assert called and called <= defined, called - defined

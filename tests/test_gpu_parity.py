@@ -634,5 +634,10 @@ def test_bulk_gemv_variants(cuda, M, N, K):
     x, q, s = random_case(M, N, K, 7 * M + N)
     got = abi_matmul(torch, cuda, x, q, s)
     assert pc.device_errors() == 0
-    ref = oracle.dequant_matmul(x, q, s, fused=True, threads=8)
+    if K > 65536:
+        # A sequential f32 sum over millions of terms carries its own rounding
+        # error well above 1e-5; compare such rows with a float64 product.
+        ref = x.astype(np.float64) @ (q.astype(np.float64) * s.astype(np.float64)[:, None]).T
+    else:
+        ref = oracle.dequant_matmul(x, q, s, fused=True, threads=8)
     assert oracle.normwise_rel_err(got, ref) <= TOL_F32
