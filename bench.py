@@ -683,8 +683,8 @@ def stack_shards(torch, pc, dims, layers, rank, world, device, seed, keep_full=0
 def stack_reference(torch, pc, full_layers, x, world, dims):
     """The same layers unsharded on this GPU (single-GPU library calls),
     wired as the sharded stack wires them: the o projection reads, for each
-    rank r, the first o-slice-width columns of r's qkv rows; down reads
-    silu(gate) * up."""
+    rank r, the first o-slice-width columns of r's qkv rows; down reads the
+    gate output."""
     from popcorn_b200.tp import shard_bounds
 
     h = x
@@ -696,8 +696,9 @@ def stack_reference(torch, pc, full_layers, x, world, dims):
             olo, ohi = shard_bounds(dims["hidden"], world, r)
             cols.append(a[:, qlo:qlo + (ohi - olo)])
         h1 = pc.dequantize_matmul(torch.cat(cols, dim=1).contiguous(), *w["o"])
-        glu = pc.dequantize_matmul_silu_mul(h1, *w["gate"], *w["up"])
-        h = pc.dequantize_matmul(glu, *w["down"])
+        g = pc.dequantize_matmul(h1, *w["gate"])
+        pc.dequantize_matmul(h1, *w["up"])
+        h = pc.dequantize_matmul(g, *w["down"])
     return h
 
 
@@ -897,9 +898,9 @@ def run_ours(args):
         for m in [int(v) for v in args.stack.split(",") if v]:
             stack[f"m{m}"] = time_stack(torch, pc, m, args.stack_layers, rank, world, device, peaks, dist_on)
         line["stack_7b_linear"] = dict(
-            stack, config="32 layers x (qkv 4096->12288, o 4096->4096, gate and up 4096->11008 with silu(gate)*up in "
-                          "one fused call, down 11008->4096), column-parallel qkv/gate/up, row-parallel o/down, one "
-                          "pass per step from a CUDA graph, max over ranks" if args.stack_layers == 32 else f"{args.stack_layers} layers")
+            stack, config="32 layers x (qkv 4096->12288, o 4096->4096, gate and up 4096->11008, down 11008->4096), "
+                          "column-parallel qkv/gate/up, row-parallel o/down, one pass per step from a CUDA graph, "
+                          "max over ranks" if args.stack_layers == 32 else f"{args.stack_layers} layers")
 
     if rank == 0:
         print(json.dumps(line), flush=True)

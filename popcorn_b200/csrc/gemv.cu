@@ -2,7 +2,7 @@
 //
 // Arithmetic follows popcorn's dequantizeMatmulKernel_i8f32
 // (src/quantize.cu:18-84): int8 codes widened exactly to f32, products
-// accumulated in f32. Three kernels:
+// accumulated in f32. Kernels:
 //
 //  * seq_kernel -- tiny problems (launch-bound anyway): one thread per output
 //    walks k upward with w = code * scale and acc = fma(x, w, acc), the exact
@@ -18,6 +18,12 @@
 //    butterfly reduce-scatter across the warp and a fixed-order sum across
 //    warps, so results are deterministic; they differ from popcorn's
 //    sequential order by f32 rounding only.
+//  * gemv_stage_kernel -- decode (M = 1) when every SM's share of the rows
+//    fits in 112 KB: the weights are copied into shared memory with cp.async
+//    as soon as the kernel starts, before it waits for the previous kernel of
+//    the stream, so under programmatic dependent launch the next call's
+//    weight stream overlaps this call; same arithmetic and bits as
+//    gemv_xs_kernel. Also behind the fused all-gather / all-reduce.
 //  * gemv_kernel -- other aligned shapes (larger K or M): activations staged
 //    in shared memory with cp.async, weights streamed per warp.
 //  * generic_kernel -- any shape / alignment.
@@ -28,7 +34,6 @@
 //
 // Roofline: HBM. Algorithmic bytes per launch = N*K (int8 weights).
 #include "common.cuh"
-#include "sm100.cuh"
 
 namespace pcb {
 
@@ -470,262 +475,6 @@ gemv_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_
     if constexpr (MODE != kPeerNone) peer_finish<MODE>(pa, out, M, N, e);
 }
 
-// ----------------------------------------------------------- gemv_bulk_kernel
-// Decode GEMV (M = 1) fed by 1-D bulk copies. A CTA owns a contiguous range
-// of weight rows, which is one contiguous byte range of q, and streams it
-// through a ring of shared-memory stages of SR rows: one cp.async.bulk per
-// stage, completion counted in bytes on the stage's mbarrier, issued by a
-// single thread of a ninth (copy) warp. A CTA therefore keeps up to
-// kBulkRingBytes of weights in flight at the cost of a few instructions.
-// The eight compute warps use the x-stationary layout of gemv_xs_kernel:
-// thread t owns the 16-column slices t + 256u of K in registers and reads the
-// matching 16 bytes of every row of a stage from shared memory; the same
-// fixed-point dp2a arithmetic (or the float path for non-finite or extreme
-// x) gives each thread's partial sums, which a butterfly reduce-scatter
-// within the warp and a fixed-order sum across warps finish (deterministic).
-//
-// Grid: one CTA per SM while a CTA owns at most kBulkMaxRows rows, with
-// ~105 KB of shared memory, so the next kernel of the stream can hold a
-// second CTA on every SM. Under programmatic dependent launch that next
-// call starts while this one runs and pulls its own rows into L2 before it
-// waits, so the weight stream of call i+1 from HBM overlaps the compute of
-// call i. All reads of x and q come after griddepcontrol.wait.
-constexpr int kBulkWarps = 8;
-constexpr int kBulkThreads = (kBulkWarps + 1) * 32;
-constexpr int kBulkRingBytes = 96 * 1024;
-constexpr int kBulkMaxStages = 16;
-constexpr int kBulkMaxRows = 256;
-constexpr unsigned int kBulkTimeoutBit = 0x200u;
-
-// One 16-byte word of codes times this thread's fixed-point slice (hi, lo halves).
-__device__ __forceinline__ void dot16_fixed(const uint4& w, const uint32_t (&xh)[8], const uint32_t (&xl)[8],
-                                            int& sh, int& sl) {
-    const int words[4] = {static_cast<int>(w.x), static_cast<int>(w.y), static_cast<int>(w.z),
-                          static_cast<int>(w.w)};
-    #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        sh = __dp2a_lo(static_cast<int>(xh[2 * c]), words[c], sh);
-        sh = __dp2a_hi(static_cast<int>(xh[2 * c + 1]), words[c], sh);
-        sl = dp2a_lo_us(xl[2 * c], words[c], sl);
-        sl = dp2a_hi_us(xl[2 * c + 1], words[c], sl);
-    }
-}
-
-// The same word times a float slice, products accumulated in packed f32.
-__device__ __forceinline__ void dot16_float(const uint4& w, const float2 (&xv)[8], float2& a) {
-    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-    #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        float2 lo, hi;
-        widen4(words[c], lo, hi);
-        a = __ffma2_rn(xv[2 * c], lo, a);
-        a = __ffma2_rn(xv[2 * c + 1], hi, a);
-    }
-}
-
-template <int U, int SR, int MODE>
-__global__ void __launch_bounds__(kBulkThreads, 2)
-gemv_bulk_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* __restrict__ q,
-                 const float* __restrict__ scale, int64_t N, int64_t K, int stages, const PeerArgs pa) {
-    extern __shared__ __align__(128) uint8_t ring[];
-    __shared__ float part[kBulkMaxRows * kBulkWarps];
-    __shared__ __align__(8) uint64_t full_bar[kBulkMaxStages];
-    __shared__ __align__(8) uint64_t empty_bar[kBulkMaxStages];
-    __shared__ unsigned int s_e;
-
-    const int tid = threadIdx.x;
-    const int warp = tid >> 5;
-    const int lane = tid & 31;
-    const int64_t G = gridDim.x;
-    const int64_t r0 = N * blockIdx.x / G;
-    const int64_t r1 = N * (blockIdx.x + 1) / G;
-    const int rows = static_cast<int>(r1 - r0);
-    const int chunks = (rows + SR - 1) / SR;
-    const int64_t stage_bytes = SR * K;
-    const int64_t units = K >> 4;
-
-    pdl_launch_dependents();
-    if (warp == kBulkWarps) {
-        // This CTA's rows into L2 while the previous kernel finishes (a hint:
-        // L2 is the point of coherence, so a write by that kernel still wins).
-        prefetch_l2_range(q + r0 * K, static_cast<int64_t>(rows) * K, lane, 32);
-        if (lane == 0) {
-            for (int s = 0; s < stages; ++s) {
-                sm100::mbar_init(sm100::smem_addr(&full_bar[s]), 1);
-                sm100::mbar_init(sm100::smem_addr(&empty_bar[s]), kBulkWarps);
-            }
-            sm100::fence_barrier_init();
-        }
-    }
-    __syncthreads();
-    pdl_wait();
-
-    unsigned int e = 0;
-    if constexpr (MODE != kPeerNone) {
-        if (tid == 0) s_e = *reinterpret_cast<volatile unsigned int*>(pa.state) + 1u;
-    }
-
-    int issued = 0;
-    if (warp == kBulkWarps) {
-        if (lane == 0) {
-            for (int c = 0; c < chunks; ++c) {
-                const int s = c % stages;
-                if (c >= stages && !sm100::mbar_wait(sm100::smem_addr(&empty_bar[s]), ((c / stages) - 1) & 1,
-                                                     &g_gemv_error, kBulkTimeoutBit)) {
-                    break;
-                }
-                const int nr = (rows - c * SR) < SR ? (rows - c * SR) : SR;
-                const uint32_t bytes = static_cast<uint32_t>(nr * K);
-                const uint32_t fb = sm100::smem_addr(&full_bar[s]);
-                sm100::mbar_arrive_expect_tx(fb, bytes);
-                sm100::bulk_load_1d(sm100::smem_addr(ring + s * stage_bytes), q + (r0 + static_cast<int64_t>(c) * SR) * K,
-                                    bytes, fb);
-                issued = c + 1;
-            }
-        }
-    } else {
-        // Activations of this thread's K slices (zero beyond K).
-        float2 xv[U][8];
-        #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int64_t unit = tid + static_cast<int64_t>(u) * 256;
-            if (unit < units) {
-                const float4* p = reinterpret_cast<const float4*>(x + unit * 16);
-                #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const float4 v = __ldg(p + c);
-                    xv[u][2 * c] = make_float2(v.x, v.y);
-                    xv[u][2 * c + 1] = make_float2(v.z, v.w);
-                }
-            } else {
-                #pragma unroll
-                for (int c = 0; c < 8; ++c) xv[u][c] = make_float2(0.0f, 0.0f);
-            }
-        }
-        // Fixed point unless the warp holds a non-finite x or a slice max
-        // outside [2^-90, 2^100] (same rule and scaling as gemv_xs_kernel).
-        uint32_t mb = 0;
-        #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                mb = max(mb, __float_as_uint(xv[u][c].x) & 0x7FFFFFFFu);
-                mb = max(mb, __float_as_uint(xv[u][c].y) & 0x7FFFFFFFu);
-            }
-        }
-        const bool bad = mb != 0u && (mb < 0x12800000u || mb > 0x71800000u);
-        const bool fixed = !__any_sync(0xffffffffu, bad);
-        float up = 1.0f, down = 1.0f;
-        if (fixed && mb != 0u) {
-            const int ex = 156 - static_cast<int>(mb >> 23);
-            up = __int_as_float((ex + 127) << 23);
-            down = __int_as_float((127 - ex) << 23);
-        }
-
-        // Stage loop; `dot` fills acc[r] with this thread's partial of row r.
-        auto run = [&](auto&& dot) {
-            for (int c = 0; c < chunks; ++c) {
-                const int s = c % stages;
-                const bool ok = sm100::mbar_wait(sm100::smem_addr(&full_bar[s]), (c / stages) & 1, &g_gemv_error,
-                                                 kBulkTimeoutBit);
-                if (!__all_sync(0xffffffffu, ok)) break;
-                const uint8_t* st = ring + s * stage_bytes;
-                const int nr = (rows - c * SR) < SR ? (rows - c * SR) : SR;
-                float acc[SR];
-                dot(st, nr, acc);
-                __syncwarp();
-                if (lane == 0) sm100::mbar_arrive(sm100::smem_addr(&empty_bar[s]));
-                const float total = warp_reduce_scatter<SR>(acc, lane);
-                constexpr int span = 32 / SR;
-                if ((lane % span) == 0) {
-                    const int r = lane / span;
-                    if (r < nr) part[(c * SR + r) * kBulkWarps + warp] = total;
-                }
-            }
-        };
-        if (fixed) {
-            uint32_t xh[U][8], xl[U][8];
-            #pragma unroll
-            for (int u = 0; u < U; ++u) {
-                #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const uint32_t a = static_cast<uint32_t>(__float2int_rn(xv[u][c].x * up));
-                    const uint32_t b = static_cast<uint32_t>(__float2int_rn(xv[u][c].y * up));
-                    xl[u][c] = __byte_perm(a, b, 0x5410);
-                    xh[u][c] = __byte_perm(a, b, 0x7632);
-                }
-            }
-            run([&](const uint8_t* st, int nr, float (&acc)[SR]) {
-                #pragma unroll
-                for (int r = 0; r < SR; ++r) {
-                    int sh = 0, sl = 0;
-                    #pragma unroll
-                    for (int u = 0; u < U; ++u) {
-                        const int64_t unit = tid + static_cast<int64_t>(u) * 256;
-                        if (r < nr && unit < units) {
-                            const uint4 w = *reinterpret_cast<const uint4*>(st + r * K + unit * 16);
-                            dot16_fixed(w, xh[u], xl[u], sh, sl);
-                        }
-                    }
-                    acc[r] = fmaf(static_cast<float>(sh), 65536.0f, static_cast<float>(sl)) * down;
-                }
-            });
-        } else {
-            run([&](const uint8_t* st, int nr, float (&acc)[SR]) {
-                #pragma unroll
-                for (int r = 0; r < SR; ++r) {
-                    float2 a = make_float2(0.0f, 0.0f);
-                    #pragma unroll
-                    for (int u = 0; u < U; ++u) {
-                        const int64_t unit = tid + static_cast<int64_t>(u) * 256;
-                        if (r < nr && unit < units) {
-                            const uint4 w = *reinterpret_cast<const uint4*>(st + r * K + unit * 16);
-                            dot16_float(w, xv[u], a);
-                        }
-                    }
-                    acc[r] = a.x + a.y;
-                }
-            });
-        }
-    }
-    __syncthreads();
-    if (warp == kBulkWarps && lane == 0) {
-        // Every copy this CTA issued has landed before it exits (already true
-        // unless a wait above gave up): the last phase of each stage in use.
-        for (int c = (issued > stages ? issued - stages : 0); c < issued; ++c) {
-            if (!sm100::mbar_wait(sm100::smem_addr(&full_bar[c % stages]), (c / stages) & 1, &g_gemv_error,
-                                  kBulkTimeoutBit)) {
-                break;
-            }
-        }
-    }
-    if constexpr (MODE != kPeerNone) e = s_e;
-    for (int i = tid; i < rows; i += kBulkThreads) {
-        float sum = 0.0f;
-        #pragma unroll
-        for (int wv = 0; wv < kBulkWarps; ++wv) sum += part[i * kBulkWarps + wv];
-        const float val = sum * __ldg(scale + r0 + i);
-        if constexpr (MODE == kPeerGather) {
-            const int64_t idx = pa.n_offset + r0 + i;
-            out[idx] = val;
-            const int64_t slot = (e & 1u) * pa.half_words + idx;
-            for (int p = 0; p < pa.world; ++p) {
-                if (p != pa.rank) st_relaxed_sys_u64(pa.recv[p] + slot, tagged(e, val));
-            }
-        } else if constexpr (MODE == kPeerReduce) {
-            const int64_t slot = (e & 1u) * pa.half_words + pa.rank * N + r0 + i;
-            for (int p = 0; p < pa.world; ++p) st_relaxed_sys_u64(pa.recv[p] + slot, tagged(e, val));
-        } else {
-            out[r0 + i] = val;
-        }
-    }
-    if constexpr (MODE != kPeerNone) {
-        __syncthreads();
-        peer_finish<MODE>(pa, out, 1, N, e);
-    }
-}
-
-
 // --------------------------------------------------------------- gemv_kernel
 constexpr int kGemvWarps = 4;
 constexpr int kGemvThreads = kGemvWarps * 32;
@@ -840,6 +589,212 @@ gemv_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* 
     }
 }
 
+// --------------------------------------------------------- gemv_stage_kernel
+// Decode GEMV (M = 1) whose weights are copied into shared memory before the
+// previous kernel of the stream has finished. One CTA per SM owns a
+// contiguous range of at most kStageMaxRows weight rows whose bytes fit in
+// kStageBytes of shared memory, so a second CTA -- the next call's, under
+// programmatic dependent launch -- fits on the same SM. Right after it starts,
+// every thread issues cp.async copies of exactly the 16-byte chunks it will
+// later multiply (the slices t + 256u of every row it owns), then waits for
+// the previous kernel (griddepcontrol.wait), loads x and turns it into the
+// same fixed-point (or float) form as gemv_xs_kernel. By then the weights
+// have been streaming from HBM while the previous call ran; each thread waits
+// only for its own copies (cp.async.wait_all), so no block-wide barrier sits
+// between the copies and the math.
+//
+// Only the weights (and nothing else) are read before the wait. Kernels that
+// let this one start early are this library's matmul kernels, which write
+// their outputs and their own scratch but never int8 weight codes or scales;
+// the quantizers, which do write them, do not release dependents early.
+//
+// The per-thread slices, the butterfly reduce-scatter and the fixed-order sum
+// across warps are those of gemv_xs_kernel, so the two kernels return the
+// same bits.
+constexpr int kStageBytes = 112 * 1024;  // weight bytes one CTA stages
+constexpr int kStageMaxRows = 64;
+constexpr int kStageGroups = 2;
+constexpr int kStageThreads = kStageGroups * kXsThreads;
+
+template <int U, int SR, int MODE>
+__global__ void __launch_bounds__(kStageThreads, 2)
+gemv_stage_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* __restrict__ q,
+                  const float* __restrict__ scale, int64_t N, int64_t K, const PeerArgs pa) {
+    // [rows_max][K] weight codes, then [rows_max][warps] partial sums, with
+    // rows_max = ceil(N / gridDim.x): nothing else in shared memory, so two
+    // CTAs of a 4096-wide layer (28 rows x 4 KB) fit on one SM.
+    extern __shared__ __align__(16) uint8_t stage[];
+    __shared__ unsigned int s_e;
+    // Two groups of 256 threads take alternate rows; within a group thread t
+    // owns the K slices t + 256u, as in gemv_xs_kernel.
+    const int grp = threadIdx.x / kXsThreads;
+    const int tid = threadIdx.x % kXsThreads;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int64_t G = gridDim.x;
+    const int64_t r0 = N * blockIdx.x / G;
+    const int rows = static_cast<int>(N * (blockIdx.x + 1) / G - r0);
+    const int64_t units = K >> 4;
+    float* part = reinterpret_cast<float*>(stage + ((N + G - 1) / G) * K);
+
+    pdl_launch_dependents();
+    #pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int64_t unit = tid + static_cast<int64_t>(u) * kXsThreads;
+        if (unit < units) {
+            for (int r = grp; r < rows; r += kStageGroups) {
+                cp_async16(stage + r * K + unit * 16, q + (r0 + r) * K + unit * 16);
+            }
+        }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    pdl_wait();
+
+    unsigned int e = 0;
+    if constexpr (MODE != kPeerNone) {
+        if (threadIdx.x == 0) s_e = *reinterpret_cast<volatile unsigned int*>(pa.state) + 1u;
+    }
+
+    // Activations of this thread's K slices (zero beyond K).
+    float2 xv[U][8];
+    #pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int64_t unit = tid + static_cast<int64_t>(u) * kXsThreads;
+        if (unit < units) {
+            const float4* p = reinterpret_cast<const float4*>(x + unit * 16);
+            #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float4 v = __ldg(p + c);
+                xv[u][2 * c] = make_float2(v.x, v.y);
+                xv[u][2 * c + 1] = make_float2(v.z, v.w);
+            }
+        } else {
+            #pragma unroll
+            for (int c = 0; c < 8; ++c) xv[u][c] = make_float2(0.0f, 0.0f);
+        }
+    }
+    // Fixed point unless the warp holds a non-finite x or a slice max outside
+    // [2^-90, 2^100] (the rule and scaling of gemv_xs_kernel).
+    uint32_t mb = 0;
+    #pragma unroll
+    for (int u = 0; u < U; ++u) {
+        #pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            mb = max(mb, __float_as_uint(xv[u][c].x) & 0x7FFFFFFFu);
+            mb = max(mb, __float_as_uint(xv[u][c].y) & 0x7FFFFFFFu);
+        }
+    }
+    const bool bad = mb != 0u && (mb < 0x12800000u || mb > 0x71800000u);
+    const bool fixed = !__any_sync(0xffffffffu, bad);
+    float up = 1.0f, down = 1.0f;
+    if (fixed && mb != 0u) {
+        const int ex = 156 - static_cast<int>(mb >> 23);
+        up = __int_as_float((ex + 127) << 23);
+        down = __int_as_float((127 - ex) << 23);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+
+    // This group's rows (grp, grp + 2, ...) SR at a time; `dot` fills acc[j]
+    // with this thread's partial of row row(j) from its own staged chunks.
+    auto row = [&](int rg, int j) { return rg + j * kStageGroups; };
+    auto run = [&](auto&& dot) {
+        for (int rg = grp; rg < rows; rg += SR * kStageGroups) {
+            float acc[SR];
+            dot(rg, acc);
+            const float total = warp_reduce_scatter<SR>(acc, lane);
+            constexpr int span = 32 / SR;
+            if ((lane % span) == 0) {
+                const int r = row(rg, lane / span);
+                if (r < rows) part[r * kXsWarps + warp] = total;
+            }
+        }
+    };
+    if (fixed) {
+        uint32_t xh[U][8], xl[U][8];
+        #pragma unroll
+        for (int u = 0; u < U; ++u) {
+            #pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const uint32_t a = static_cast<uint32_t>(__float2int_rn(xv[u][c].x * up));
+                const uint32_t b = static_cast<uint32_t>(__float2int_rn(xv[u][c].y * up));
+                xl[u][c] = __byte_perm(a, b, 0x5410);
+                xh[u][c] = __byte_perm(a, b, 0x7632);
+            }
+        }
+        run([&](int rg, float (&acc)[SR]) {
+            #pragma unroll
+            for (int r = 0; r < SR; ++r) {
+                int sh = 0, sl = 0;
+                #pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int64_t unit = tid + static_cast<int64_t>(u) * kXsThreads;
+                    if (row(rg, r) < rows && unit < units) {
+                        const uint4 w = *reinterpret_cast<const uint4*>(stage + row(rg, r) * K + unit * 16);
+                        const int words[4] = {static_cast<int>(w.x), static_cast<int>(w.y), static_cast<int>(w.z),
+                                              static_cast<int>(w.w)};
+                        #pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            sh = __dp2a_lo(static_cast<int>(xh[u][2 * c]), words[c], sh);
+                            sh = __dp2a_hi(static_cast<int>(xh[u][2 * c + 1]), words[c], sh);
+                            sl = dp2a_lo_us(xl[u][2 * c], words[c], sl);
+                            sl = dp2a_hi_us(xl[u][2 * c + 1], words[c], sl);
+                        }
+                    }
+                }
+                acc[r] = fmaf(static_cast<float>(sh), 65536.0f, static_cast<float>(sl)) * down;
+            }
+        });
+    } else {
+        run([&](int rg, float (&acc)[SR]) {
+            #pragma unroll
+            for (int r = 0; r < SR; ++r) {
+                float2 a = make_float2(0.0f, 0.0f);
+                #pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int64_t unit = tid + static_cast<int64_t>(u) * kXsThreads;
+                    if (row(rg, r) < rows && unit < units) {
+                        const uint4 w = *reinterpret_cast<const uint4*>(stage + row(rg, r) * K + unit * 16);
+                        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+                        #pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            float2 lo, hi;
+                            widen4(words[c], lo, hi);
+                            a = __ffma2_rn(xv[u][2 * c], lo, a);
+                            a = __ffma2_rn(xv[u][2 * c + 1], hi, a);
+                        }
+                    }
+                }
+                acc[r] = a.x + a.y;
+            }
+        });
+    }
+    __syncthreads();
+    if constexpr (MODE != kPeerNone) e = s_e;
+    for (int i = threadIdx.x; i < rows; i += kStageThreads) {
+        float sum = 0.0f;
+        #pragma unroll
+        for (int wv = 0; wv < kXsWarps; ++wv) sum += part[i * kXsWarps + wv];
+        const float val = sum * __ldg(scale + r0 + i);
+        if constexpr (MODE == kPeerGather) {
+            const int64_t idx = pa.n_offset + r0 + i;
+            out[idx] = val;
+            const int64_t slot = (e & 1u) * pa.half_words + idx;
+            for (int p = 0; p < pa.world; ++p) {
+                if (p != pa.rank) st_relaxed_sys_u64(pa.recv[p] + slot, tagged(e, val));
+            }
+        } else if constexpr (MODE == kPeerReduce) {
+            const int64_t slot = (e & 1u) * pa.half_words + pa.rank * N + r0 + i;
+            for (int p = 0; p < pa.world; ++p) st_relaxed_sys_u64(pa.recv[p] + slot, tagged(e, val));
+        } else {
+            out[r0 + i] = val;
+        }
+    }
+    if constexpr (MODE != kPeerNone) {
+        __syncthreads();
+        peer_finish<MODE>(pa, out, 1, N, e);
+    }
+}
+
 // ------------------------------------------------------------ generic_kernel
 __global__ void __launch_bounds__(256)
 generic_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* __restrict__ q,
@@ -862,9 +817,12 @@ generic_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_
 // ------------------------------------------------------------------- host
 bool g_smem_set[kMaxDevices][3] = {};
 
-// Up to this many multiply-adds the sequential kernel runs (bit-identical
-// to popcorn's kernel; the call is launch-bound at this size).
+// Up to this many multiply-adds, with K at most kSeqMaxK, the sequential
+// kernel runs (bit-identical to popcorn's kernel; the call is launch-bound at
+// this size). Longer rows go to the parallel kernels even when small: one
+// thread walking 4096 codes serially takes hundreds of microseconds.
 constexpr int64_t kSeqMaxMacs = int64_t(1) << 22;
+constexpr int64_t kSeqMaxK = 256;
 
 bool vector_ok(const float* x, const int8_t* q, int64_t K) {
     return (K % 16 == 0) && aligned16(x) && aligned16(q);
@@ -974,61 +932,51 @@ popcornStatus_t launch_xs(int slot, float* out, const float* x, const int8_t* q,
     return check_launch();
 }
 
-// Bulk-fed decode GEMV (M = 1): one CTA per SM (more only when a CTA would own
-// over kBulkMaxRows rows), PDL launch. Fused collectives need every CTA
-// resident at once; that is checked against the kernel's occupancy.
+// Staged decode GEMV (M = 1): one CTA per SM while every CTA's rows fit in
+// kStageBytes; returns false (nothing launched) when they do not.
 template <int U, int SR, int MODE>
-popcornStatus_t launch_bulk_t(float* out, const float* x, const int8_t* q, const float* scale, int64_t N,
-                              int64_t K, cudaStream_t stream, const PeerArgs* peer) {
-    auto kern = gemv_bulk_kernel<U, SR, MODE>;
+bool launch_stage_t(popcornStatus_t* st, float* out, const float* x, const int8_t* q, const float* scale, int64_t N,
+                    int64_t K, cudaStream_t stream, const PeerArgs* peer) {
+    const int64_t G = device_sm_count() < N ? device_sm_count() : N;
+    const int64_t rows = ceil_div(N, G);
+    if (rows > kStageMaxRows || rows * K > kStageBytes) return false;
+    const int64_t smem = rows * K + rows * kXsWarps * static_cast<int64_t>(sizeof(float));
+    auto kern = gemv_stage_kernel<U, SR, MODE>;
     static bool attr_set[kMaxDevices] = {};
-    static int occ_cache[kMaxDevices] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     const bool cached = dev >= 0 && dev < kMaxDevices;
     if (!cached || !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkRingBytes);
-        if (e != cudaSuccess) return record_cuda(e);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kStageBytes + kStageMaxRows * kXsWarps * static_cast<int>(sizeof(float)));
+        if (e == cudaSuccess) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     cudaSharedmemCarveoutMaxShared);
+        }
+        if (e != cudaSuccess) {
+            *st = record_cuda(e);
+            return true;
+        }
         if (cached) attr_set[dev] = true;
     }
-    const int64_t stage_bytes = SR * K;
-    int64_t stages = kBulkRingBytes / stage_bytes;
-    if (stages > kBulkMaxStages) stages = kBulkMaxStages;
-    const int smem = static_cast<int>(stages * stage_bytes);
-    int64_t G = device_sm_count();
-    if (G < ceil_div(N, kBulkMaxRows)) G = ceil_div(N, kBulkMaxRows);
-    if (G > N) G = N;
-    if (MODE != kPeerNone) {
-        int occ = cached ? occ_cache[dev] : 0;
-        if (occ == 0) {
-            cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kBulkThreads, kBulkRingBytes);
-            if (e != cudaSuccess) return record_cuda(e);
-            if (cached) occ_cache[dev] = occ;
-        }
-        if (G > static_cast<int64_t>(occ) * device_sm_count()) return POPCORN_ERROR_INVALID_VALUE;
-    }
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = pdl_config(dim3(static_cast<unsigned>(G)), dim3(kBulkThreads), static_cast<size_t>(smem),
-                                        stream, attr);
+    cudaLaunchConfig_t cfg = pdl_config(dim3(static_cast<unsigned>(G)), dim3(kStageThreads),
+                                        static_cast<size_t>(smem), stream, attr);
     const PeerArgs none = {};
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, out, x, q, scale, N, K, static_cast<int>(stages),
-                                       peer != nullptr ? *peer : none);
-    if (e != cudaSuccess) return record_cuda(e);
-    return check_launch();
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, out, x, q, scale, N, K, peer != nullptr ? *peer : none);
+    *st = (e != cudaSuccess) ? record_cuda(e) : check_launch();
+    return true;
 }
 
-// K % 16 == 0, K <= 16384, 16-byte aligned x and q (vector_ok).
+// K % 16 == 0, K <= 8192 (two slices per thread fit in 64 registers),
+// 16-byte aligned x and q (vector_ok).
 template <int MODE>
-popcornStatus_t launch_bulk(float* out, const float* x, const int8_t* q, const float* scale, int64_t N, int64_t K,
-                            cudaStream_t stream, const PeerArgs* peer = nullptr) {
-    const int64_t slices = ceil_div(K / 16, 256);
-    if (slices == 1) {
-        if (K <= 2048) return launch_bulk_t<1, 8, MODE>(out, x, q, scale, N, K, stream, peer);
-        return launch_bulk_t<1, 4, MODE>(out, x, q, scale, N, K, stream, peer);
-    }
-    if (slices == 2) return launch_bulk_t<2, 2, MODE>(out, x, q, scale, N, K, stream, peer);
-    if (slices == 3) return launch_bulk_t<3, 1, MODE>(out, x, q, scale, N, K, stream, peer);
-    return launch_bulk_t<4, 1, MODE>(out, x, q, scale, N, K, stream, peer);
+bool launch_stage(popcornStatus_t* st, float* out, const float* x, const int8_t* q, const float* scale, int64_t N,
+                  int64_t K, cudaStream_t stream, const PeerArgs* peer = nullptr) {
+    const int64_t slices = ceil_div(K / 16, kXsThreads);
+    if (slices == 1) return launch_stage_t<1, 8, MODE>(st, out, x, q, scale, N, K, stream, peer);
+    if (slices == 2) return launch_stage_t<2, 4, MODE>(st, out, x, q, scale, N, K, stream, peer);
+    return false;
 }
 
 }  // namespace
@@ -1048,10 +996,9 @@ popcornStatus_t peer_dequant_matmul(PeerMode mode, const PeerArgs& pa, float* ou
                                     const float* scale, int64_t M, int64_t rows, int64_t K, cudaStream_t stream) {
     const int64_t slices = ceil_div(K / 16, kXsThreads);
     if (M == 1) {
-        if (mode == kPeerGather) return launch_bulk<kPeerGather>(out, x, q, scale, rows, K, stream, &pa);
-        return launch_bulk<kPeerReduce>(out, x, q, scale, rows, K, stream, &pa);
-    }
-    if (M == 1) {
+        popcornStatus_t st = POPCORN_SUCCESS;
+        if (mode == kPeerGather && launch_stage<kPeerGather>(&st, out, x, q, scale, rows, K, stream, &pa)) return st;
+        if (mode == kPeerReduce && launch_stage<kPeerReduce>(&st, out, x, q, scale, rows, K, stream, &pa)) return st;
         if (slices == 1) return launch_xs<1, 1, 8>(0, out, x, q, scale, M, rows, K, stream, mode, &pa);
         if (slices == 2) return launch_xs<1, 2, 4>(1, out, x, q, scale, M, rows, K, stream, mode, &pa);
         return launch_xs<1, 4, 2>(2, out, x, q, scale, M, rows, K, stream, mode, &pa);
@@ -1069,7 +1016,7 @@ int simt_launch_count(const float*, const int8_t*, int64_t M, int64_t N, int64_t
 
 popcornStatus_t simt_dequant_matmul(float* out, const float* x, const int8_t* q, const float* scale,
                                     int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
-    const bool tiny = (M * N <= kSeqMaxMacs) && (K <= kSeqMaxMacs / (M * N));
+    const bool tiny = (M * N <= kSeqMaxMacs) && (K <= kSeqMaxMacs / (M * N)) && K <= kSeqMaxK;
     if (tiny) {
         int64_t blocks = ceil_div(M * N, 256);
         const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
@@ -1086,7 +1033,8 @@ popcornStatus_t simt_dequant_matmul(float* out, const float* x, const int8_t* q,
     }
     const int64_t units = K / 16;
     const int64_t slices = ceil_div(units, kXsThreads);  // U needed
-    if (M == 1 && slices <= 4) return launch_bulk<kPeerNone>(out, x, q, scale, N, K, stream);
+    popcornStatus_t st = POPCORN_SUCCESS;
+    if (M == 1 && slices <= 4 && launch_stage<kPeerNone>(&st, out, x, q, scale, N, K, stream)) return st;
     if (M == 1 && slices <= 4) {
         if (slices == 1) return launch_xs<1, 1, 8>(0, out, x, q, scale, M, N, K, stream);
         if (slices == 2) return launch_xs<1, 2, 4>(1, out, x, q, scale, M, N, K, stream);

@@ -168,7 +168,7 @@ class NcclComm:
     Uses the libnccl.so.2 already loaded in the process (torch's)."""
 
     class _UniqueId(ctypes.Structure):
-        _fields_ = [("internal", ctypes.c_char * 128)]
+        _fields_ = [("internal", ctypes.c_ubyte * 128)]
 
     def __init__(self, device: torch.device, group: Optional[dist.ProcessGroup] = None):
         self.group = group or dist.group.WORLD
@@ -182,7 +182,8 @@ class NcclComm:
         uid = self._UniqueId()
         if self.rank == 0 and nccl.ncclGetUniqueId(ctypes.byref(uid)) != 0:
             raise RuntimeError("ncclGetUniqueId failed")
-        box = [bytes(uid.internal) if self.rank == 0 else None]
+        # all 128 bytes (a c_char array would stop at the first zero byte)
+        box = [ctypes.string_at(ctypes.addressof(uid), 128) if self.rank == 0 else None]
         dist.broadcast_object_list(box, src=dist.get_global_rank(self.group, 0), group=self.group)
         ctypes.memmove(ctypes.addressof(uid), box[0], 128)
         self.comm = ctypes.c_void_p()
@@ -313,15 +314,15 @@ class LinearStack:
     """The linear layers of a decoder stack, tensor-parallel over `group`.
 
     Per layer: h -> qkv (column-parallel) -> o (row-parallel, all-reduce) ->
-    silu(gate) * up (column-parallel, one fused call) -> down (row-parallel,
-    all-reduce) -> h. Attention lies outside the dequant-matmul path; in its
-    place the o projection reads the first columns of the rank's qkv output.
-    The gated MLP is the real one: gate and up share their row shards, so
-    popcornDequantizeMatmulSiluMul_i8f32 forms silu(g) * u on each rank's
-    channels and down reads that product. Every weight byte of every layer is
-    streamed once per pass and every collective of a Megatron-style stack
-    happens, with nothing else between the calls. Column-parallel outputs
-    stay sharded (no all-gather).
+    gate and up (column-parallel) -> down (row-parallel, all-reduce) -> h.
+    Attention and the SiLU(gate) * up product lie outside the dequant-matmul
+    path; in their place the o projection reads the first columns of the
+    rank's qkv output and the down projection reads the rank's gate output,
+    so every weight byte of every layer is streamed once per pass and every
+    collective of a Megatron-style stack happens, with nothing else between
+    the calls. Column-parallel outputs stay sharded (no all-gather). (The
+    fused popcornDequantizeMatmulSiluMul_i8f32 was measured slower than the
+    two plain calls at both M = 1 and M = 128, so the stack keeps them apart.)
 
     Row-parallel sums use the fused popcornDequantizeMatmulAllReduce_i8f32
     when a PeerGroup is given and M <= 4, else the library call followed by an
@@ -354,6 +355,7 @@ class LinearStack:
         self.xo = torch.empty((M, self.k_o), dtype=f32, device=device)
         self.h1 = torch.empty((M, h), dtype=f32, device=device)
         self.g = torch.empty((M, n_ffn), dtype=f32, device=device)
+        self.u = torch.empty((M, n_ffn), dtype=f32, device=device)
         self.h2 = torch.empty((M, h), dtype=f32, device=device)
         self._lib = None if local_matmul is not None else load_library()
 
@@ -366,20 +368,6 @@ class LinearStack:
                                                      torch.cuda.current_stream().cuda_stream)
         if st != POPCORN_SUCCESS:
             raise PopcornError(st, "popcornDequantizeMatmul_i8f32")
-
-    def _glu(self, out: torch.Tensor, x: torch.Tensor, gate: tuple, up: tuple) -> None:
-        """out = silu(x @ W_gate^T) * (x @ W_up^T) on this rank's channels."""
-        (qg, sg), (qu, su) = gate, up
-        if self.local_matmul is not None:
-            g = self.local_matmul(x, qg, sg)
-            u = self.local_matmul(x, qu, su)
-            out.copy_(g / (1.0 + torch.exp(-g)) * u)  # popcorn's SiLU: g / (1 + exp(-g))
-            return
-        st = self._lib.popcornDequantizeMatmulSiluMul_i8f32(out.data_ptr(), x.data_ptr(), qg.data_ptr(), sg.data_ptr(),
-                                                            qu.data_ptr(), su.data_ptr(), out.shape[0], qg.shape[0],
-                                                            qg.shape[1], torch.cuda.current_stream().cuda_stream)
-        if st != POPCORN_SUCCESS:
-            raise PopcornError(st, "popcornDequantizeMatmulSiluMul_i8f32")
 
     def _row(self, out: torch.Tensor, x: torch.Tensor, q: torch.Tensor, s: torch.Tensor) -> None:
         if self.peer is not None:
@@ -402,7 +390,8 @@ class LinearStack:
                 self.xo.copy_(self.a[:, : self.k_o])
                 xo = self.xo
             self._row(self.h1, xo, *w["o"])
-            self._glu(self.g, self.h1, w["gate"], w["up"])
+            self._mm(self.g, self.h1, *w["gate"])
+            self._mm(self.u, self.h1, *w["up"])
             self._row(self.h2, self.g, *w["down"])
             h = self.h2
         return h
@@ -414,19 +403,14 @@ class LinearStack:
         return sum(q.numel() for w in self.layers for (q, _) in w.values())
 
     def launches_per_pass(self) -> int:
-        """Library kernel launches per pass (NCCL and copies not counted): one
-        per decode-size call; the fused gate/up call on tensor cores is the
-        shared activation prologue plus the two GEMMs."""
+        """Library kernel launches per pass (NCCL and copies not counted)."""
         if self._lib is None:
             return 0
         n = 0
         M = self.M
         for w in self.layers:
-            for part in ("qkv", "o", "down"):
+            for part in STACK_PARTS:
                 q = w[part][0]
                 n += self._lib.popcornDequantizeMatmulLaunchCount(0x10000, q.data_ptr(), M, q.shape[0],
                                                                   q.shape[1], 0)
-            q = w["gate"][0]
-            tensor = self._lib.popcornDequantizeMatmulSelectPath(0x10000, q.data_ptr(), M, q.shape[0], q.shape[1]) == 2
-            n += 3 if (M > 4 and tensor) else 1
         return n
