@@ -34,11 +34,12 @@
 //
 // Roofline: HBM. Algorithmic bytes per launch = N*K (int8 weights).
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace pcb {
 
 // Error bits of bounded waits in this file's kernels (read by
-// popcornB200DeviceErrors); none of the current kernels waits on a barrier.
+// popcornB200DeviceErrors): kPeerTimeoutBit, kStageTimeoutBit.
 __device__ unsigned int g_gemv_error = 0;
 
 namespace {
@@ -96,6 +97,7 @@ constexpr int kXsSlots = 8;  // decode kernel variants (launch_xs slot numbers)
 // one has not read yet.
 constexpr uint64_t kPeerWaitNs = 1000ull * 1000ull * 1000ull;  // 1 s
 constexpr unsigned int kPeerTimeoutBit = 0x100u;
+constexpr unsigned int kStageTimeoutBit = 0x200u;  // staged decode weights did not land within 1 s
 
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
@@ -595,13 +597,14 @@ gemv_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* 
 // contiguous range of at most kStageMaxRows weight rows whose bytes fit in
 // kStageBytes of shared memory, so a second CTA -- the next call's, under
 // programmatic dependent launch -- fits on the same SM. Right after it starts,
-// every thread issues cp.async copies of exactly the 16-byte chunks it will
-// later multiply (the slices t + 256u of every row it owns), then waits for
-// the previous kernel (griddepcontrol.wait), loads x and turns it into the
-// same fixed-point (or float) form as gemv_xs_kernel. By then the weights
-// have been streaming from HBM while the previous call ran; each thread waits
-// only for its own copies (cp.async.wait_all), so no block-wide barrier sits
-// between the copies and the math.
+// the CTA hands its rows to the TMA engine as one 1-D bulk copy per row
+// (cp.async.bulk, completing on one mbarrier) and asks for x to be pulled
+// into L2, then waits for the previous kernel (griddepcontrol.wait), loads x
+// and turns it into the same fixed-point (or float) form as gemv_xs_kernel.
+// By then the weights have been streaming from HBM while the previous call
+// ran. Bulk copies bypass the load/store units, so the next call's weight
+// stream does not queue in front of this call's reads of x (per-thread
+// 16-byte cp.async copies measured ~12 % slower per call on a B200).
 //
 // Only the weights (and nothing else) are read before the wait. Kernels that
 // let this one start early are this library's matmul kernels, which write
@@ -625,6 +628,7 @@ gemv_stage_kernel(float* __restrict__ out, const float* __restrict__ x, const in
     // CTAs of a 4096-wide layer (28 rows x 4 KB) fit on one SM.
     extern __shared__ __align__(16) uint8_t stage[];
     __shared__ unsigned int s_e;
+    __shared__ __align__(8) uint64_t s_full;  // completes when every staged row has landed
     // Two groups of 256 threads take alternate rows; within a group thread t
     // owns the K slices t + 256u, as in gemv_xs_kernel.
     const int grp = threadIdx.x / kXsThreads;
@@ -636,18 +640,23 @@ gemv_stage_kernel(float* __restrict__ out, const float* __restrict__ x, const in
     const int rows = static_cast<int>(N * (blockIdx.x + 1) / G - r0);
     const int64_t units = K >> 4;
     float* part = reinterpret_cast<float*>(stage + ((N + G - 1) / G) * K);
+    const uint32_t full = sm100::smem_addr(&s_full);
 
-    pdl_launch_dependents();
-    #pragma unroll
-    for (int u = 0; u < U; ++u) {
-        const int64_t unit = tid + static_cast<int64_t>(u) * kXsThreads;
-        if (unit < units) {
-            for (int r = grp; r < rows; r += kStageGroups) {
-                cp_async16(stage + r * K + unit * 16, q + (r0 + r) * K + unit * 16);
-            }
-        }
+    if (threadIdx.x == 0) {
+        sm100::mbar_init(full, 1);
+        sm100::fence_barrier_init();
+        // rows * K <= kStageBytes, far below the 2^20 - 1 limit of a transaction count.
+        sm100::mbar_arrive_expect_tx(full, static_cast<uint32_t>(rows * K));
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    pdl_launch_dependents();
+    __syncthreads();
+    if (threadIdx.x < rows) {
+        // One contiguous row of K bytes (K % 16 == 0, q 16-byte aligned).
+        sm100::bulk_load_1d(sm100::smem_addr(stage + threadIdx.x * K), q + (r0 + threadIdx.x) * K,
+                            static_cast<uint32_t>(K), full);
+    } else if (threadIdx.x == kStageThreads - 1) {
+        prefetch_l2_range(x, K * static_cast<int64_t>(sizeof(float)), 0, 1);
+    }
     pdl_wait();
 
     unsigned int e = 0;
@@ -692,7 +701,12 @@ gemv_stage_kernel(float* __restrict__ out, const float* __restrict__ x, const in
         up = __int_as_float((ex + 127) << 23);
         down = __int_as_float((127 - ex) << 23);
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
+    // Bounded wait for the staged rows. A timeout sets kStageTimeoutBit (the
+    // launch's results are then invalid) and waits once more, so the CTA does
+    // not leave while a copy may still be writing its shared memory.
+    if (!sm100::mbar_wait(full, 0, &g_gemv_error, kStageTimeoutBit)) {
+        sm100::mbar_wait(full, 0, &g_gemv_error, kStageTimeoutBit);
+    }
 
     // This group's rows (grp, grp + 2, ...) SR at a time; `dot` fills acc[j]
     // with this thread's partial of row row(j) from its own staged chunks.

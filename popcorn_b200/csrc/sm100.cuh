@@ -70,6 +70,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
 }
 
 // -------------------------------------------------------------------- TMA
+// 1-D bulk copy of `bytes` from global memory into this CTA's shared memory,
+// completing that many bytes of transaction count on `bar`. Both addresses
+// must be 16-byte aligned and `bytes` a multiple of 16. No multicast.
+__device__ __forceinline__ void bulk_load_1d(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
 // Pull one box of a 2D tensor map into L2 (a hint; no shared memory, no barrier).
 __device__ __forceinline__ void tma_prefetch_l2_2d(const void* map, int32_t c0, int32_t c1) {
     asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
