@@ -1015,6 +1015,7 @@ popcornStatus_t peer_dequant_matmul(PeerMode mode, const PeerArgs& pa, float* ou
         if (mode == kPeerReduce && launch_stage<kPeerReduce>(&st, out, x, q, scale, rows, K, stream, &pa)) return st;
         if (slices == 1) return launch_xs<1, 1, 8>(0, out, x, q, scale, M, rows, K, stream, mode, &pa);
         if (slices == 2) return launch_xs<1, 2, 4>(1, out, x, q, scale, M, rows, K, stream, mode, &pa);
+        if (slices == 3) return launch_xs<1, 3, 2>(6, out, x, q, scale, M, rows, K, stream, mode, &pa);
         return launch_xs<1, 4, 2>(2, out, x, q, scale, M, rows, K, stream, mode, &pa);
     }
     if (M == 2) {
@@ -1052,6 +1053,7 @@ popcornStatus_t simt_dequant_matmul(float* out, const float* x, const int8_t* q,
     if (M == 1 && slices <= 4) {
         if (slices == 1) return launch_xs<1, 1, 8>(0, out, x, q, scale, M, N, K, stream);
         if (slices == 2) return launch_xs<1, 2, 4>(1, out, x, q, scale, M, N, K, stream);
+        if (slices == 3) return launch_xs<1, 3, 2>(6, out, x, q, scale, M, N, K, stream);
         return launch_xs<1, 4, 2>(2, out, x, q, scale, M, N, K, stream);
     }
     if (M == 2 && slices <= 2) {

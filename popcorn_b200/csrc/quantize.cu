@@ -7,7 +7,10 @@
 // warp per row, so no temporary buffer, no cudaMalloc/cudaFree and no device
 // synchronisation is needed (popcorn allocates one, :547-562). The division
 // and rint are the IEEE round-to-nearest-even operations popcorn uses, so
-// codes and scales are bit-identical.
+// codes and scales are bit-identical. The division itself is replaced by a
+// multiply with the row's reciprocal except within 1e-4 of a rounding
+// boundary (quantize_one_rcp states the bound), which keeps the codes
+// identical while taking the division off the per-element path.
 //
 // For 1024 <= K <= 16384 (K % 16 == 0, aligned) one block handles a row and
 // holds it in registers between the max and the quantize step; otherwise one
@@ -34,6 +37,30 @@ __device__ __forceinline__ int8_t quantize_one(float v, float sc) {
     if (q > 127.0f) q = 127.0f;
     if (q < -128.0f) q = -128.0f;
     return static_cast<int8_t>(q);
+}
+
+// The same code as quantize_one(v, sc), with the division replaced by a
+// multiply wherever that cannot change the result. rcp = 1 / sc rounded to
+// nearest (a normal number: the caller checks that sc is normal and finite).
+// With Q = v / sc exactly and |Q| <= 127 (sc = max / 127 >= |v| / 127
+// within 2^-24), t = v * rcp lies within |Q| (2^-24 + 2^-24 + 2^-48) and
+// popcorn's rounded quotient fl(Q) within |Q| 2^-24 of Q, so |t - fl(Q)| <
+// 127 * 1.8e-7 < 2.3e-5. When t is more than 1e-4 away from every
+// half-integer, rint(t) = rint(fl(Q)); otherwise (and for NaN t, where the
+// compare is false) the exact division decides, ties to even included.
+__device__ __forceinline__ int8_t quantize_one_rcp(float v, float sc, float rcp) {
+    const float t = v * rcp;
+    float q = rintf(t);
+    if (!(fabsf(t - q) <= 0.4999f)) q = rintf(v / sc);
+    if (q > 127.0f) q = 127.0f;
+    if (q < -128.0f) q = -128.0f;
+    return static_cast<int8_t>(q);
+}
+
+// Rows whose scale is not a finite normal number (a zero, denormal or
+// infinite row maximum) keep the division for every element.
+__device__ __forceinline__ bool rcp_ok(float sc) {
+    return sc >= 1.17549435e-38f && sc <= 3.40282347e38f;
 }
 
 // kVec: K % 16 == 0 and both row bases 16-byte aligned; each lane then owns
@@ -75,6 +102,9 @@ quantize_rows_kernel(int8_t* __restrict__ out, float* __restrict__ scale,
         if (sc == 0.0f) sc = 1.0f;
         if (lane == 0) scale[row] = sc;
 
+        const bool fast = rcp_ok(sc);
+        const float rcp = fast ? __frcp_rn(sc) : 0.0f;
+        auto code = [&](float v) { return fast ? quantize_one_rcp(v, sc, rcp) : quantize_one(v, sc); };
         if (kVec) {
             const float4* r4 = reinterpret_cast<const float4*>(r);
             uint4* o16 = reinterpret_cast<uint4*>(o);
@@ -84,16 +114,16 @@ quantize_rows_kernel(int8_t* __restrict__ out, float* __restrict__ scale,
                 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     float4 v = __ldg(r4 + c * 4 + j);
-                    uint32_t b0 = static_cast<uint8_t>(quantize_one(v.x, sc));
-                    uint32_t b1 = static_cast<uint8_t>(quantize_one(v.y, sc));
-                    uint32_t b2 = static_cast<uint8_t>(quantize_one(v.z, sc));
-                    uint32_t b3 = static_cast<uint8_t>(quantize_one(v.w, sc));
+                    uint32_t b0 = static_cast<uint8_t>(code(v.x));
+                    uint32_t b1 = static_cast<uint8_t>(code(v.y));
+                    uint32_t b2 = static_cast<uint8_t>(code(v.z));
+                    uint32_t b3 = static_cast<uint8_t>(code(v.w));
                     w[j] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
                 }
                 o16[c] = make_uint4(w[0], w[1], w[2], w[3]);
             }
         } else {
-            for (int64_t k = lane; k < K; k += 32) o[k] = quantize_one(__ldg(r + k), sc);
+            for (int64_t k = lane; k < K; k += 32) o[k] = code(__ldg(r + k));
         }
     }
 }
@@ -153,6 +183,8 @@ quantize_row_block_kernel(int8_t* __restrict__ out, float* __restrict__ scale, c
         if (tid == 0) scale[row] = sc;
 
         uint4* o16 = reinterpret_cast<uint4*>(out + row * K);
+        const bool fast = rcp_ok(sc);
+        const float rcp = fast ? __frcp_rn(sc) : 0.0f;
         #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int64_t unit = tid + static_cast<int64_t>(u) * kRowThreads;
@@ -160,10 +192,18 @@ quantize_row_block_kernel(int8_t* __restrict__ out, float* __restrict__ scale, c
                 uint32_t w[4];
                 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    const uint32_t b0 = static_cast<uint8_t>(quantize_one(v[u][c].x, sc));
-                    const uint32_t b1 = static_cast<uint8_t>(quantize_one(v[u][c].y, sc));
-                    const uint32_t b2 = static_cast<uint8_t>(quantize_one(v[u][c].z, sc));
-                    const uint32_t b3 = static_cast<uint8_t>(quantize_one(v[u][c].w, sc));
+                    uint32_t b0, b1, b2, b3;
+                    if (fast) {
+                        b0 = static_cast<uint8_t>(quantize_one_rcp(v[u][c].x, sc, rcp));
+                        b1 = static_cast<uint8_t>(quantize_one_rcp(v[u][c].y, sc, rcp));
+                        b2 = static_cast<uint8_t>(quantize_one_rcp(v[u][c].z, sc, rcp));
+                        b3 = static_cast<uint8_t>(quantize_one_rcp(v[u][c].w, sc, rcp));
+                    } else {
+                        b0 = static_cast<uint8_t>(quantize_one(v[u][c].x, sc));
+                        b1 = static_cast<uint8_t>(quantize_one(v[u][c].y, sc));
+                        b2 = static_cast<uint8_t>(quantize_one(v[u][c].z, sc));
+                        b3 = static_cast<uint8_t>(quantize_one(v[u][c].w, sc));
+                    }
                     w[c] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
                 }
                 o16[unit] = make_uint4(w[0], w[1], w[2], w[3]);

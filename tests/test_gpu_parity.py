@@ -200,6 +200,51 @@ def test_quantize_bitexact_vs_popcorn_kernel(cuda, K):
     np.testing.assert_array_equal(s1.cpu().numpy().view(np.uint32), so.view(np.uint32))
 
 
+def near_tie_rows(K, rows=8):
+    """Rows whose values sit on and within a few ulps of every half-integer
+    multiple of the row's scale (the boundaries where rint(v / scale) changes),
+    with the row maximum pinned so that scale = max / 127 is known."""
+    out = []
+    for r in range(rows):
+        mx = np.float32(0.37 * (r + 1))
+        sc = np.float32(mx / np.float32(127.0))
+        vals = []
+        for j in range(-128, 127):
+            v = np.float32(np.float32(j + 0.5) * sc)
+            for d in range(-3, 4):
+                vals.append(v)
+                v = np.nextafter(v, np.float32(np.inf) if d >= 0 else np.float32(-np.inf))
+        row = np.resize(np.array(vals, np.float32), K)
+        row = np.clip(row, -mx, mx)
+        row[0] = mx
+        out.append(row.astype(np.float32))
+    return np.stack(out)
+
+
+@needs_ref_gpu
+@pytest.mark.parametrize("K", [1000, 4096, 8192, 12288, 20000])
+def test_quantize_near_ties_bitexact(cuda, K):
+    # The quantizer multiplies by the reciprocal scale and falls back to the
+    # division near rounding boundaries; codes must still equal popcorn's
+    # rint(v / scale) bit for bit (row-block kernels for K <= 16384, the
+    # per-warp kernel beyond and for K % 16 != 0).
+    import torch
+
+    w = near_tie_rows(K)
+    N = w.shape[0]
+    wd = dev(w, torch, cuda)
+    q1, s1 = pc.quantize(wd)
+    q2 = torch.empty_like(q1)
+    s2 = torch.empty_like(s1)
+    ref = oracle.popcorn_ref_gpu()
+    assert ref.popcornQuantize_f32i8(q2.data_ptr(), s2.data_ptr(), wd.data_ptr(), N, K, None) == 0
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(q1.cpu().numpy(), q2.cpu().numpy())
+    np.testing.assert_array_equal(s1.cpu().numpy().view(np.uint32), s2.cpu().numpy().view(np.uint32))
+    qo, so = oracle.quantize(w)
+    np.testing.assert_array_equal(q1.cpu().numpy(), qo)
+
+
 @needs_ref_gpu
 @pytest.mark.parametrize("shape", [(1, 64, 64), (3, 40, 96), (16, 256, 1024), (33, 100, 512)])
 def test_oracle_pinned_to_popcorn_matmul_kernel(cuda, shape):
