@@ -212,80 +212,116 @@ quantize_row_block_kernel(int8_t* __restrict__ out, float* __restrict__ scale, c
     }
 }
 
-// out[n, k] = float(q[n, k]) * scale[n]; kVec: K % 16 == 0 and aligned bases,
-// each thread expands 16 codes (one 16-byte load, four 16-byte stores).
+// out[n, k] = float(q[n, k]) * scale[n]. kVec (K % 16 == 0, aligned bases):
+// a block walks rows, its warps take 512-code chunks of the row; lane l
+// reads code words l, 32 + l, 64 + l, 96 + l of the chunk (four 128-byte
+// loads per warp) and store j writes outputs [128 j, 128 j + 128) of the
+// chunk, so every warp store covers 512 contiguous bytes.
+constexpr int kDeqThreads = 256;
+constexpr int kDeqWarps = kDeqThreads / 32;
+
+__device__ __forceinline__ float4 expand4(uint32_t w, float sc) {
+    float4 v;
+    v.x = static_cast<float>(static_cast<int8_t>(w & 0xffu)) * sc;
+    v.y = static_cast<float>(static_cast<int8_t>((w >> 8) & 0xffu)) * sc;
+    v.z = static_cast<float>(static_cast<int8_t>((w >> 16) & 0xffu)) * sc;
+    v.w = static_cast<float>(static_cast<int8_t>(w >> 24)) * sc;
+    return v;
+}
+
 template <bool kVec>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kDeqThreads)
 dequantize_kernel(float* __restrict__ out, const int8_t* __restrict__ q,
                   const float* __restrict__ scale, int64_t N, int64_t K) {
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (kVec) {
-        const int64_t per_row = K >> 4;
-        const int64_t total = N * per_row;
-        for (; t < total; t += stride) {
-            const int64_t row = t / per_row;
+        const int lane = threadIdx.x & 31;
+        const int warp = threadIdx.x >> 5;
+        const int64_t words = K >> 2;  // code words per row
+        const int64_t chunks = (K + 511) >> 9;
+        for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
             const float sc = __ldg(scale + row);
-            const uint4 packed = __ldg(reinterpret_cast<const uint4*>(q) + t);
-            const uint32_t w[4] = {packed.x, packed.y, packed.z, packed.w};
-            float4* o = reinterpret_cast<float4*>(out) + t * 4;
-            #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                float4 v;
-                v.x = static_cast<float>(static_cast<int8_t>(w[j] & 0xffu)) * sc;
-                v.y = static_cast<float>(static_cast<int8_t>((w[j] >> 8) & 0xffu)) * sc;
-                v.z = static_cast<float>(static_cast<int8_t>((w[j] >> 16) & 0xffu)) * sc;
-                v.w = static_cast<float>(static_cast<int8_t>(w[j] >> 24)) * sc;
-                o[j] = v;
+            const uint32_t* qr = reinterpret_cast<const uint32_t*>(q + row * K);
+            float4* orow = reinterpret_cast<float4*>(out + row * K);
+            for (int64_t c = warp; c < chunks; c += kDeqWarps) {
+                uint32_t w[4];
+                #pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int64_t i = c * 128 + j * 32 + lane;
+                    w[j] = i < words ? __ldg(qr + i) : 0u;
+                }
+                #pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int64_t i = c * 128 + j * 32 + lane;
+                    if (i < words) orow[i] = expand4(w[j], sc);
+                }
             }
         }
     } else {
+        const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
         const int64_t total = N * K;
-        for (; t < total; t += stride) {
+        for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < total; t += stride) {
             out[t] = static_cast<float>(q[t]) * __ldg(scale + t / K);
         }
     }
 }
 
 // The bf16 form: the same f32 product, rounded once to bf16 (nearest even,
-// cvt.rn.bf16x2.f32); each thread expands 16 codes into two 16-byte stores.
+// cvt.rn.bf16x2.f32). kVec: lane l reads code-word pairs l and 32 + l of a
+// 512-code chunk (two 256-byte loads per warp) and store j writes bf16
+// outputs [256 j, 256 j + 256) of the chunk (512 contiguous bytes).
 template <bool kVec>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kDeqThreads)
 dequantize_bf16_kernel(uint16_t* __restrict__ out, const int8_t* __restrict__ q,
                        const float* __restrict__ scale, int64_t N, int64_t K) {
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (kVec) {
-        const int64_t per_row = K >> 4;
-        const int64_t total = N * per_row;
-        for (; t < total; t += stride) {
-            const int64_t row = t / per_row;
+        const int lane = threadIdx.x & 31;
+        const int warp = threadIdx.x >> 5;
+        const int64_t pairs = K >> 3;  // 8-code pairs of words per row
+        const int64_t chunks = (K + 511) >> 9;
+        for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
             const float sc = __ldg(scale + row);
-            const uint4 packed = __ldg(reinterpret_cast<const uint4*>(q) + t);
-            const uint32_t w[4] = {packed.x, packed.y, packed.z, packed.w};
-            uint32_t o[8];
-            #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float a = static_cast<float>(static_cast<int8_t>(w[j] & 0xffu)) * sc;
-                const float b = static_cast<float>(static_cast<int8_t>((w[j] >> 8) & 0xffu)) * sc;
-                const float c = static_cast<float>(static_cast<int8_t>((w[j] >> 16) & 0xffu)) * sc;
-                const float d = static_cast<float>(static_cast<int8_t>(w[j] >> 24)) * sc;
-                const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b);  // a in the low half
-                const __nv_bfloat162 hi = __floats2bfloat162_rn(c, d);
-                o[2 * j] = *reinterpret_cast<const uint32_t*>(&lo);
-                o[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&hi);
+            const uint2* qr = reinterpret_cast<const uint2*>(q + row * K);
+            uint4* orow = reinterpret_cast<uint4*>(out + row * K);
+            for (int64_t c = warp; c < chunks; c += kDeqWarps) {
+                uint2 w[2];
+                #pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const int64_t i = c * 64 + j * 32 + lane;
+                    w[j] = i < pairs ? __ldg(qr + i) : make_uint2(0u, 0u);
+                }
+                #pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const int64_t i = c * 64 + j * 32 + lane;
+                    if (i < pairs) {
+                        const float4 a = expand4(w[j].x, sc);
+                        const float4 b = expand4(w[j].y, sc);
+                        const __nv_bfloat162 p0 = __floats2bfloat162_rn(a.x, a.y);  // first code in the low half
+                        const __nv_bfloat162 p1 = __floats2bfloat162_rn(a.z, a.w);
+                        const __nv_bfloat162 p2 = __floats2bfloat162_rn(b.x, b.y);
+                        const __nv_bfloat162 p3 = __floats2bfloat162_rn(b.z, b.w);
+                        orow[i] = make_uint4(*reinterpret_cast<const uint32_t*>(&p0),
+                                             *reinterpret_cast<const uint32_t*>(&p1),
+                                             *reinterpret_cast<const uint32_t*>(&p2),
+                                             *reinterpret_cast<const uint32_t*>(&p3));
+                    }
+                }
             }
-            uint4* dst = reinterpret_cast<uint4*>(out) + t * 2;
-            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
         }
     } else {
+        const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
         const int64_t total = N * K;
-        for (; t < total; t += stride) {
+        for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < total; t += stride) {
             const __nv_bfloat16 v = __float2bfloat16_rn(static_cast<float>(q[t]) * __ldg(scale + t / K));
             out[t] = *reinterpret_cast<const uint16_t*>(&v);
         }
     }
+}
+
+// Blocks for the row-walking expand kernels: one row per block up to eight
+// resident blocks per SM.
+int deq_rows_grid(int64_t N) {
+    const int64_t cap = static_cast<int64_t>(device_sm_count()) * 8;
+    return static_cast<int>(N < cap ? N : cap);
 }
 
 int grid_for(int64_t work_items, int threads) {
@@ -340,7 +376,7 @@ extern "C" popcornStatus_t popcornDequantize_i8f32(float* out, const int8_t* qwe
 
     const bool vec = (K % 16 == 0) && aligned16(qweight) && aligned16(out);
     if (vec) {
-        dequantize_kernel<true><<<grid_for(N * (K / 16), 256), 256, 0, stream>>>(out, qweight, scale, N, K);
+        dequantize_kernel<true><<<deq_rows_grid(N), kDeqThreads, 0, stream>>>(out, qweight, scale, N, K);
     } else {
         dequantize_kernel<false><<<grid_for(N * K, 256), 256, 0, stream>>>(out, qweight, scale, N, K);
     }
@@ -355,7 +391,7 @@ extern "C" popcornStatus_t popcornDequantize_i8bf16(uint16_t* out, const int8_t*
 
     const bool vec = (K % 16 == 0) && aligned16(qweight) && aligned16(out);
     if (vec) {
-        dequantize_bf16_kernel<true><<<grid_for(N * (K / 16), 256), 256, 0, stream>>>(out, qweight, scale, N, K);
+        dequantize_bf16_kernel<true><<<deq_rows_grid(N), kDeqThreads, 0, stream>>>(out, qweight, scale, N, K);
     } else {
         dequantize_bf16_kernel<false><<<grid_for(N * K, 256), 256, 0, stream>>>(out, qweight, scale, N, K);
     }

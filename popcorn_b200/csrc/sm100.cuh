@@ -308,6 +308,19 @@ __device__ __forceinline__ void mma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem
         : "memory");
 }
 
+// D (+)= A * B^T over the CTA pair, kind::i8 (signed 8-bit A and B, s32
+// accumulate): A rows split across the two CTAs' shared memory (same
+// offset in each), B rows likewise, D rows follow A. K = 32 per instruction.
+__device__ __forceinline__ void mma_i8_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive once on the mbarrier at offset `bar` of every CTA in `cta_mask` when
 // the pair's tcgen05 ops issued so far by this thread are complete.
 __device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint16_t cta_mask) {

@@ -1988,6 +1988,214 @@ tc_i8_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__
     }
 }
 
+// ------------------------------- int8 tensor path on CTA pairs (32 < M <= 128)
+// The same arithmetic as tc_i8_kernel with tcgen05.mma.cta_group::2: a pair
+// of CTAs (cluster of two) computes 256 weight rows. CTA r holds its own 128
+// weight rows (the A operand is split by rows across the pair) and only
+// digit plane r of the activation tile -- rank 0 the hi digits, rank 1 the
+// lo digits -- as its half of the B operand, so the pair's N = 2 BM columns
+// are hi then lo, exactly the single-CTA layout, and each CTA's tensor
+// memory receives its 128 weight rows x 2 BM columns. Per 128-deep k-block
+// a CTA loads 16 KB of weights and BM x 128 digit bytes instead of 2 BM x
+// 128: at BM = 128 that is 32 KB instead of 48 KB per SM, the stream that
+// bounds the single-CTA kernel when M = 128 (the MMAs of a k-block need
+// ~540 cycles; 48 KB at the ~70 bytes per cycle an SM receives takes ~700).
+// Used for 128-row activation tiles when the 128-row weight tiles already
+// fill half the GPU (no split-K); instantiated for BM = 128 only.
+//
+// All four TMA loads of a stage (weights and digits of both CTAs) complete
+// on the leader's full[s]; the leader alone posts the expected bytes and
+// issues the MMAs; release[s], acc_full and drain are multicast commits to
+// both CTAs. The first ring of weight tiles is requested before the
+// dependent-launch wait (the prologue writes only the digit planes and row
+// factors); the digit tiles and the epilogue's row factors come after it.
+template <int BM>
+struct CfgI8Pair {
+    static constexpr int kBK = 128;
+    static constexpr int kN = 2 * BM;                // pair MMA N: hi rows (rank 0), then lo rows (rank 1)
+    static constexpr int kXBytes = BM * kBK;         // this CTA's digit plane tile per stage
+    static constexpr int kWBytes = kTileN * kBK;     // this CTA's weight tile per stage
+    static constexpr int kStages = 6;
+    static constexpr int kAcc = 1;                   // one accumulator: each k-step is 128 x 256 x 32 per CTA
+    static constexpr int kTmemCols = kAcc * kN;      // 256
+    static constexpr int kNumBars = 2 * kStages + 2;
+    static constexpr int kStageBytes = 4 * 32 * 32 * 4;
+    static constexpr int kSmem = 1024 + kStages * (kXBytes + kWBytes) + kNumBars * 8 + 16 + 16 + kStageBytes + 2 * BM * 4;
+    static_assert(kXBytes % 1024 == 0 && kWBytes % 1024 == 0, "stages stay 1024-byte aligned");
+    static_assert(BM == 128 && kTmemCols == 256, "tensor-memory allocation");
+    static_assert(kSmem <= 227 * 1024, "shared memory per block");
+};
+
+template <int BM>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kI8Threads, 1)
+tc_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                  float* __restrict__ out, const float* __restrict__ scale, const float* __restrict__ rowfactor,
+                  const float* __restrict__ rowpow, int M, int N, int K, int epi) {
+    using C = CfgI8Pair<BM>;
+    constexpr int S = C::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* xs = smem;                                  // S x [BM][128] digits of plane `rank`, 128B swizzle
+    uint8_t* ws = smem + S * C::kXBytes;                 // S x [128][128] weight codes, 128B swizzle
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ws + S * C::kWBytes);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+    float* stage = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(tmem_slot + 4) + 15) & ~uintptr_t(15));
+    float* rf_s = stage + C::kStageBytes / 4;            // row factors: [BM] mantissas, then [BM] powers
+
+    // full[s] (leader): all four tiles of stage s landed. release[s] (both):
+    // the MMAs reading stage s finished. acc_full, drain (both): multicast.
+    const uint32_t full0 = smem_addr(bars);
+    const uint32_t release0 = full0 + 8 * S;
+    const uint32_t acc_full = release0 + 8 * S;
+    const uint32_t drain = acc_full + 8;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int n0 = static_cast<int>(blockIdx.x >> 1) * (2 * kTileN) + static_cast<int>(rank) * kTileN;
+    const int num_kb = (K + C::kBK - 1) / C::kBK;
+    unsigned int* err = &g_tc_error;
+    const bool vec_out = epi == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && (N & 3) == 0;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(full0 + 8 * i, 1);
+            mbar_init(release0 + 8 * i, 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmap_x);
+        tma_prefetch_desc(&tmap_w);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_addr(tmem_slot), C::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // the leader's barriers exist before the peer's loads complete on them
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;  // accumulator: hi at columns [0, BM), lo at [BM, 2 BM)
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t full_leader0 = mapa_shared(full0, 0);
+            constexpr uint32_t kStageTx = 2 * (C::kXBytes + C::kWBytes);
+            const int first = num_kb < S ? num_kb : S;
+            for (int kb = 0; kb < first; ++kb) {
+                if (leader) mbar_arrive_expect_tx(full0 + 8 * kb, kStageTx);
+                tma_load_2d_pair(smem_addr(ws + kb * C::kWBytes), &tmap_w, kb * C::kBK, n0, full_leader0 + 8 * kb);
+            }
+            asm volatile("griddepcontrol.wait;" ::: "memory");  // the digit planes come from the prologue
+            for (int kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % S;
+                if (kb >= S) {
+                    if (!mbar_wait_cluster(release0 + 8 * s, ((kb / S) - 1) & 1, err, 1u)) break;
+                    if (leader) mbar_arrive_expect_tx(full0 + 8 * s, kStageTx);
+                    tma_load_2d_pair(smem_addr(ws + s * C::kWBytes), &tmap_w, kb * C::kBK, n0, full_leader0 + 8 * s);
+                }
+                tma_load_2d_pair(smem_addr(xs + s * C::kXBytes), &tmap_x, kb * C::kBK, static_cast<int>(rank) * M,
+                                 full_leader0 + 8 * s);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = idesc_i8_s32(2 * kTileN, C::kN);
+            for (int kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % S;
+                if (!mbar_wait_cluster(full0 + 8 * s, (kb / S) & 1, err, 2u)) break;
+                tc_fence_after();
+                const uint64_t adesc = smem_desc_sw128_kmajor(smem_addr(ws + s * C::kWBytes));
+                const uint64_t bdesc = smem_desc_sw128_kmajor(smem_addr(xs + s * C::kXBytes));
+                #pragma unroll
+                for (int j = 0; j < C::kBK / 32; ++j) {
+                    // K step of 32 int8 = 32 bytes inside the 128-byte swizzle rows.
+                    mma_i8_ss_pair(tmem + (j % C::kAcc) * C::kN, adesc + static_cast<uint64_t>(2 * j),
+                                   bdesc + static_cast<uint64_t>(2 * j), idesc, (kb > 0 || j >= C::kAcc) ? 1u : 0u);
+                }
+                mma_commit_pair(release0 + 8 * s, 0x3);
+            }
+            mma_commit_pair(acc_full, 0x3);
+            // Every MMA (and so every load it consumed) is finished before the
+            // pair releases tensor or shared memory.
+            mma_commit_pair(drain, 0x3);
+        }
+    } else {
+        // Epilogue: lane = weight row n of this CTA, 32 activation rows per chunk.
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const int n = n0 + row;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        const float sc = n < N ? __ldg(scale + n) : 0.0f;
+        asm volatile("griddepcontrol.wait;" ::: "memory");  // row factors come from the prologue
+        for (int i = threadIdx.x - kI8WarpEpi0 * 32; i < BM; i += 128) {
+            rf_s[i] = i < M ? __ldg(rowfactor + i) : 0.0f;
+            rf_s[BM + i] = i < M ? __ldg(rowpow + i) : 0.0f;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const bool ok = mbar_wait_cluster(acc_full, 0, err, 32u) && num_kb > 0;
+        if (__all_sync(0xffffffffu, ok)) {
+            tc_fence_after();
+            #pragma unroll 1
+            for (int c0 = 0; c0 < BM; c0 += 32) {
+                if (c0 >= M) break;
+                // Exact int32 hi and lo digit sums of activation rows c0 .. c0 + 31.
+                uint32_t h[32], l[32];
+                tmem_ld_32x32b_x32(tmem + lane_addr + c0, h);
+                tmem_ld_32x32b_x32(tmem + lane_addr + BM + c0, l);
+                tmem_wait_ld();
+                const int cnt = M - c0;
+                // ((acc * mantissa_m) * scale[n]) * 2^e_m, acc = 256 hi + lo.
+                float o[32];
+                #pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float acc = fmaf(256.0f, static_cast<float>(static_cast<int>(h[j])),
+                                           static_cast<float>(static_cast<int>(l[j])));
+                    o[j] = ((acc * rf_s[c0 + j]) * sc) * rf_s[BM + c0 + j];
+                }
+                if (vec_out && n0 + quarter * 32 + 32 <= N) {
+                    // [32 m][32 n] staging tile of this warp, out as float4 runs along n.
+                    float* st = stage + quarter * 1024;
+                    #pragma unroll
+                    for (int j = 0; j < 32; ++j) st[j * 32 + lane] = o[j];
+                    __syncwarp();
+                    const int q4 = lane & 7;
+                    const int mr = lane >> 3;
+                    #pragma unroll
+                    for (int it = 0; it < 8; ++it) {
+                        const int ml = it * 4 + mr;
+                        if (ml < cnt) {
+                            float* dst = out + static_cast<int64_t>(c0 + ml) * N + n0 + quarter * 32 + 4 * q4;
+                            *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(st + ml * 32 + 4 * q4);
+                        }
+                    }
+                    __syncwarp();
+                } else if (n < N) {
+                    float* base = out + static_cast<int64_t>(c0) * N + n;
+                    #pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (j < cnt) store_out(base + static_cast<int64_t>(j) * N, o[j], epi);
+                    }
+                }
+            }
+        }
+    }
+
+    if (warp == 1 && lane == 0) mbar_wait_cluster(drain, 0, err, 128u);
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, C::kTmemCols);
+    }
+}
+
 // ------------------------------------------------------------------ host side
 constexpr int kMaxDevices = 64;
 
@@ -2306,6 +2514,38 @@ int pick_splits_i8(int64_t tiles, int64_t num_kb) {
     return 1;
 }
 
+// The pair form of the int8 GEMM: 256 weight rows per cluster of two CTAs.
+template <int BM>
+popcornStatus_t launch_i8_pair(const CUtensorMap& tx, const CUtensorMap& tw, float* out, const float* scale,
+                               const float* rowfactor, const float* rowpow, int64_t M, int64_t N, int64_t K, int epi,
+                               cudaStream_t stream) {
+    using C = CfgI8Pair<BM>;
+    static bool attr_set[kMaxDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const bool known = dev >= 0 && dev < kMaxDevices;
+    if (!known || !attr_set[dev]) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(tc_i8_pair_kernel<BM>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+        if (e != cudaSuccess) return record_cuda(e);
+        if (known) attr_set[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * ceil_div(N, 2 * kTileN)));
+    cfg.blockDim = dim3(kI8Threads);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_i8_pair_kernel<BM>, tx, tw, out, scale, rowfactor, rowpow,
+                                             static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), epi);
+    if (e != cudaSuccess) return record_cuda(e);
+    return check_launch();
+}
+
 template <int BM>
 popcornStatus_t launch_i8(PFN_cuTensorMapEncodeTiled_v12000 encode, const int8_t* xd, const float* rowfactor,
                           const float* rowpow, float* part, int splits, float* out, const void* q,
@@ -2332,6 +2572,12 @@ popcornStatus_t launch_i8(PFN_cuTensorMapEncodeTiled_v12000 encode, const int8_t
         return POPCORN_ERROR_INVALID_VALUE;
     }
     const int64_t tiles = ceil_div(N, kTileN);
+    if constexpr (BM == 128) {
+        // Tiles that fill half the GPU without split-K: CTA pairs (measured
+        // ~10 % faster at M = 128; at 64-row tiles the pair's fixed cost
+        // outweighs the smaller stream, so those keep single CTAs).
+        if (splits == 1) return launch_i8_pair<BM>(tx, tw, out, scale, rowfactor, rowpow, M, N, K, epi, stream);
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(tiles * splits));
     cfg.blockDim = dim3(kI8Threads);

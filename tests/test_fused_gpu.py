@@ -100,7 +100,8 @@ def test_popcorn_silu_fixture_through_identity_weights(cuda):
 # activation rows, tensor cores (single CTA with split-K, CTA pairs), the
 # unfused sequence (K % 16 != 0).
 SHAPES = [(1, 4096, 4096), (1, 11008, 4096), (1, 4096, 11008), (1, 1000, 16384), (2, 4096, 4096), (2, 999, 8192),
-          (3, 2048, 4096), (4, 4097, 4096), (8, 4096, 4096), (64, 2048, 4096), (256, 4096, 4096), (3, 500, 1000)]
+          (3, 2048, 4096), (4, 4097, 4096), (8, 4096, 4096), (64, 2048, 4096), (100, 9600, 1024), (256, 4096, 4096),
+          (3, 500, 1000)]
 
 
 def _tol(M, N, K):

@@ -317,7 +317,8 @@ def test_tensor_path_rejects_what_it_cannot_run(cuda):
     assert st == pc.POPCORN_ERROR_INVALID_VALUE
 
 
-@pytest.mark.parametrize("N,K", [(1, 1), (3, 5), (64, 4096), (130, 4112), (7, 100)])
+@pytest.mark.parametrize("N,K", [(1, 1), (3, 5), (64, 4096), (130, 4112), (7, 100), (5, 48), (2000, 1040),
+                                 (3, 8192)])
 def test_dequantize_bitexact(cuda, N, K):
     import torch
 
@@ -331,7 +332,8 @@ def test_dequantize_bitexact(cuda, N, K):
     np.testing.assert_array_equal(got.view(np.uint32), oracle.dequantize(q, s).view(np.uint32))
 
 
-@pytest.mark.parametrize("N,K", [(1, 1), (3, 5), (64, 4096), (130, 4112), (7, 100), (4096, 4096)])
+@pytest.mark.parametrize("N,K", [(1, 1), (3, 5), (64, 4096), (130, 4112), (7, 100), (4096, 4096), (5, 48),
+                                 (2000, 1040), (3, 8192)])
 def test_dequantize_bf16_bitexact(cuda, N, K):
     # bf16 output: the f32 product rounded once to nearest even, bit for bit;
     # scales spanning many binades (ties and bf16 subnormals included).
