@@ -1060,7 +1060,9 @@ popcornStatus_t simt_dequant_matmul(float* out, const float* x, const int8_t* q,
         if (slices == 1) return launch_xs<2, 1, 8>(3, out, x, q, scale, M, N, K, stream);
         return launch_xs<2, 2, 4>(4, out, x, q, scale, M, N, K, stream);
     }
-    if (M <= 4 && slices == 1) return launch_xs<4, 1, 4>(5, out, x, q, scale, M, N, K, stream);
+    // Up to eight rows: two row groups of four (grid.y = 2) read each weight
+    // row twice, mostly from L2; still far ahead of gemv_kernel here.
+    if (M <= 8 && slices == 1) return launch_xs<4, 1, 4>(5, out, x, q, scale, M, N, K, stream);
     if (M == 1) return launch_gemv<1, 2>(0, out, x, q, scale, M, N, K, stream);
     if (M == 2) return launch_gemv<2, 2>(1, out, x, q, scale, M, N, K, stream);
     return launch_gemv<4, 2>(2, out, x, q, scale, M, N, K, stream);

@@ -200,6 +200,18 @@ def test_quantize_bitexact_vs_popcorn_kernel(cuda, K):
     np.testing.assert_array_equal(s1.cpu().numpy().view(np.uint32), so.view(np.uint32))
 
 
+@pytest.mark.parametrize("M,N,K", [(5, 1000, 4096), (6, 4096, 4096), (7, 513, 2048), (8, 300, 4000)])
+def test_f32_path_five_to_eight_rows(cuda, M, N, K):
+    # Five to eight activation rows on the CUDA-core path: two row groups of
+    # the x-stationary kernel (K <= 4096), or the generic kernel (K % 16 != 0).
+    import torch
+
+    x, q, s = random_case(M, N, K, 3 * M + N + K)
+    got = abi_matmul(torch, cuda, x, q, s, path=pc.PATH_SIMT_F32)
+    err = oracle.normwise_rel_err(got, oracle.dequant_matmul(x, q, s))
+    assert err <= TOL_F32, err
+
+
 def near_tie_rows(K, rows=8):
     """Rows whose values sit on and within a few ulps of every half-integer
     multiple of the row's scale (the boundaries where rint(v / scale) changes),
