@@ -63,18 +63,24 @@ WORKLOADS = {
     "quantize": dict(M=0, K=4096, N=4096, unit="GB/s", bound="hbm", op="quantize"),
     "dequantize": dict(M=0, K=4096, N=4096, unit="GB/s", bound="hbm", op="dequantize"),
     "dequantize_bf16": dict(M=0, K=4096, N=4096, unit="GB/s", bound="hbm", op="dequantize", out_bytes=2),
+    # The stack's qkv projection at 128 activation rows (4096 -> 12288): the
+    # int8 tensor path on CTA pairs; FLOPs = 2*M*N*K.
+    "qkv_m128": dict(M=128, K=4096, N=12288, unit="TFLOP/s", bound="tensor"),
 }
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of
 # the dominant kernel from one ncu capture of that workload; the command that
 # produced each figure is in the profiles/ summary named beside it.
 NCU_TRAFFIC = {
-    "decode": 16836864,    # profiles/gemv_xs_decode_m1_k4096_n4096.md
+    "decode": 16836096,    # profiles/gemv_stage_decode_m1_k4096_n4096.md
     "skinny": 45440256,    # profiles/tc_i8_skinny_m32_k4096_n11008.md
     "prefill": 35509504,   # profiles/tc_gemm_pair_prefill_m2048_k4096_n4096.md
     "grouped_decode": 17335296,  # profiles/grouped_xs_decode_m1_k4096_n4096_g128.md
     "int4_decode": 9476608,      # profiles/i4_xs_decode_m1_k4096_n4096_g128.md
     "mlp_decode": 93543168,      # profiles/fused_xs_mlp_decode_m1_k4096_n11008.md
+    "quantize": 72432640,        # profiles/quantize_row_block_n4096_k4096.md (codes partly still in L2)
+    "dequantize": 27141120,      # profiles/dequantize_n4096_k4096.md (output partly still in L2)
+    "qkv_m128": 51826176,        # profiles/tc_i8_pair_m128_k4096_n12288.md
 }
 
 
@@ -86,7 +92,7 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
     p.add_argument("--extras", default="skinny,prefill,grouped_decode,int4_decode,grouped_prefill,int4_prefill,"
-                                       "mlp_decode,quantize,dequantize,dequantize_bf16",
+                                       "mlp_decode,quantize,dequantize,dequantize_bf16,qkv_m128",
                    help="comma-separated extra single-GPU workloads reported beside the headline (N=1 only)")
     p.add_argument("--stack", default="1,128",
                    help="M values of the 32-layer 7B-shaped linear stack timed at every N ('none' to skip)")
@@ -350,7 +356,11 @@ class MlpSetup:
         self.u = torch.empty_like(self.out)
         self.xn = torch.empty_like(self.x)
         self.lib = pc.load_library()
+        self.Nl = N
         torch.cuda.synchronize()
+
+    def launches_per_step(self):
+        return 1 if self.fused else 2
 
     def step(self, i, stream_handle, group=None):
         j = i % self.sets
@@ -404,7 +414,11 @@ class OpSetup:
             self.q.append(q)
             self.s.append(sc)
         self.lib = pc.load_library()
+        self.Nl = N
         torch.cuda.synchronize()
+
+    def launches_per_step(self):
+        return 1
 
     def step(self, i, stream_handle, group=None):
         j = i % self.sets
@@ -798,7 +812,13 @@ def run_ours(args):
     pool = 2.5 * l2
 
     wl = WORKLOADS[args.workload]
-    setup = Setup(torch, pc, wl, rank, world, device, pool)
+    if wl.get("op") or wl.get("mlp"):
+        # The weight-side kernels and the fused MLP front are single-GPU workloads.
+        if world > 1:
+            raise SystemExit(f"--workload {args.workload} runs on one GPU")
+        setup = (OpSetup if wl.get("op") else MlpSetup)(torch, pc, wl, device, pool)
+    else:
+        setup = Setup(torch, pc, wl, rank, world, device, pool)
     sampler = ClockSampler(device)
     sampler.start()
     ms, clocks = time_graph(torch, setup, args.steps, args.warmup, args.soak_s, sampler, dist_on)
