@@ -13,6 +13,8 @@ Checks, in the spirit of popcorn's own suite (test/test_quantize.cu):
 """
 import ctypes
 
+import os
+
 import numpy as np
 import pytest
 
@@ -659,6 +661,36 @@ def test_decode_full_size_vs_oracle(cuda):
     x, q, s = random_case(1, 4096, 4096, 55)
     got = abi_matmul(torch, cuda, x, q, s)
     assert oracle.normwise_rel_err(got, oracle.dequant_matmul(x, q, s, fused=True, threads=8)) <= TOL_F32
+
+
+@needs_ref_gpu
+@pytest.mark.parametrize("M,N,K", [
+    (32, 11008, 4096),    # skinny decode batch (MLP up-projection)
+    (128, 12288, 4096),   # stack qkv at 128 rows: CTA pairs
+    (2048, 4096, 4096),   # prefill: persistent CTA pairs, f16 activations
+])
+def test_workload_sizes_vs_oracle_and_popcorn_kernel(cuda, M, N, K):
+    # The matmul workloads at their full sizes on the seeded generator's data
+    # (X ~ N(0,1), W ~ N(0,0.02), per-row int8): the library against the
+    # oracle (popcorn's loop order, fused multiply-add, all host threads) and
+    # against popcorn's own kernel rebuilt for sm_100a, same inputs.
+    import torch
+
+    x, q, s = random_case(M, N, K, 77 + M)
+    got = abi_matmul(torch, cuda, x, q, s)
+    assert pc.device_errors() == 0
+    threads = max(1, min(32, os.cpu_count() or 1))
+    ref = oracle.dequant_matmul(x, q, s, fused=True, threads=threads)
+    err = oracle.normwise_rel_err(got, ref)
+    assert err <= 5e-4, err
+    xd, qd, sd = dev(x, torch, cuda), dev(q, torch, cuda), dev(s, torch, cuda)
+    theirs = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    assert oracle.popcorn_ref_gpu().popcornDequantizeMatmul_i8f32(theirs.data_ptr(), xd.data_ptr(), qd.data_ptr(),
+                                                                  sd.data_ptr(), M, N, K, None) == 0
+    torch.cuda.synchronize()
+    theirs = theirs.cpu().numpy()
+    assert np.array_equal(theirs, ref), "popcorn's kernel and the oracle disagree"
+    assert oracle.normwise_rel_err(got, theirs) <= 5e-4
 
 
 def test_tensor_path_back_to_back_calls_reuse_scratch(cuda):
