@@ -141,6 +141,7 @@ popcornStatus_t peer_dequant_matmul(PeerMode mode, const PeerArgs& pa, float* ou
 // Read and clear the device error words of the bounded-wait kernels.
 cudaError_t tc_take_errors(unsigned int* bits);
 cudaError_t gemv_take_errors(unsigned int* bits);
+cudaError_t i4_take_errors(unsigned int* bits);
 
 }  // namespace pcb
 

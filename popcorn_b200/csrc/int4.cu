@@ -28,11 +28,18 @@
 //    from the stored parameters. Codes, scales and zero points are
 //    bit-identical to popcorn's kernels; no temporary buffer.
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace pcb {
+
+// Error bits of bounded waits in this file's kernels (read by
+// popcornB200DeviceErrors).
+__device__ unsigned int g_i4_error = 0;
+
 namespace {
 
 constexpr int kI4Threads = 256;
+constexpr unsigned int kI4StageTimeoutBit = 0x400u;  // staged int4 rows did not land within 1 s
 constexpr int kI4Warps = kI4Threads / 32;
 
 // Butterfly reduce-scatter of V values over a warp: afterwards the lanes with
@@ -102,6 +109,33 @@ __device__ __forceinline__ void widen8(uint32_t word, float2 (&c)[4]) {
                                      __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440 + j)));
         c[j] = __fadd2_rn(f, bias);
     }
+}
+
+// A slice holding an infinity or a NaN: popcorn's per-element form
+// w = (c - z) * s, acc = fma(x, w, acc) over the 16 elements in k order, so
+// the slice gives +-inf or NaN exactly where popcorn's sum does (the
+// factored form below would turn inf * (c - 8) - (z - 8) * inf into NaN).
+__device__ __forceinline__ float i4_direct_slice(uint2 w, const float4 (&xr)[4], float sc, float zp) {
+    const uint32_t words[2] = {w.x, w.y};
+    const float xk[16] = {xr[0].x, xr[0].y, xr[0].z, xr[0].w, xr[1].x, xr[1].y, xr[1].z, xr[1].w,
+                          xr[2].x, xr[2].y, xr[2].z, xr[2].w, xr[3].x, xr[3].y, xr[3].z, xr[3].w};
+    float acc = 0.0f;
+    #pragma unroll
+    for (int e = 0; e < 16; ++e) {
+        const uint32_t code = (words[e >> 3] >> (4 * (e & 7))) & 0xFu;
+        const float wk = __fmul_rn(__fsub_rn(static_cast<float>(code), zp), sc);
+        acc = __fmaf_rn(xk[e], wk, acc);
+    }
+    return acc;
+}
+
+__device__ __forceinline__ bool slice_finite(const float4 (&xr)[4]) {
+    bool ok = true;
+    #pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        ok = ok && isfinite(xr[c].x) && isfinite(xr[c].y) && isfinite(xr[c].z) && isfinite(xr[c].w);
+    }
+    return ok;
 }
 
 // MT activation rows (<= 4), U 16-element K slices per thread, R weight rows
@@ -201,6 +235,9 @@ i4_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const uint8_t
                 }
                 xsum[m] = s;
             }
+            bool fin[MT];
+            #pragma unroll
+            for (int m = 0; m < MT; ++m) fin[m] = slice_finite(xr[m][u]);
             #pragma unroll
             for (int r = 0; r < R; ++r) {
                 float2 a[MT];
@@ -219,8 +256,12 @@ i4_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const uint8_t
                 }
                 #pragma unroll
                 for (int m = 0; m < MT; ++m) {
-                    const float d = fmaf(-zc[r][u], xsum[m], a[m].x + a[m].y);
-                    acc[r * MT + m] = fmaf(sc[r][u], d, acc[r * MT + m]);
+                    if (fin[m]) {
+                        const float d = fmaf(-zc[r][u], xsum[m], a[m].x + a[m].y);
+                        acc[r * MT + m] = fmaf(sc[r][u], d, acc[r * MT + m]);
+                    } else {
+                        acc[r * MT + m] += i4_direct_slice(w[r][u], xr[m][u], sc[r][u], zc[r][u] + 8.0f);
+                    }
                 }
             }
         }
@@ -335,6 +376,207 @@ i4_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const uint8_t
     }
 }
 
+// Decode (M = 1) with the weights staged in shared memory before the
+// previous kernel of the stream has finished: the int4 counterpart of the
+// per-channel gemv_stage_kernel. One 512-thread CTA per SM owns a contiguous
+// range of rows; right after it starts, each row's packed codes, group scales
+// and group zero points go to the TMA engine as three 1-D bulk copies (one
+// mbarrier for all), and only then does the CTA wait for the previous kernel
+// and read x. At K = 4096, group 128, a CTA holds 28 rows in 64.5 KB, so the
+// next call's CTA fits on the same SM and streams its weights while this one
+// computes. Two groups of 256 threads take alternate rows; thread t of a
+// group owns the 16-element slice t (as in i4_xs_kernel<1, 1, 8>), and the
+// per-row arithmetic, the butterfly reduce-scatter (whose pairings do not
+// depend on a row's place in it) and the fixed-order sum across warps are
+// i4_xs_kernel's, so the two kernels return the same bits. Only weight-side
+// data is read before the wait (the matmul kernels that release this one
+// early never write codes, scales or zero points).
+constexpr int kI4StageGroups = 2;
+constexpr int kI4StageThreads = kI4StageGroups * kI4Threads;
+constexpr int kI4StageSR = 8;              // rows per group per iteration
+constexpr int kI4StageMaxRows = 64;
+constexpr int kI4StageBytes = 100 * 1024;  // room for a second CTA on the SM
+
+__global__ void __launch_bounds__(kI4StageThreads, 2)
+i4_stage_kernel(float* __restrict__ out, const float* __restrict__ x, const uint8_t* __restrict__ q,
+                const float* __restrict__ scale, const float* __restrict__ zero, int64_t N, int64_t K, int64_t gs) {
+    extern __shared__ __align__(16) uint8_t st[];
+    __shared__ __align__(8) uint64_t s_full;
+    const int grp = threadIdx.x / kI4Threads;
+    const int tid = threadIdx.x % kI4Threads;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int64_t G = gridDim.x;
+    const int64_t r0 = N * blockIdx.x / G;
+    const int rows = static_cast<int>(N * (blockIdx.x + 1) / G - r0);
+    const int rows_max = static_cast<int>((N + G - 1) / G);
+    const int64_t units = K >> 4;
+    const int groups = static_cast<int>(K / gs);
+    const int row_bytes = static_cast<int>(K >> 1);
+    uint8_t* codes = st;                                                            // [rows_max][K/2]
+    float* sc_s = reinterpret_cast<float*>(st + rows_max * row_bytes);              // [rows_max][groups]
+    float* zp_s = sc_s + rows_max * groups;                                         // [rows_max][groups]
+    float* part = zp_s + rows_max * groups;                                         // [rows_max][8 warps]
+    const uint32_t full = sm100::smem_addr(&s_full);
+
+    if (threadIdx.x == 0) {
+        sm100::mbar_init(full, 1);
+        sm100::fence_barrier_init();
+        sm100::mbar_arrive_expect_tx(full, static_cast<uint32_t>(rows * (row_bytes + 8 * groups)));
+    }
+    pdl_launch_dependents();
+    __syncthreads();
+    if (threadIdx.x < rows) {
+        const int r = threadIdx.x;
+        sm100::bulk_load_1d(sm100::smem_addr(codes + r * row_bytes), q + (r0 + r) * row_bytes,
+                            static_cast<uint32_t>(row_bytes), full);
+    } else if (threadIdx.x >= 128 && threadIdx.x < 128 + rows) {
+        const int r = threadIdx.x - 128;
+        sm100::bulk_load_1d(sm100::smem_addr(sc_s + r * groups), scale + (r0 + r) * groups,
+                            static_cast<uint32_t>(4 * groups), full);
+    } else if (threadIdx.x >= 256 && threadIdx.x < 256 + rows) {
+        const int r = threadIdx.x - 256;
+        sm100::bulk_load_1d(sm100::smem_addr(zp_s + r * groups), zero + (r0 + r) * groups,
+                            static_cast<uint32_t>(4 * groups), full);
+    } else if (threadIdx.x == kI4StageThreads - 1) {
+        prefetch_l2_range(x, K * static_cast<int64_t>(sizeof(float)), 0, 1);
+    }
+    pdl_wait();
+
+    // This thread's 16 activations (zero beyond K), as i4_xs_kernel loads them.
+    const bool in_k = tid < units;
+    float4 xr[4];
+    #pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        xr[c] = in_k ? __ldg(reinterpret_cast<const float4*>(x + tid * 16) + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    const int g = in_k ? static_cast<int>(tid / (gs >> 4)) : 0;
+    if (!sm100::mbar_wait(full, 0, &g_i4_error, kI4StageTimeoutBit)) {
+        sm100::mbar_wait(full, 0, &g_i4_error, kI4StageTimeoutBit);
+    }
+
+    // The row loop: this group's rows rg, rg + 2, ..., SR at a time; `dot`
+    // returns this thread's partial of one row from its staged bytes.
+    auto run = [&](auto&& dot) {
+        for (int rg = grp; rg < rows; rg += kI4StageSR * kI4StageGroups) {
+            float acc[kI4StageSR];
+            #pragma unroll
+            for (int r = 0; r < kI4StageSR; ++r) {
+                const int row = rg + r * kI4StageGroups;
+                acc[r] = 0.0f;
+                if (row < rows && in_k) {
+                    const uint2 w = *reinterpret_cast<const uint2*>(codes + row * row_bytes + tid * 8);
+                    acc[r] = dot(w, sc_s[row * groups + g], zp_s[row * groups + g]);
+                }
+            }
+            const float total = i4_reduce_scatter<kI4StageSR>(acc, lane);
+            constexpr int span = 32 / kI4StageSR;
+            if ((lane % span) == 0) {
+                const int row = rg + (lane / span) * kI4StageGroups;
+                if (row < rows) part[row * kI4Warps + warp] = total;
+            }
+        }
+    };
+
+    // Fixed point unless the warp holds a non-finite x or a slice max
+    // outside [2^-90, 2^100] (i4_xs_kernel's rule and scaling).
+    uint32_t mb = 0;
+    #pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const float4 v = xr[c];
+        mb = max(mb, max(max(__float_as_uint(v.x) & 0x7FFFFFFFu, __float_as_uint(v.y) & 0x7FFFFFFFu),
+                         max(__float_as_uint(v.z) & 0x7FFFFFFFu, __float_as_uint(v.w) & 0x7FFFFFFFu)));
+    }
+    const bool bad = mb != 0u && (mb < 0x12800000u || mb > 0x71800000u);
+    if (!__any_sync(0xffffffffu, bad)) {
+        float up = 1.0f, down = 1.0f;
+        if (mb != 0u) {
+            const int ex = 148 - static_cast<int>(mb >> 23);  // max |x| * 2^ex < 2^22
+            up = __int_as_float((ex + 127) << 23);
+            down = __int_as_float((127 - ex) << 23);
+        }
+        int xi[16];
+        #pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            xi[4 * c] = __float2int_rn(xr[c].x * up);
+            xi[4 * c + 1] = __float2int_rn(xr[c].y * up);
+            xi[4 * c + 2] = __float2int_rn(xr[c].z * up);
+            xi[4 * c + 3] = __float2int_rn(xr[c].w * up);
+        }
+        int xs = 0;
+        #pragma unroll
+        for (int e = 0; e < 16; ++e) xs += xi[e];
+        uint32_t digit[2][2][3];
+        #pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            #pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                const int e = 8 * h + p;
+                const uint32_t a = xi[e], b = xi[e + 2], c = xi[e + 4], d = xi[e + 6];
+                const uint32_t t01 = __byte_perm(a, b, 0x5140), t23 = __byte_perm(c, d, 0x5140);
+                const uint32_t v01 = __byte_perm(a, b, 0x7362), v23 = __byte_perm(c, d, 0x7362);
+                digit[h][p][0] = __byte_perm(t01, t23, 0x5410);
+                digit[h][p][1] = __byte_perm(t01, t23, 0x7632);
+                digit[h][p][2] = __byte_perm(v01, v23, 0x5410);
+            }
+        }
+        run([&](uint2 w, float sc, float zp) {
+            const float zc = zp - 8.0f;
+            unsigned s0 = 0u, s1 = 0u;
+            int s2 = 0;
+            const uint32_t words[2] = {w.x, w.y};
+            #pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t lo = words[h] & 0x0F0F0F0Fu;
+                const uint32_t hi = (words[h] >> 4) & 0x0F0F0F0Fu;
+                s0 = __dp4a(digit[h][0][0], lo, s0);
+                s0 = __dp4a(digit[h][1][0], hi, s0);
+                s1 = __dp4a(digit[h][0][1], lo, s1);
+                s1 = __dp4a(digit[h][1][1], hi, s1);
+                s2 = __dp4a(static_cast<int>(digit[h][0][2]), static_cast<int>(lo), s2);
+                s2 = __dp4a(static_cast<int>(digit[h][1][2]), static_cast<int>(hi), s2);
+            }
+            const int t = s2 * 65536 + static_cast<int>(s1 * 256u + s0) - 8 * xs;
+            const float d = fmaf(-zc, static_cast<float>(xs), static_cast<float>(t));
+            return fmaf(sc, d, 0.0f) * down;
+        });
+    } else {
+        float2 xv[8];
+        float s = 0.0f;
+        #pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const float4 v = xr[c];
+            s += (v.x + v.y) + (v.z + v.w);
+            xv[2 * c] = make_float2(v.x, v.y * 0.0625f);
+            xv[2 * c + 1] = make_float2(v.z, v.w * 0.0625f);
+        }
+        const float xsum = s;
+        const bool fin = slice_finite(xr);
+        run([&](uint2 w, float sc, float zp) {
+            if (!fin) return i4_direct_slice(w, xr, sc, zp);
+            const float zc = zp - 8.0f;
+            float2 a = make_float2(0.0f, 0.0f);
+            const uint32_t words[2] = {w.x, w.y};
+            #pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float2 c[4];
+                widen8(words[h], c);
+                #pragma unroll
+                for (int j = 0; j < 4; ++j) a = __ffma2_rn(xv[4 * h + j], c[j], a);
+            }
+            const float d = fmaf(-zc, xsum, a.x + a.y);
+            return fmaf(sc, d, 0.0f);
+        });
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < rows; i += kI4StageThreads) {
+        float sum = 0.0f;
+        #pragma unroll
+        for (int wv = 0; wv < kI4Warps; ++wv) sum += part[i * kI4Warps + wv];
+        out[r0 + i] = sum;
+    }
+}
+
 // Position of element i of a group in the order in which popcorn's min/max
 // block (256 threads, thread t scanning t, t + 256, ...; a halving tree that
 // keeps the lower partner on a tie) lets it win a tie: threads rank by their
@@ -421,6 +663,39 @@ i4_pack_kernel(uint8_t* __restrict__ out, const float* __restrict__ scale, const
     }
 }
 
+// The staged decode kernel when its conditions hold (M = 1, K <= 4096 with
+// 16-byte rows, group scales and zero points in 16-byte rows, every CTA's
+// rows within kI4StageBytes); returns false (nothing launched) otherwise.
+bool launch_i4_stage(popcornStatus_t* stp, float* out, const float* x, const uint8_t* q, const float* scale,
+                     const float* zero, int64_t N, int64_t K, int64_t gs, cudaStream_t stream) {
+    const int64_t groups = K / gs;
+    if (K > 16 * kI4Threads || K % 32 != 0 || gs % 16 != 0 || groups % 4 != 0) return false;
+    if (!aligned16(x) || !aligned16(q) || !aligned16(scale) || !aligned16(zero)) return false;
+    const int64_t G = device_sm_count() < N ? device_sm_count() : N;
+    const int64_t rows_max = ceil_div(N, G);
+    const int64_t smem = rows_max * (K / 2 + 8 * groups) + rows_max * kI4Warps * 4;
+    if (rows_max > kI4StageMaxRows || smem > kI4StageBytes) return false;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const bool known = dev >= 0 && dev < 64;
+    if (!known || !attr_set[dev]) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(i4_stage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kI4StageBytes);
+        if (e != cudaSuccess) {
+            *stp = record_cuda(e);
+            return true;
+        }
+        if (known) attr_set[dev] = true;
+    }
+    cudaLaunchAttribute attr[1];
+    const cudaLaunchConfig_t cfg = pdl_config(dim3(static_cast<unsigned>(G)), dim3(kI4StageThreads),
+                                              static_cast<size_t>(smem), stream, attr);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, i4_stage_kernel, out, x, q, scale, zero, N, K, gs);
+    *stp = (e != cudaSuccess) ? record_cuda(e) : check_launch();
+    return true;
+}
+
 template <int MT, int U, int R>
 popcornStatus_t launch_i4_xs(float* out, const float* x, const uint8_t* q, const float* scale, const float* zero,
                              int64_t M, int64_t N, int64_t K, int64_t gs, cudaStream_t stream) {
@@ -435,6 +710,14 @@ popcornStatus_t launch_i4_xs(float* out, const float* x, const uint8_t* q, const
 }
 
 }  // namespace
+
+cudaError_t i4_take_errors(unsigned int* bits) {
+    unsigned int zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(bits, g_i4_error, sizeof(unsigned int));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_i4_error, &zero, sizeof(unsigned int));
+    return e;
+}
+
 }  // namespace pcb
 
 extern "C" popcornStatus_t popcornDequantizeMatmulGrouped_i4f32(float* out, const float* x, const uint8_t* qweight,
@@ -460,6 +743,8 @@ extern "C" popcornStatus_t popcornDequantizeMatmulGrouped_i4f32(float* out, cons
     const bool grid_ok = ceil_div(M, 4) <= 65535 && ceil_div(N, 2) <= 0x7FFFFFFF;
     if (!tiny && aligned && group_size % 16 == 0 && slices <= 4 && grid_ok) {
         if (M == 1) {
+            popcornStatus_t st = POPCORN_SUCCESS;
+            if (launch_i4_stage(&st, out, x, qweight, scale, zero, N, K, group_size, stream)) return st;
             if (slices == 1) return launch_i4_xs<1, 1, 8>(out, x, qweight, scale, zero, M, N, K, group_size, stream);
             if (slices == 2) return launch_i4_xs<1, 2, 4>(out, x, qweight, scale, zero, M, N, K, group_size, stream);
             return launch_i4_xs<1, 4, 2>(out, x, qweight, scale, zero, M, N, K, group_size, stream);

@@ -97,6 +97,9 @@ def test_matches_popcorn_kernel_bitwise(cuda, shape):
     (2, 4096, 4096, 64), (2, 999, 8192, 256), (3, 1000, 4096, 32), (4, 4097, 4096, 16),
     (16, 2048, 1024, 128), (33, 512, 2048, 512), (8, 300, 96, 24), (5, 1000, 4112, 16), (1, 5000, 4096, 4096),
     (2, 3000, 1030, 10), (1, 2000, 4098, 2),
+    # staged decode (M = 1, K <= 4096, rows in shared memory): ragged row
+    # counts per SM, one row per CTA, 41 rows per CTA
+    (1, 1000, 4096, 32), (1, 100, 2048, 64), (1, 6000, 4096, 128),
 ])
 def test_random_shapes_match_oracle(cuda, shape):
     import torch
@@ -106,6 +109,32 @@ def test_random_shapes_match_oracle(cuda, shape):
     got = _matmul(torch, cuda, x, q, s, z, gs)
     ref = oracle.dequant_matmul_grouped_i4(x, q, s, z, gs, fused=True, threads=8)
     assert oracle.normwise_rel_err(got, ref) <= TOL_F32
+
+
+@pytest.mark.parametrize("kind", ["nan", "inf", "tiny"])
+def test_decode_nonfinite_and_tiny_activations(cuda, kind):
+    # M = 1 with a NaN, an infinity or a slice of denormals in x: those warps
+    # leave the fixed-point layout; every output must match the oracle's
+    # (non-finite exactly where popcorn's sum is).
+    import torch
+
+    M, N, K, gs = 1, 2000, 4096, 128
+    x, q, s, z = _case(M, N, K, gs, 31)
+    x = x.copy()
+    if kind == "nan":
+        x[0, 37] = np.nan
+    elif kind == "inf":
+        x[0, 1000] = np.inf
+    else:
+        x[0, 2048:2064] = np.float32(1e-40)
+    got = _matmul(torch, cuda, x, q, s, z, gs)
+    ref = oracle.dequant_matmul_grouped_i4(x, q, s, z, gs, fused=True, threads=8)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    assert np.array_equal(np.isinf(got), np.isinf(ref))
+    fin = np.isfinite(ref)
+    if fin.any():
+        assert oracle.normwise_rel_err(got[fin], ref[fin]) <= TOL_F32
+        assert np.array_equal(np.sign(got[~fin & ~np.isnan(ref)]), np.sign(ref[~fin & ~np.isnan(ref)]))
 
 
 @pytest.mark.parametrize("offsets", [(1, 0), (0, 1), (0, 4)])
