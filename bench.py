@@ -76,7 +76,7 @@ NCU_TRAFFIC = {
     "skinny": 45440256,    # profiles/tc_i8_skinny_m32_k4096_n11008.md
     "prefill": 35509504,   # profiles/tc_gemm_pair_prefill_m2048_k4096_n4096.md
     "grouped_decode": 17335296,  # profiles/grouped_xs_decode_m1_k4096_n4096_g128.md
-    "int4_decode": 9476608,      # profiles/i4_xs_decode_m1_k4096_n4096_g128.md
+    "int4_decode": 9502464,      # profiles/i4_stage_decode_m1_k4096_n4096_g128.md
     "mlp_decode": 93543168,      # profiles/fused_xs_mlp_decode_m1_k4096_n11008.md
     "quantize": 72432640,        # profiles/quantize_row_block_n4096_k4096.md (codes partly still in L2)
     "dequantize": 27141120,      # profiles/dequantize_n4096_k4096.md (output partly still in L2)
@@ -325,8 +325,10 @@ class Setup:
         if self.gs:
             fmt = "int4" if self.bits == 4 else "grouped"
             return f"{fmt}_{'tensor_f16' if self.grouped_tensor() else 'f32'} (group {self.gs})"
-        return self.pc.PATH_NAMES[self.pc.select_path(self.x[0].data_ptr(), self.q[0].data_ptr(),
-                                                      self.M, self.Nl, self.K)]
+        path = self.pc.select_path(self.x[0].data_ptr(), self.q[0].data_ptr(), self.M, self.Nl, self.K)
+        if path == self.pc.PATH_TENSOR_F16 and self.M <= 128 and self.K <= 65536:
+            return "tensor_i8 (activations as two int8 digits)"
+        return self.pc.PATH_NAMES[path]
 
 
 class MlpSetup:
