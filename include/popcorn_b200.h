@@ -139,9 +139,13 @@ popcornStatus_t popcornDequantizeMatmulNoAlloc_i8f32(
 );
 
 /* Diagnostic: copies the current device's kernel error bits into *flags and
- * clears them (synchronous). Non-zero bits mean a bounded wait inside a
- * tensor-core kernel gave up (the kernel ended early instead of hanging);
- * the results of that launch are not valid. */
+ * clears them (synchronous). Non-zero bits mean a bounded wait (1 s) inside
+ * a kernel gave up -- the kernel ended early instead of hanging -- and the
+ * results of that launch are not valid. Bits 0-15: tensor-core kernels
+ * (pipeline barriers). Bits 16-31, shifted by 16: 0x100 a fused collective
+ * waited for another rank's values, 0x200 a decode kernel waited for the
+ * weight rows it staged in shared memory, 0x400 the int4 decode kernel
+ * likewise. */
 int popcornB200DeviceErrors(unsigned int* flags);
 
 /*
