@@ -24,6 +24,12 @@
 //    the stream, so under programmatic dependent launch the next call's
 //    weight stream overlaps this call; same arithmetic and bits as
 //    gemv_xs_kernel. Also behind the fused all-gather / all-reduce.
+//  * gemv_mma_kernel -- the staged decode for K = 1024, 2048, 4096 with the
+//    dot products on the warp-level tensor path (mma.sync m16n8k32, s8 x s8
+//    -> s32): activations as four signed base-256 digits of a 30-bit fixed
+//    point value per warp, exact integer column sums, partials combined in
+//    double and rounded once. Takes the place of gemv_stage_kernel (and
+//    behind the fused collectives) wherever its rows fit.
 //  * gemv_kernel -- other aligned shapes (larger K or M): activations staged
 //    in shared memory with cp.async, weights streamed per warp.
 //  * generic_kernel -- any shape / alignment.
@@ -809,6 +815,238 @@ gemv_stage_kernel(float* __restrict__ out, const float* __restrict__ x, const in
     }
 }
 
+// ---------------------------------------------------------- gemv_mma_kernel
+// The staged decode GEMV (M = 1, K = 1024, 2048 or 4096) with its dot
+// products on the tensor pipe: mma.sync m16n8k32, signed 8-bit A and B,
+// s32 accumulate. Staging is gemv_stage_kernel's (rows copied into shared
+// memory by 1-D bulk copies before griddepcontrol.wait, one CTA per SM with
+// room for the next call's), except that rows sit K + 16 bytes apart, so
+// the eight rows an ldmatrix phase reads fall in eight different 16-byte
+// bank groups.
+//
+// Warp w owns the K-range [w K/16, (w + 1) K/16) and every row of the CTA.
+// Its activations become 32-bit fixed point X = rint(x 2^s) with one power
+// of two per warp (max |X| < 2^30), written as four signed bytes
+// X = sum_d d_d 256^d, d_d in [-128, 127] (the bytes of X + 0x80808080, each
+// xor 0x80). B column n < 4 of a 32-deep k-step holds digit n of the
+// step's 32 activations, columns 4..7 are zero; A is 16 weight rows x 32
+// codes from ldmatrix. The four int32 column sums of a row are exact
+// (|code * digit| < 2^14, at most 256 terms), so the warp's partial is the
+// exact integer sum_d 256^d D_d times 2^-s, formed in double. The partials of
+// the 16 warps are added in warp order in double and rounded once after the
+// channel scale: the result is the dot product of the codes with x rounded
+// to ~2^-30 of each warp's max |x|, correctly rounded -- closer to the exact
+// product than popcorn's f32 sum. A warp whose activations hold a non-finite
+// value or a max |x| outside [2^-90, 2^100] adds its K-range in f32 instead
+// (codes widened exactly), so NaN and infinities propagate as in popcorn's.
+constexpr int kMmaWarps = 16;
+constexpr int kMmaThreads = kMmaWarps * 32;
+// Staged bytes (rows x (K + 16)) of one CTA: two CTAs, each with 1 KB of
+// reserved and a few bytes of static shared memory, fit in an SM's 228 KB.
+constexpr int kMmaStageBytes = (228 * 1024 - 2 * 1024) / 2 - 64;
+
+__device__ __forceinline__ void mma_s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&a)[4], uint32_t saddr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+                 : "r"(saddr));
+}
+
+template <int KS, int MODE>
+__global__ void __launch_bounds__(kMmaThreads, 2)
+gemv_mma_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* __restrict__ q,
+                const float* __restrict__ scale, int64_t N, int64_t K, const PeerArgs pa) {
+    extern __shared__ __align__(16) uint8_t stage[];  // [rows][K + 16]
+    __shared__ unsigned int s_e;
+    __shared__ __align__(8) uint64_t s_full;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t G = gridDim.x;
+    const int64_t r0 = N * blockIdx.x / G;
+    const int rows = static_cast<int>(N * (blockIdx.x + 1) / G - r0);
+    const int k32 = static_cast<int>(K);
+    const int pitch = k32 + 16;
+    const uint32_t full = sm100::smem_addr(&s_full);
+    const uint32_t base = sm100::smem_addr(stage);
+
+    if (threadIdx.x == 0) {
+        sm100::mbar_init(full, 1);
+        sm100::fence_barrier_init();
+        sm100::mbar_arrive_expect_tx(full, static_cast<uint32_t>(rows * K));  // < 2^20 - 1
+    }
+    pdl_launch_dependents();
+    __syncthreads();
+    if (threadIdx.x < rows) {
+        sm100::bulk_load_1d(base + threadIdx.x * pitch, q + (r0 + threadIdx.x) * K, static_cast<uint32_t>(k32), full);
+    } else if (threadIdx.x == kMmaThreads - 1) {
+        prefetch_l2_range(x, K * static_cast<int64_t>(sizeof(float)), 0, 1);
+    }
+    // Channel scales of the rows a thread will finish (weight-side, like the rows).
+    const float sc_row = static_cast<int>(threadIdx.x) < rows ? __ldg(scale + r0 + threadIdx.x) : 0.0f;
+    pdl_wait();
+    if constexpr (MODE != kPeerNone) {
+        if (threadIdx.x == 0) s_e = *reinterpret_cast<volatile unsigned int*>(pa.state) + 1u;
+    }
+
+    // This warp's K-range and its activations: lane (g, t) = (lane / 4,
+    // lane % 4) reads, for k-step c, the four values at 32 c + 4 t + 16 h,
+    // h = g / 4 (the even-k half of the step for g < 4, the odd half above).
+    const int kw = warp * (k32 / kMmaWarps);
+    const int g = lane >> 2;
+    const int t = lane & 3;
+    const int h = g >> 2;
+    const float4* xw = reinterpret_cast<const float4*>(x + kw + 4 * t + 16 * h);
+    uint32_t mb = 0;
+    #pragma unroll
+    for (int c = 0; c < KS; ++c) {
+        const float4 v = __ldg(xw + 8 * c);
+        mb = max(mb, max(max(__float_as_uint(v.x) & 0x7FFFFFFFu, __float_as_uint(v.y) & 0x7FFFFFFFu),
+                         max(__float_as_uint(v.z) & 0x7FFFFFFFu, __float_as_uint(v.w) & 0x7FFFFFFFu)));
+    }
+    mb = __reduce_max_sync(0xffffffffu, mb);
+    const bool fixed = mb == 0u || (mb >= 0x12800000u && mb <= 0x71800000u);
+    // max |x| * 2^s in [2^29, 2^30): s = 29 - exponent of max |x|.
+    const int s_exp = mb == 0u ? 0 : 29 - (static_cast<int>(mb >> 23) - 127);
+    const float up = mb == 0u ? 1.0f : __int_as_float((s_exp + 127) << 23);
+
+    if (!sm100::mbar_wait(full, 0, &g_gemv_error, kStageTimeoutBit)) {
+        sm100::mbar_wait(full, 0, &g_gemv_error, kStageTimeoutBit);
+    }
+
+    // Partial sums of this warp for every row, into registers: row-group j
+    // (16 rows), lane (g, t) ends up with rows 16 j + g and 16 j + g + 8.
+    // K = 4096 holds at most 28 rows (two groups); K-steps alternate between
+    // kSets accumulators so no chain of dependent mma is longer than two.
+    constexpr int kMaxGroups = KS == 8 ? 2 : 4;
+    constexpr int kSets = KS == 8 ? 4 : 2;
+    const int groups = (rows + 15) >> 4;
+    double part_lo[kMaxGroups], part_hi[kMaxGroups];  // rows 16 j + g, 16 j + g + 8
+    if (fixed) {
+        int d[kMaxGroups][kSets][4];
+        #pragma unroll
+        for (int j = 0; j < kMaxGroups; ++j) {
+            #pragma unroll
+            for (int e2 = 0; e2 < kSets; ++e2) d[j][e2][0] = d[j][e2][1] = d[j][e2][2] = d[j][e2][3] = 0;
+        }
+        // ldmatrix row addresses of this lane: matrix i = lane / 8 (rows + 8 (i & 1),
+        // k + 16 (i >> 1)), row lane % 8 of it.
+        const int mi = lane >> 3;
+        const int mrow = (lane & 7) + 8 * (mi & 1);
+        const int mk = 16 * (mi >> 1);
+        const uint32_t sel = static_cast<uint32_t>((g & 3) | (((g & 3) + 4) << 4));
+        #pragma unroll
+        for (int c = 0; c < KS; ++c) {
+            // B fragment of k-step c: digit g of the four activations of this lane.
+            const float4 v = __ldg(xw + 8 * c);
+            const uint32_t y0 = static_cast<uint32_t>(__float2int_rn(v.x * up)) + 0x80808080u;
+            const uint32_t y1 = static_cast<uint32_t>(__float2int_rn(v.y * up)) + 0x80808080u;
+            const uint32_t y2 = static_cast<uint32_t>(__float2int_rn(v.z * up)) + 0x80808080u;
+            const uint32_t y3 = static_cast<uint32_t>(__float2int_rn(v.w * up)) + 0x80808080u;
+            const uint32_t t01 = __byte_perm(y0, y1, sel);
+            const uint32_t t23 = __byte_perm(y2, y3, sel);
+            const uint32_t bw = __byte_perm(t01, t23, 0x5410) ^ 0x80808080u;
+            const uint32_t odd = __shfl_down_sync(0xffffffffu, bw, 16);  // digit g of the step's odd half
+            const uint32_t b0 = g < 4 ? bw : 0u;
+            const uint32_t b1 = g < 4 ? odd : 0u;
+            const int k0 = kw + 32 * c + mk;
+            #pragma unroll
+            for (int j = 0; j < kMaxGroups; ++j) {
+                if (j < groups) {
+                    int r = 16 * j + mrow;
+                    r = r < rows ? r : rows - 1;  // past the last row: read it again, never stored
+                    uint32_t a[4];
+                    ldmatrix_x4(a, base + r * pitch + k0);
+                    mma_s8_16832(d[j][c % kSets], a, b0, b1);
+                }
+            }
+        }
+        // Column sums d0 = digit 2t, d1 = digit 2t + 1 of row g (d2, d3: row g + 8);
+        // lanes t = 0, 1 hold digits 0-1 and 2-3.
+        const double down = __longlong_as_double(static_cast<long long>(1023 - s_exp) << 52);
+        #pragma unroll
+        for (int j = 0; j < kMaxGroups; ++j) {
+            #pragma unroll
+            for (int e2 = 1; e2 < kSets; ++e2) {  // exact: |column sum| < 2^22
+                #pragma unroll
+                for (int v = 0; v < 4; ++v) d[j][0][v] += d[j][e2][v];
+            }
+            const double lo0 = static_cast<double>(d[j][0][0]) + 256.0 * static_cast<double>(d[j][0][1]);
+            const double lo8 = static_cast<double>(d[j][0][2]) + 256.0 * static_cast<double>(d[j][0][3]);
+            const double hi0 = __shfl_down_sync(0xffffffffu, lo0, 1);
+            const double hi8 = __shfl_down_sync(0xffffffffu, lo8, 1);
+            part_lo[j] = (hi0 * 65536.0 + lo0) * down;
+            part_hi[j] = (hi8 * 65536.0 + lo8) * down;
+        }
+    } else {
+        // f32 form of this warp's K-range (rare: non-finite or extreme x);
+        // lane r % 32 keeps row r's sum.
+        float fb0 = 0.0f, fb1 = 0.0f;
+        for (int r = 0; r < rows; ++r) {
+            const int8_t* qr = reinterpret_cast<const int8_t*>(stage + r * pitch + kw);
+            float a = 0.0f;
+            for (int k = lane; k < k32 / kMmaWarps; k += 32) a = fmaf(__ldg(x + kw + k), static_cast<float>(qr[k]), a);
+            #pragma unroll
+            for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+            if (lane == (r & 31)) {
+                if (r < 32) fb0 = a;
+                else fb1 = a;
+            }
+        }
+        #pragma unroll
+        for (int j = 0; j < kMaxGroups; ++j) part_lo[j] = part_hi[j] = 0.0;
+        part_lo[0] = static_cast<double>(fb0);
+        part_hi[0] = static_cast<double>(fb1);
+    }
+    __syncthreads();  // every read of the staged rows is done: reuse them as [16][rows] doubles
+    double* part = reinterpret_cast<double*>(stage);
+    if (fixed) {
+        if (t == 0) {
+            #pragma unroll
+            for (int j = 0; j < kMaxGroups; ++j) {
+                if (16 * j + g < rows) part[warp * rows + 16 * j + g] = part_lo[j];
+                if (16 * j + g + 8 < rows) part[warp * rows + 16 * j + g + 8] = part_hi[j];
+            }
+        }
+    } else {
+        if (lane < rows) part[warp * rows + lane] = part_lo[0];
+        if (lane + 32 < rows) part[warp * rows + lane + 32] = part_hi[0];
+    }
+    __syncthreads();
+    unsigned int e = 0;
+    if constexpr (MODE != kPeerNone) e = s_e;
+    if (static_cast<int>(threadIdx.x) < rows) {
+        const int i = threadIdx.x;
+        double sum = 0.0;
+        #pragma unroll
+        for (int w = 0; w < kMmaWarps; ++w) sum += part[w * rows + i];
+        const float val = static_cast<float>(sum * static_cast<double>(sc_row));
+        if constexpr (MODE == kPeerGather) {
+            const int64_t idx = pa.n_offset + r0 + i;
+            out[idx] = val;
+            const int64_t slot = (e & 1u) * pa.half_words + idx;
+            for (int p = 0; p < pa.world; ++p) {
+                if (p != pa.rank) st_relaxed_sys_u64(pa.recv[p] + slot, tagged(e, val));
+            }
+        } else if constexpr (MODE == kPeerReduce) {
+            const int64_t slot = (e & 1u) * pa.half_words + pa.rank * N + r0 + i;
+            for (int p = 0; p < pa.world; ++p) st_relaxed_sys_u64(pa.recv[p] + slot, tagged(e, val));
+        } else {
+            out[r0 + i] = val;
+        }
+    }
+    if constexpr (MODE != kPeerNone) {
+        __syncthreads();
+        peer_finish<MODE>(pa, out, 1, N, e);
+    }
+}
+
 // ------------------------------------------------------------ generic_kernel
 __global__ void __launch_bounds__(256)
 generic_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* __restrict__ q,
@@ -982,11 +1220,49 @@ bool launch_stage_t(popcornStatus_t* st, float* out, const float* x, const int8_
     return true;
 }
 
+// Staged decode GEMV on the tensor pipe: K in {1024, 2048, 4096} and every
+// CTA's rows within kMmaStageBytes (and kStageMaxRows); returns false
+// (nothing launched) otherwise.
+template <int MODE>
+bool launch_mma(popcornStatus_t* st, float* out, const float* x, const int8_t* q, const float* scale, int64_t N,
+                int64_t K, cudaStream_t stream, const PeerArgs* peer) {
+    if (K != 1024 && K != 2048 && K != 4096) return false;
+    const int64_t G = device_sm_count() < N ? device_sm_count() : N;
+    const int64_t rows = ceil_div(N, G);
+    if (rows > kStageMaxRows || rows * (K + 16) > kMmaStageBytes) return false;
+    auto kern = K == 4096 ? gemv_mma_kernel<8, MODE> : (K == 2048 ? gemv_mma_kernel<4, MODE> : gemv_mma_kernel<2, MODE>);
+    static bool attr_set[kMaxDevices][3] = {};
+    const int ki = K == 4096 ? 2 : (K == 2048 ? 1 : 0);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const bool cached = dev >= 0 && dev < kMaxDevices;
+    if (!cached || !attr_set[dev][ki]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaStageBytes);
+        if (e == cudaSuccess) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     cudaSharedmemCarveoutMaxShared);
+        }
+        if (e != cudaSuccess) {
+            *st = record_cuda(e);
+            return true;
+        }
+        if (cached) attr_set[dev][ki] = true;
+    }
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_config(dim3(static_cast<unsigned>(G)), dim3(kMmaThreads),
+                                        static_cast<size_t>(rows * (K + 16)), stream, attr);
+    const PeerArgs none = {};
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, out, x, q, scale, N, K, peer != nullptr ? *peer : none);
+    *st = (e != cudaSuccess) ? record_cuda(e) : check_launch();
+    return true;
+}
+
 // K % 16 == 0, K <= 8192 (two slices per thread fit in 64 registers),
 // 16-byte aligned x and q (vector_ok).
 template <int MODE>
 bool launch_stage(popcornStatus_t* st, float* out, const float* x, const int8_t* q, const float* scale, int64_t N,
                   int64_t K, cudaStream_t stream, const PeerArgs* peer = nullptr) {
+    if (launch_mma<MODE>(st, out, x, q, scale, N, K, stream, peer)) return true;
     const int64_t slices = ceil_div(K / 16, kXsThreads);
     if (slices == 1) return launch_stage_t<1, 8, MODE>(st, out, x, q, scale, N, K, stream, peer);
     if (slices == 2) return launch_stage_t<2, 4, MODE>(st, out, x, q, scale, N, K, stream, peer);
