@@ -329,6 +329,9 @@ class Setup:
         path = self.pc.select_path(self.x[0].data_ptr(), self.q[0].data_ptr(), self.M, self.Nl, self.K)
         if path == self.pc.PATH_TENSOR_F16 and self.M <= 128 and self.K <= 65536:
             return "tensor_i8 (activations as two int8 digits)"
+        sms = self.torch.cuda.get_device_properties(self.x[0].device).multi_processor_count
+        if path == self.pc.PATH_SIMT_F32 and self.M == 1 and staged_mma(self.K, self.Nl, sms):
+            return "simt_f32 (staged rows, mma.sync s8)"
         return self.pc.PATH_NAMES[path]
 
 
@@ -563,13 +566,30 @@ def time_e2e(torch, setup, steps, warmup, dist_on):
     return ms, xb, yb
 
 
+def staged_mma(K, N, sms):
+    """Whether an M = 1 per-channel call runs the staged decode kernel with
+    mma.sync: K % 32 == 0, 32 <= K <= 8192, each SM's rows (at most 64)
+    within 115,648 bytes at a pitch of K + 16, and at most 20 MMAs per warp
+    (16-row groups x k-steps per warp)."""
+    if K % 32 or not 32 <= K <= 8192 or N < 1:
+        return False
+    rows = -(-N // min(sms, N))
+    per_warp = -(-(K // 32) // 16)
+    return rows <= 64 and rows * max(K + 16, 128) <= 115648 and -(-rows // 16) * per_warp <= 20
+
+
 def compute_dtype(path, M, K, grouped):
-    """Arithmetic of the path a workload takes. CUDA cores at M = 1 (per
-    channel): each thread's 16-column slice of x as 30-bit fixed point, int8
-    codes, exact dp2a int32 sums, then f32; other CUDA-core cases f32. Tensor
-    cores: per-channel int8 weights with M <= 128 (K <= 65536) run tcgen05
-    kind::i8 on activations held as 16-bit fixed point in two int8 digits,
-    everything else f16 x f16 with f32 accumulation."""
+    """Arithmetic of the path a workload takes. The staged M = 1 decode
+    (per channel, K % 32 == 0, K <= 8192, rows fitting): x as 30-bit fixed point per warp in
+    four signed base-256 digits, mma.sync s8 x s8 -> s32 column sums, exact
+    partials in f64. Other CUDA-core cases at M = 1: each thread's
+    16-column slice of x as 30-bit fixed point, int8 codes, exact dp2a int32
+    sums, then f32; otherwise f32. Tensor cores: per-channel int8 weights
+    with M <= 128 (K <= 65536) run tcgen05 kind::i8 on activations held as
+    16-bit fixed point in two int8 digits, everything else f16 x f16 with
+    f32 accumulation."""
+    if "mma.sync" in path:
+        return "s30 fixed-point as 4 s8 digits x s8 (mma.sync) -> s32/f64"
     if "tensor" not in path:
         if M == 1 and not grouped:
             return "s30 fixed-point x s8 (dp2a) -> s32/f32"

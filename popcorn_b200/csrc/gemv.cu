@@ -24,12 +24,13 @@
 //    the stream, so under programmatic dependent launch the next call's
 //    weight stream overlaps this call; same arithmetic and bits as
 //    gemv_xs_kernel. Also behind the fused all-gather / all-reduce.
-//  * gemv_mma_kernel -- the staged decode for K = 1024, 2048, 4096 with the
-//    dot products on the warp-level tensor path (mma.sync m16n8k32, s8 x s8
-//    -> s32): activations as four signed base-256 digits of a 30-bit fixed
-//    point value per warp, exact integer column sums, partials combined in
-//    double and rounded once. Takes the place of gemv_stage_kernel (and
-//    behind the fused collectives) wherever its rows fit.
+//  * gemv_mma_kernel -- the staged decode for K % 32 == 0, K <= 8192, with
+//    the dot products on the warp-level tensor path (mma.sync m16n8k32,
+//    s8 x s8 -> s32): activations as four signed base-256 digits of a
+//    30-bit fixed point value per warp, exact integer column sums, partials
+//    combined in double and rounded once. Takes the place of
+//    gemv_stage_kernel (and behind the fused collectives) wherever its rows
+//    fit and each warp has at most 20 MMAs.
 //  * gemv_kernel -- other aligned shapes (larger K or M): activations staged
 //    in shared memory with cp.async, weights streamed per warp.
 //  * generic_kernel -- any shape / alignment.
@@ -816,29 +817,32 @@ gemv_stage_kernel(float* __restrict__ out, const float* __restrict__ x, const in
 }
 
 // ---------------------------------------------------------- gemv_mma_kernel
-// The staged decode GEMV (M = 1, K = 1024, 2048 or 4096) with its dot
-// products on the tensor pipe: mma.sync m16n8k32, signed 8-bit A and B,
-// s32 accumulate. Staging is gemv_stage_kernel's (rows copied into shared
-// memory by 1-D bulk copies before griddepcontrol.wait, one CTA per SM with
-// room for the next call's), except that rows sit K + 16 bytes apart, so
-// the eight rows an ldmatrix phase reads fall in eight different 16-byte
-// bank groups.
+// The staged decode GEMV (M = 1, K % 32 == 0, K <= 8192) with its dot
+// products on the warp-level tensor path: mma.sync m16n8k32, signed 8-bit A
+// and B, s32 accumulate. Staging is gemv_stage_kernel's (rows copied into
+// shared memory by 1-D bulk copies before griddepcontrol.wait, two CTAs per
+// SM so the next call's rows stream in during this call), except that rows
+// sit K + 16 bytes apart: K % 32 == 0 makes the pitch an odd multiple of 16
+// bytes, so the eight rows an ldmatrix phase reads fall in eight different
+// 16-byte bank groups.
 //
-// Warp w owns the K-range [w K/16, (w + 1) K/16) and every row of the CTA.
-// Its activations become 32-bit fixed point X = rint(x 2^s) with one power
-// of two per warp (max |X| < 2^30), written as four signed bytes
-// X = sum_d d_d 256^d, d_d in [-128, 127] (the bytes of X + 0x80808080, each
-// xor 0x80). B column n < 4 of a 32-deep k-step holds digit n of the
-// step's 32 activations, columns 4..7 are zero; A is 16 weight rows x 32
-// codes from ldmatrix. The four int32 column sums of a row are exact
-// (|code * digit| < 2^14, at most 256 terms), so the warp's partial is the
-// exact integer sum_d 256^d D_d times 2^-s, formed in double. The partials of
-// the 16 warps are added in warp order in double and rounded once after the
-// channel scale: the result is the dot product of the codes with x rounded
-// to ~2^-30 of each warp's max |x|, correctly rounded -- closer to the exact
-// product than popcorn's f32 sum. A warp whose activations hold a non-finite
-// value or a max |x| outside [2^-90, 2^100] adds its K-range in f32 instead
-// (codes widened exactly), so NaN and infinities propagate as in popcorn's.
+// K splits into 32-wide k-steps; warp w owns the contiguous steps
+// [w S / 16, (w + 1) S / 16), S = K / 32, for every row of the CTA. Its activations become 32-bit fixed point
+// X = rint(x 2^s) with one power of two per warp (max |X| < 2^30), written
+// as four signed bytes X = sum_d d_d 256^d, d_d in [-128, 127] (the bytes of
+// X + 0x80808080, each xor 0x80). B column n < 4 of a k-step holds digit n
+// of the step's 32 activations, columns 4..7 are zero; A is 16 weight rows x
+// 32 codes from ldmatrix. The four int32 column sums of a row are exact
+// (|code * digit| <= 2^14, at most 16 x 32 terms per warp at K = 8192), so
+// the warp's partial is the exact integer sum_d 256^d D_d times 2^-s, formed
+// in double. The partials of the 16 warps are added in warp order in double
+// and rounded once after the channel scale: the result is the dot product of
+// the codes with x rounded to ~2^-30 of each warp's max |x|, correctly
+// rounded -- closer to the exact product than popcorn's f32 sum, and the
+// same bits however the rows are split over CTAs or ranks. A warp whose
+// activations hold a non-finite value or a max |x| outside [2^-90, 2^100]
+// adds its steps in f32 instead (codes widened exactly), so NaN and
+// infinities propagate as in popcorn's.
 constexpr int kMmaWarps = 16;
 constexpr int kMmaThreads = kMmaWarps * 32;
 // Staged bytes (rows x (K + 16)) of one CTA: two CTAs, each with 1 KB of
@@ -859,7 +863,104 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t (&a)[4], uint32_t saddr) {
                  : "r"(saddr));
 }
 
-template <int KS, int MODE>
+// Per-warp fixed-point scaling of the activations a warp owns.
+struct WarpScale {
+    bool fixed;  // false: non-finite or extreme values, use the f32 form
+    int s;       // X = rint(x 2^s)
+    float up;    // 2^s
+};
+
+// Lane (g, t) = (lane / 4, lane % 4) reads, for k-step c, the four
+// activations at 32 c + 4 t + 16 h, h = g / 4 (the first half of the step
+// for g < 4, the second above): KSMAX steps c = c0 + i, those at i >= cnt
+// masked out. The loads are unconditional (a step past the end reads step
+// steps - 1) so that all of them are in flight at once.
+template <int KSMAX, bool EVEN>
+__device__ __forceinline__ WarpScale warp_scale(const float* x, int steps, int c0, int cnt, int lane) {
+    const int g = lane >> 2;
+    const float4* xl = reinterpret_cast<const float4*>(x + 4 * (lane & 3) + 16 * (g >> 2));
+    uint32_t mb = 0;
+    #pragma unroll
+    for (int i = 0; i < KSMAX; ++i) {
+        const float4 v = __ldg(xl + 8 * (EVEN ? c0 + i : min(c0 + i, steps - 1)));
+        const uint32_t keep = (EVEN || i < cnt) ? 0x7FFFFFFFu : 0u;
+        mb = max(mb, max(max(__float_as_uint(v.x) & keep, __float_as_uint(v.y) & keep),
+                         max(__float_as_uint(v.z) & keep, __float_as_uint(v.w) & keep)));
+    }
+    mb = __reduce_max_sync(0xffffffffu, mb);
+    WarpScale ws;
+    ws.fixed = mb == 0u || (mb >= 0x12800000u && mb <= 0x71800000u);
+    // max |x| 2^s in [2^29, 2^30): s = 29 - exponent of max |x|.
+    ws.s = mb == 0u ? 0 : 29 - (static_cast<int>(mb >> 23) - 127);
+    ws.up = mb == 0u ? 1.0f : __int_as_float((ws.s + 127) << 23);
+    return ws;
+}
+
+// B fragment of k-step c: digit g % 4 of this lane's four activations in
+// b0 (first half of the step) and b1 (second half) for g < 4, zero above.
+__device__ __forceinline__ void b_fragment(const float* x, int c, float up, int lane, uint32_t& b0, uint32_t& b1) {
+    const int g = lane >> 2;
+    const float4 v = __ldg(reinterpret_cast<const float4*>(x + 32 * c + 4 * (lane & 3) + 16 * (g >> 2)));
+    const uint32_t sel = static_cast<uint32_t>((g & 3) | (((g & 3) + 4) << 4));
+    const uint32_t y0 = static_cast<uint32_t>(__float2int_rn(v.x * up)) + 0x80808080u;
+    const uint32_t y1 = static_cast<uint32_t>(__float2int_rn(v.y * up)) + 0x80808080u;
+    const uint32_t y2 = static_cast<uint32_t>(__float2int_rn(v.z * up)) + 0x80808080u;
+    const uint32_t y3 = static_cast<uint32_t>(__float2int_rn(v.w * up)) + 0x80808080u;
+    const uint32_t bw = __byte_perm(__byte_perm(y0, y1, sel), __byte_perm(y2, y3, sel), 0x5410) ^ 0x80808080u;
+    const uint32_t odd = __shfl_down_sync(0xffffffffu, bw, 16);  // digit g of the step's second half
+    b0 = g < 4 ? bw : 0u;
+    b1 = g < 4 ? odd : 0u;
+}
+
+// Column sums d0, d1 = digits 2t, 2t + 1 of row g (d2, d3: row g + 8), lanes
+// t = 0, 1 holding digits 0-1 and 2-3: lane t = 0 gets the exact partials
+// of rows g and g + 8 times 2^-s.
+__device__ __forceinline__ void combine_digits(const int (&d)[4], int s, double& lo_row, double& hi_row) {
+    const double down = __longlong_as_double(static_cast<long long>(1023 - s) << 52);
+    const double l0 = static_cast<double>(d[0]) + 256.0 * static_cast<double>(d[1]);
+    const double l8 = static_cast<double>(d[2]) + 256.0 * static_cast<double>(d[3]);
+    const double h0 = __shfl_down_sync(0xffffffffu, l0, 1);
+    const double h8 = __shfl_down_sync(0xffffffffu, l8, 1);
+    lo_row = (h0 * 65536.0 + l0) * down;
+    hi_row = (h8 * 65536.0 + l8) * down;
+}
+
+// f32 form of a warp's steps [c0, c1) for one row of codes (lane-strided,
+// butterfly).
+__device__ __forceinline__ float warp_row_f32(const float* x, const int8_t* codes, int c0, int c1, int lane) {
+    float a = 0.0f;
+    for (int c = c0; c < c1; ++c) a = fmaf(__ldg(x + 32 * c + lane), static_cast<float>(codes[32 * c + lane]), a);
+    #pragma unroll
+    for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+    return a;
+}
+
+// Channel-scaled result of row i (sum of the 16 warp partials in warp
+// order), stored to out or sent to the peers.
+template <int MODE>
+__device__ __forceinline__ void finish_row(float* out, const PeerArgs& pa, int64_t N, int64_t row, double sum,
+                                           float sc, unsigned int e) {
+    const float val = static_cast<float>(sum * static_cast<double>(sc));
+    if constexpr (MODE == kPeerGather) {
+        const int64_t idx = pa.n_offset + row;
+        out[idx] = val;
+        const int64_t slot = (e & 1u) * pa.half_words + idx;
+        for (int p = 0; p < pa.world; ++p) {
+            if (p != pa.rank) st_relaxed_sys_u64(pa.recv[p] + slot, tagged(e, val));
+        }
+    } else if constexpr (MODE == kPeerReduce) {
+        const int64_t slot = (e & 1u) * pa.half_words + pa.rank * N + row;
+        for (int p = 0; p < pa.world; ++p) st_relaxed_sys_u64(pa.recv[p] + slot, tagged(e, val));
+    } else {
+        out[row] = val;
+    }
+}
+
+// KSMAX: most k-steps of one warp (K / 32 / 16, rounded up), EVEN: every
+// warp has exactly KSMAX (K = 512 KSMAX); GROUPS: most
+// 16-row groups of a CTA; SETS: accumulators per group that consecutive
+// steps alternate between, so no chain of dependent MMAs is long.
+template <int KSMAX, bool EVEN, int GROUPS, int SETS, int MODE>
 __global__ void __launch_bounds__(kMmaThreads, 2)
 gemv_mma_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_t* __restrict__ q,
                 const float* __restrict__ scale, int64_t N, int64_t K, const PeerArgs pa) {
@@ -873,6 +974,7 @@ gemv_mma_kernel(float* __restrict__ out, const float* __restrict__ x, const int8
     const int rows = static_cast<int>(N * (blockIdx.x + 1) / G - r0);
     const int k32 = static_cast<int>(K);
     const int pitch = k32 + 16;
+    const int steps = k32 >> 5;
     const uint32_t full = sm100::smem_addr(&s_full);
     const uint32_t base = sm100::smem_addr(stage);
 
@@ -894,122 +996,79 @@ gemv_mma_kernel(float* __restrict__ out, const float* __restrict__ x, const int8
     if constexpr (MODE != kPeerNone) {
         if (threadIdx.x == 0) s_e = *reinterpret_cast<volatile unsigned int*>(pa.state) + 1u;
     }
-
-    // This warp's K-range and its activations: lane (g, t) = (lane / 4,
-    // lane % 4) reads, for k-step c, the four values at 32 c + 4 t + 16 h,
-    // h = g / 4 (the even-k half of the step for g < 4, the odd half above).
-    const int kw = warp * (k32 / kMmaWarps);
-    const int g = lane >> 2;
-    const int t = lane & 3;
-    const int h = g >> 2;
-    const float4* xw = reinterpret_cast<const float4*>(x + kw + 4 * t + 16 * h);
-    uint32_t mb = 0;
-    #pragma unroll
-    for (int c = 0; c < KS; ++c) {
-        const float4 v = __ldg(xw + 8 * c);
-        mb = max(mb, max(max(__float_as_uint(v.x) & 0x7FFFFFFFu, __float_as_uint(v.y) & 0x7FFFFFFFu),
-                         max(__float_as_uint(v.z) & 0x7FFFFFFFu, __float_as_uint(v.w) & 0x7FFFFFFFu)));
-    }
-    mb = __reduce_max_sync(0xffffffffu, mb);
-    const bool fixed = mb == 0u || (mb >= 0x12800000u && mb <= 0x71800000u);
-    // max |x| * 2^s in [2^29, 2^30): s = 29 - exponent of max |x|.
-    const int s_exp = mb == 0u ? 0 : 29 - (static_cast<int>(mb >> 23) - 127);
-    const float up = mb == 0u ? 1.0f : __int_as_float((s_exp + 127) << 23);
+    const int c0 = EVEN ? warp * KSMAX : warp * steps / kMmaWarps;
+    const int c1 = EVEN ? c0 + KSMAX : (warp + 1) * steps / kMmaWarps;
+    const WarpScale ws = warp_scale<KSMAX, EVEN>(x, steps, c0, c1 - c0, lane);
 
     if (!sm100::mbar_wait(full, 0, &g_gemv_error, kStageTimeoutBit)) {
         sm100::mbar_wait(full, 0, &g_gemv_error, kStageTimeoutBit);
     }
 
-    // Partial sums of this warp for every row, into registers: row-group j
-    // (16 rows), lane (g, t) ends up with rows 16 j + g and 16 j + g + 8.
-    // K = 4096 holds at most 28 rows (two groups); K-steps alternate between
-    // kSets accumulators so no chain of dependent mma is longer than two.
-    constexpr int kMaxGroups = KS == 8 ? 2 : 4;
-    constexpr int kSets = KS == 8 ? 4 : 2;
+    // This warp's partials, lane (g, t = 0) holding rows 16 j + g and 16 j + g + 8.
+    const int g = lane >> 2;
     const int groups = (rows + 15) >> 4;
-    double part_lo[kMaxGroups], part_hi[kMaxGroups];  // rows 16 j + g, 16 j + g + 8
-    if (fixed) {
-        int d[kMaxGroups][kSets][4];
+    double part_lo[GROUPS], part_hi[GROUPS];
+    if (ws.fixed) {
+        int d[GROUPS][SETS][4];
         #pragma unroll
-        for (int j = 0; j < kMaxGroups; ++j) {
+        for (int j = 0; j < GROUPS; ++j) {
             #pragma unroll
-            for (int e2 = 0; e2 < kSets; ++e2) d[j][e2][0] = d[j][e2][1] = d[j][e2][2] = d[j][e2][3] = 0;
+            for (int e2 = 0; e2 < SETS; ++e2) d[j][e2][0] = d[j][e2][1] = d[j][e2][2] = d[j][e2][3] = 0;
         }
-        // ldmatrix row addresses of this lane: matrix i = lane / 8 (rows + 8 (i & 1),
-        // k + 16 (i >> 1)), row lane % 8 of it.
+        // ldmatrix row addresses of this lane: matrix i = lane / 8 covers rows
+        // + 8 (i & 1), codes + 16 (i >> 1); row lane % 8 of it.
         const int mi = lane >> 3;
         const int mrow = (lane & 7) + 8 * (mi & 1);
         const int mk = 16 * (mi >> 1);
-        const uint32_t sel = static_cast<uint32_t>((g & 3) | (((g & 3) + 4) << 4));
+        // Branch-free over the KSMAX steps: a step past the end multiplies
+        // the codes of step steps - 1 by zero digits.
         #pragma unroll
-        for (int c = 0; c < KS; ++c) {
-            // B fragment of k-step c: digit g of the four activations of this lane.
-            const float4 v = __ldg(xw + 8 * c);
-            const uint32_t y0 = static_cast<uint32_t>(__float2int_rn(v.x * up)) + 0x80808080u;
-            const uint32_t y1 = static_cast<uint32_t>(__float2int_rn(v.y * up)) + 0x80808080u;
-            const uint32_t y2 = static_cast<uint32_t>(__float2int_rn(v.z * up)) + 0x80808080u;
-            const uint32_t y3 = static_cast<uint32_t>(__float2int_rn(v.w * up)) + 0x80808080u;
-            const uint32_t t01 = __byte_perm(y0, y1, sel);
-            const uint32_t t23 = __byte_perm(y2, y3, sel);
-            const uint32_t bw = __byte_perm(t01, t23, 0x5410) ^ 0x80808080u;
-            const uint32_t odd = __shfl_down_sync(0xffffffffu, bw, 16);  // digit g of the step's odd half
-            const uint32_t b0 = g < 4 ? bw : 0u;
-            const uint32_t b1 = g < 4 ? odd : 0u;
-            const int k0 = kw + 32 * c + mk;
+        for (int i = 0; i < KSMAX; ++i) {
+            const int cc = EVEN ? c0 + i : min(c0 + i, steps - 1);
+            uint32_t b0, b1;
+            b_fragment(x, cc, ws.up, lane, b0, b1);
+            if (!EVEN && c0 + i >= c1) b0 = b1 = 0u;
             #pragma unroll
-            for (int j = 0; j < kMaxGroups; ++j) {
+            for (int j = 0; j < GROUPS; ++j) {
                 if (j < groups) {
                     int r = 16 * j + mrow;
                     r = r < rows ? r : rows - 1;  // past the last row: read it again, never stored
                     uint32_t a[4];
-                    ldmatrix_x4(a, base + r * pitch + k0);
-                    mma_s8_16832(d[j][c % kSets], a, b0, b1);
+                    ldmatrix_x4(a, base + r * pitch + 32 * cc + mk);
+                    mma_s8_16832(d[j][i % SETS], a, b0, b1);
                 }
             }
         }
-        // Column sums d0 = digit 2t, d1 = digit 2t + 1 of row g (d2, d3: row g + 8);
-        // lanes t = 0, 1 hold digits 0-1 and 2-3.
-        const double down = __longlong_as_double(static_cast<long long>(1023 - s_exp) << 52);
         #pragma unroll
-        for (int j = 0; j < kMaxGroups; ++j) {
+        for (int j = 0; j < GROUPS; ++j) {
             #pragma unroll
-            for (int e2 = 1; e2 < kSets; ++e2) {  // exact: |column sum| < 2^22
+            for (int e2 = 1; e2 < SETS; ++e2) {  // exact: |column sum| < 2^23
                 #pragma unroll
                 for (int v = 0; v < 4; ++v) d[j][0][v] += d[j][e2][v];
             }
-            const double lo0 = static_cast<double>(d[j][0][0]) + 256.0 * static_cast<double>(d[j][0][1]);
-            const double lo8 = static_cast<double>(d[j][0][2]) + 256.0 * static_cast<double>(d[j][0][3]);
-            const double hi0 = __shfl_down_sync(0xffffffffu, lo0, 1);
-            const double hi8 = __shfl_down_sync(0xffffffffu, lo8, 1);
-            part_lo[j] = (hi0 * 65536.0 + lo0) * down;
-            part_hi[j] = (hi8 * 65536.0 + lo8) * down;
+            combine_digits(d[j][0], ws.s, part_lo[j], part_hi[j]);
         }
     } else {
-        // f32 form of this warp's K-range (rare: non-finite or extreme x);
-        // lane r % 32 keeps row r's sum.
+        // f32 form (rare); lane r % 32 keeps row r's sum.
         float fb0 = 0.0f, fb1 = 0.0f;
         for (int r = 0; r < rows; ++r) {
-            const int8_t* qr = reinterpret_cast<const int8_t*>(stage + r * pitch + kw);
-            float a = 0.0f;
-            for (int k = lane; k < k32 / kMmaWarps; k += 32) a = fmaf(__ldg(x + kw + k), static_cast<float>(qr[k]), a);
-            #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+            const float a = warp_row_f32(x, reinterpret_cast<const int8_t*>(stage + r * pitch), c0, c1, lane);
             if (lane == (r & 31)) {
                 if (r < 32) fb0 = a;
                 else fb1 = a;
             }
         }
         #pragma unroll
-        for (int j = 0; j < kMaxGroups; ++j) part_lo[j] = part_hi[j] = 0.0;
+        for (int j = 0; j < GROUPS; ++j) part_lo[j] = part_hi[j] = 0.0;
         part_lo[0] = static_cast<double>(fb0);
         part_hi[0] = static_cast<double>(fb1);
     }
     __syncthreads();  // every read of the staged rows is done: reuse them as [16][rows] doubles
     double* part = reinterpret_cast<double*>(stage);
-    if (fixed) {
-        if (t == 0) {
+    if (ws.fixed) {
+        if ((lane & 3) == 0) {
             #pragma unroll
-            for (int j = 0; j < kMaxGroups; ++j) {
+            for (int j = 0; j < GROUPS; ++j) {
                 if (16 * j + g < rows) part[warp * rows + 16 * j + g] = part_lo[j];
                 if (16 * j + g + 8 < rows) part[warp * rows + 16 * j + g + 8] = part_hi[j];
             }
@@ -1026,20 +1085,7 @@ gemv_mma_kernel(float* __restrict__ out, const float* __restrict__ x, const int8
         double sum = 0.0;
         #pragma unroll
         for (int w = 0; w < kMmaWarps; ++w) sum += part[w * rows + i];
-        const float val = static_cast<float>(sum * static_cast<double>(sc_row));
-        if constexpr (MODE == kPeerGather) {
-            const int64_t idx = pa.n_offset + r0 + i;
-            out[idx] = val;
-            const int64_t slot = (e & 1u) * pa.half_words + idx;
-            for (int p = 0; p < pa.world; ++p) {
-                if (p != pa.rank) st_relaxed_sys_u64(pa.recv[p] + slot, tagged(e, val));
-            }
-        } else if constexpr (MODE == kPeerReduce) {
-            const int64_t slot = (e & 1u) * pa.half_words + pa.rank * N + r0 + i;
-            for (int p = 0; p < pa.world; ++p) st_relaxed_sys_u64(pa.recv[p] + slot, tagged(e, val));
-        } else {
-            out[r0 + i] = val;
-        }
+        finish_row<MODE>(out, pa, N, r0 + i, sum, sc_row, e);
     }
     if constexpr (MODE != kPeerNone) {
         __syncthreads();
@@ -1220,40 +1266,87 @@ bool launch_stage_t(popcornStatus_t* st, float* out, const float* x, const int8_
     return true;
 }
 
-// Staged decode GEMV on the tensor pipe: K in {1024, 2048, 4096} and every
-// CTA's rows within kMmaStageBytes (and kStageMaxRows); returns false
-// (nothing launched) otherwise.
-template <int MODE>
-bool launch_mma(popcornStatus_t* st, float* out, const float* x, const int8_t* q, const float* scale, int64_t N,
-                int64_t K, cudaStream_t stream, const PeerArgs* peer) {
-    if (K != 1024 && K != 2048 && K != 4096) return false;
-    const int64_t G = device_sm_count() < N ? device_sm_count() : N;
-    const int64_t rows = ceil_div(N, G);
-    if (rows > kStageMaxRows || rows * (K + 16) > kMmaStageBytes) return false;
-    auto kern = K == 4096 ? gemv_mma_kernel<8, MODE> : (K == 2048 ? gemv_mma_kernel<4, MODE> : gemv_mma_kernel<2, MODE>);
-    static bool attr_set[kMaxDevices][3] = {};
-    const int ki = K == 4096 ? 2 : (K == 2048 ? 1 : 0);
+template <int KSMAX, bool EVEN, int GROUPS, int SETS, int MODE>
+popcornStatus_t launch_mma_t(float* out, const float* x, const int8_t* q, const float* scale, int64_t N, int64_t K,
+                             int64_t G, int64_t smem, cudaStream_t stream, const PeerArgs* peer) {
+    auto kern = gemv_mma_kernel<KSMAX, EVEN, GROUPS, SETS, MODE>;
+    static bool attr_set[kMaxDevices] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     const bool cached = dev >= 0 && dev < kMaxDevices;
-    if (!cached || !attr_set[dev][ki]) {
+    if (!cached || !attr_set[dev]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMmaStageBytes);
         if (e == cudaSuccess) {
             e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                                      cudaSharedmemCarveoutMaxShared);
         }
-        if (e != cudaSuccess) {
-            *st = record_cuda(e);
-            return true;
-        }
-        if (cached) attr_set[dev][ki] = true;
+        if (e != cudaSuccess) return record_cuda(e);
+        if (cached) attr_set[dev] = true;
     }
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pdl_config(dim3(static_cast<unsigned>(G)), dim3(kMmaThreads),
-                                        static_cast<size_t>(rows * (K + 16)), stream, attr);
+                                        static_cast<size_t>(smem), stream, attr);
     const PeerArgs none = {};
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, out, x, q, scale, N, K, peer != nullptr ? *peer : none);
-    *st = (e != cudaSuccess) ? record_cuda(e) : check_launch();
+    return (e != cudaSuccess) ? record_cuda(e) : check_launch();
+}
+
+// Staged decode GEMV on the tensor pipe: K % 32 == 0, K <= 8192, and every
+// CTA's rows (at most kStageMaxRows) within kMmaStageBytes at a pitch of
+// K + 16; returns false (nothing launched) otherwise.
+template <int MODE>
+bool launch_mma(popcornStatus_t* st, float* out, const float* x, const int8_t* q, const float* scale, int64_t N,
+                int64_t K, cudaStream_t stream, const PeerArgs* peer) {
+    if (K < 32 || K > 8192 || K % 32 != 0) return false;
+    const int64_t G = device_sm_count() < N ? device_sm_count() : N;
+    const int64_t rows = ceil_div(N, G);
+    // The staged rows, later reused for 16 doubles per row.
+    const int64_t smem = rows * (K + 16 > 128 ? K + 16 : 128);
+    if (rows > kStageMaxRows || smem > kMmaStageBytes) return false;
+    const int64_t per_warp = ceil_div(K / 32, kMmaWarps);  // k-steps of one warp
+    // Past ~20 MMAs per warp (16-row groups x k-steps) the legacy tensor
+    // path's issue time outweighs what it saves: K = 3072 at 56 rows per CTA
+    // took 9.8 us against 8.0 us on the CUDA-core kernels.
+    if (ceil_div(rows, 16) * per_warp > 20) return false;
+    // K a multiple of 512: every warp has the same steps (per_warp).
+    const bool even = (K / 32) % kMmaWarps == 0;
+    const bool wide = rows > 32;  // more than two 16-row groups
+    popcornStatus_t r = POPCORN_SUCCESS;
+#define PCB_MMA(KS, EV, GR, SE) r = launch_mma_t<KS, EV, GR, SE, MODE>(out, x, q, scale, N, K, G, smem, stream, peer)
+    if (even && per_warp <= 4) {
+        switch (per_warp) {
+            case 1: PCB_MMA(1, true, 4, 1); break;
+            case 2: PCB_MMA(2, true, 4, 2); break;
+            case 3: PCB_MMA(3, true, 4, 2); break;
+            default: PCB_MMA(4, true, 4, 2); break;
+        }
+    } else if (even && per_warp <= 6 && wide) {  // K = 2560, 3072: up to 44 rows
+        if (per_warp == 5) PCB_MMA(5, true, 4, 2);
+        else PCB_MMA(6, true, 4, 2);
+    } else if (even && (per_warp <= 8 || per_warp % 2 == 0)) {  // at most 32 rows from here on
+        switch (per_warp) {
+            case 5: PCB_MMA(5, true, 2, 4); break;
+            case 6: PCB_MMA(6, true, 2, 4); break;
+            case 7: PCB_MMA(7, true, 2, 4); break;
+            case 8: PCB_MMA(8, true, 2, 4); break;
+            case 10: PCB_MMA(10, true, 2, 4); break;
+            case 12: PCB_MMA(12, true, 2, 4); break;
+            case 14: PCB_MMA(14, true, 2, 4); break;
+            default: PCB_MMA(16, true, 2, 4); break;
+        }
+    } else if (per_warp <= 2) {
+        PCB_MMA(2, false, 4, 2);
+    } else if (per_warp <= 4) {
+        PCB_MMA(4, false, 4, 2);
+    } else if (per_warp <= 8 && wide) {
+        PCB_MMA(8, false, 4, 2);
+    } else if (per_warp <= 8) {
+        PCB_MMA(8, false, 2, 4);
+    } else {
+        PCB_MMA(16, false, 2, 4);  // K > 4096: at most 27 rows
+    }
+#undef PCB_MMA
+    *st = r;
     return true;
 }
 

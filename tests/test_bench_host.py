@@ -69,6 +69,11 @@ def test_traffic_figures_name_existing_profiles():
 def test_compute_dtype_routes():
     # M = 1 per channel: fixed-point activations times int8 codes on dp2a.
     assert bench.compute_dtype("simt_f32", 1, 4096, False) == "s30 fixed-point x s8 (dp2a) -> s32/f32"
+    assert bench.compute_dtype("simt_f32 (staged rows, mma.sync s8)", 1, 4096, False).endswith("(mma.sync) -> s32/f64")
+    assert bench.staged_mma(4096, 4096, 148) and bench.staged_mma(1024, 8192, 148)
+    assert not bench.staged_mma(4096, 4500, 148)  # 31 rows x 4112 B > 115,648 B
+    assert not bench.staged_mma(11008, 4096, 148) and not bench.staged_mma(4096, 12288, 148)
+    assert not bench.staged_mma(3072, 8192, 148)  # 4 row groups x 6 k-steps > 20 MMAs per warp
     assert bench.compute_dtype("simt_f32", 2, 4096, False) == "f32"
     assert bench.compute_dtype("simt_f32", 1, 4096, True) == "f32"
     assert bench.compute_dtype("tensor_f16", 32, 4096, False).startswith("s8")

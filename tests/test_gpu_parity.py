@@ -655,6 +655,33 @@ def test_tensor_path_skinny_full_size(cuda):
     assert err <= TOL_TENSOR, err
 
 
+@pytest.mark.parametrize("N,K", [
+    (1000, 288),    # 9 k-steps: warps 9..15 own none
+    (5000, 544),    # 34 rows per CTA, 17 k-steps
+    (4096, 1376),   # down projection slice of an 8-way split
+    (4096, 2752),   # ... of a 4-way split
+    (3000, 5120),   # 10 or 11 k-steps per warp
+    (2000, 8192),   # the largest staged K, 14 rows per CTA
+    (8192, 2048),   # 56 rows per CTA in four row groups
+    (8000, 2080),   # 65 k-steps (uneven warps), 55 rows per CTA
+    (3000, 1536),   # 3 k-steps per warp
+])
+def test_staged_decode_any_k_and_row_split(cuda, N, K):
+    # The staged M = 1 kernel (K % 32 == 0, rows within shared memory): the
+    # oracle's result within the f32 tolerance, and each row's bits
+    # independent of how many rows share a CTA (a sub-range of rows as its
+    # own call returns the same values).
+    import torch
+
+    x, q, s = random_case(1, N, K, 91 + K)
+    got = abi_matmul(torch, cuda, x, q, s)
+    assert pc.device_errors() == 0
+    assert oracle.normwise_rel_err(got, oracle.dequant_matmul(x, q, s, fused=True, threads=8)) <= TOL_F32
+    lo, n2 = 37, 151
+    sub = abi_matmul(torch, cuda, x, np.ascontiguousarray(q[lo:lo + n2]), np.ascontiguousarray(s[lo:lo + n2]))
+    assert np.array_equal(sub.view(np.uint32), got[:, lo:lo + n2].view(np.uint32))
+
+
 def test_decode_full_size_vs_oracle(cuda):
     import torch
 
