@@ -325,6 +325,9 @@ class Setup:
     def path(self):
         if self.gs:
             fmt = "int4" if self.bits == 4 else "grouped"
+            sms = self.torch.cuda.get_device_properties(self.x[0].device).multi_processor_count
+            if self.bits != 4 and self.M == 1 and staged_mma_grouped(self.K, self.Nl, self.gs, sms):
+                return f"grouped_f32 (group {self.gs}, staged rows, mma.sync s8)"
             return f"{fmt}_{'tensor_f16' if self.grouped_tensor() else 'f32'} (group {self.gs})"
         path = self.pc.select_path(self.x[0].data_ptr(), self.q[0].data_ptr(), self.M, self.Nl, self.K)
         if path == self.pc.PATH_TENSOR_F16 and self.M <= 128 and self.K <= 65536:
@@ -576,6 +579,24 @@ def staged_mma(K, N, sms):
     rows = -(-N // min(sms, N))
     per_warp = -(-(K // 32) // 16)
     return rows <= 64 and rows * max(K + 16, 128) <= 115648 and -(-rows // 16) * per_warp <= 20
+
+
+def staged_mma_grouped(K, N, gs, sms):
+    """Whether an M = 1 per-group int8 call runs the staged mma.sync decode:
+    K of 1024, 2048 or 4096, group_size % 32 == 0 with a warp's K / 16
+    columns holding whole groups or lying in one (at K = 4096 groups of at
+    least 128; at K = 2048 at least 64), each SM's rows (at most 64) within
+    115,648 bytes at a pitch of K + 16, and at most 20 MMAs per warp."""
+    if K not in (1024, 2048, 4096) or gs % 32 or N < 1:
+        return False
+    span = K // 16
+    if span % gs and gs % span:
+        return False
+    gsteps = K // 512 if gs >= span else gs // 32
+    if (K == 4096 and gsteps < 4) or (K == 2048 and gsteps < 2):
+        return False
+    rows = -(-N // min(sms, N))
+    return rows <= 64 and rows * (K + 16) <= 115648 and -(-rows // 16) * (K // 512) <= 20
 
 
 def compute_dtype(path, M, K, grouped):

@@ -145,7 +145,7 @@ popcornStatus_t popcornDequantizeMatmulNoAlloc_i8f32(
  * (pipeline barriers). Bits 16-31, shifted by 16: 0x100 a fused collective
  * waited for another rank's values, 0x200 a decode kernel waited for the
  * weight rows it staged in shared memory, 0x400 the int4 decode kernel
- * likewise. */
+ * likewise, 0x1000 the per-group int8 decode kernel likewise. */
 int popcornB200DeviceErrors(unsigned int* flags);
 
 /*

@@ -142,6 +142,7 @@ popcornStatus_t peer_dequant_matmul(PeerMode mode, const PeerArgs& pa, float* ou
 cudaError_t tc_take_errors(unsigned int* bits);
 cudaError_t gemv_take_errors(unsigned int* bits);
 cudaError_t i4_take_errors(unsigned int* bits);
+cudaError_t grouped_take_errors(unsigned int* bits);
 
 }  // namespace pcb
 

@@ -99,10 +99,11 @@ extern "C" int popcornDequantizeMatmulLaunchCount(const float* x, const int8_t* 
 
 extern "C" int popcornB200DeviceErrors(unsigned int* flags) {
     if (flags == nullptr) return POPCORN_ERROR_INVALID_VALUE;
-    unsigned int a = 0, b = 0, c = 0;
+    unsigned int a = 0, b = 0, c = 0, d = 0;
     cudaError_t e = pcb::tc_take_errors(&a);
     if (e == cudaSuccess) e = pcb::gemv_take_errors(&b);
     if (e == cudaSuccess) e = pcb::i4_take_errors(&c);
-    *flags = a | ((b | c) << 16);
+    if (e == cudaSuccess) e = pcb::grouped_take_errors(&d);
+    *flags = a | ((b | c | d) << 16);
     return pcb::record_cuda(e);
 }

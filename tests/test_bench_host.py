@@ -74,6 +74,10 @@ def test_compute_dtype_routes():
     assert not bench.staged_mma(4096, 4500, 148)  # 31 rows x 4112 B > 115,648 B
     assert not bench.staged_mma(11008, 4096, 148) and not bench.staged_mma(4096, 12288, 148)
     assert not bench.staged_mma(3072, 8192, 148)  # 4 row groups x 6 k-steps > 20 MMAs per warp
+    assert bench.staged_mma_grouped(4096, 4096, 128, 148) and bench.staged_mma_grouped(1024, 8192, 32, 148)
+    assert not bench.staged_mma_grouped(4096, 4096, 64, 148)  # four scale flushes per warp: slower
+    assert not bench.staged_mma_grouped(2048, 6000, 32, 148)  # 32 scales per lane
+    assert bench.compute_dtype("grouped_f32 (group 128, staged rows, mma.sync s8)", 1, 4096, True).endswith("f64")
     assert bench.compute_dtype("simt_f32", 2, 4096, False) == "f32"
     assert bench.compute_dtype("simt_f32", 1, 4096, True) == "f32"
     assert bench.compute_dtype("tensor_f16", 32, 4096, False).startswith("s8")

@@ -101,6 +101,33 @@ def test_random_shapes_match_oracle(cuda, shape):
     assert oracle.normwise_rel_err(got, ref) <= TOL_F32
 
 
+@pytest.mark.parametrize("N,K,gs", [
+    (4096, 4096, 128), (4000, 4096, 256), (2000, 4096, 1024),
+    (8192, 1024, 32), (8192, 1024, 64), (6000, 2048, 64), (6000, 2048, 128), (3000, 2048, 2048),
+])
+def test_staged_decode_vs_oracle_and_row_split(cuda, N, K, gs):
+    # The staged M = 1 kernel (tensor path, group scales applied to exact
+    # per-group sums): the oracle within the f32 tolerance, each row's bits
+    # independent of how rows share a CTA, and popcorn's per-element form in
+    # warps holding a non-finite or extreme activation.
+    import torch
+
+    x, q, s = _case(1, N, K, gs, N + K + gs)
+    got = _grouped(torch, cuda, x, q, s, gs)
+    ref = oracle.dequant_matmul_grouped(x, q, s, gs, fused=True, threads=8)
+    assert oracle.normwise_rel_err(got, ref) <= TOL_F32
+    lo, n2 = 29, (1 << 22) // K + 51  # above the sequential kernel's 2^22 multiply-adds
+    sub = _grouped(torch, cuda, x, np.ascontiguousarray(q[lo:lo + n2]), np.ascontiguousarray(s[lo:lo + n2]), gs)
+    assert np.array_equal(sub.view(np.uint32), got[:, lo:lo + n2].view(np.uint32))
+    xi = x.copy()
+    xi[0, 5] = np.inf
+    xi[0, K // 2:K // 2 + 64] *= 2.0 ** -120
+    got = _grouped(torch, cuda, xi, q, s, gs)
+    want = oracle.dequant_matmul_grouped(xi, q, s, gs, fused=True, threads=8)
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    assert np.array_equal(got[np.isinf(want)], want[np.isinf(want)])
+
+
 def test_unaligned_activations_take_the_exact_path(cuda):
     import torch
 
