@@ -314,7 +314,8 @@ class LinearStack:
     """The linear layers of a decoder stack, tensor-parallel over `group`.
 
     Per layer: h -> qkv (column-parallel) -> o (row-parallel, all-reduce) ->
-    gate and up (column-parallel) -> down (row-parallel, all-reduce) -> h.
+    gate and up (column-parallel; at M <= 4 one call over the rank's gate
+    rows stacked on its up rows) -> down (row-parallel, all-reduce) -> h.
     Attention and the SiLU(gate) * up product lie outside the dequant-matmul
     path; in their place the o projection reads the first columns of the
     rank's qkv output and the down projection reads the rank's gate output,
@@ -329,6 +330,12 @@ class LinearStack:
     NCCL all-reduce. All buffers are allocated here, so a pass can be captured
     in a CUDA graph. ``local_matmul`` (x, q, s) -> y replaces the library call
     (for host-side tests on CPU ranks, with torch.distributed all-reduce).
+
+    Each layer dict gains a "gate_up" entry (the rank's gate and up shards
+    concatenated by rows) and its "gate" and "up" entries become views of
+    it, so at decode sizes the two projections stream as one matrix in one
+    launch (at M = 128 two launches measured faster: 3.33 against 3.40 ms
+    per pass, the merged 22016-row GEMM taking a second wave of CTA pairs).
     """
 
     def __init__(self, layers: list, M: int, dims: dict, device, group: Optional[dist.ProcessGroup] = None,
@@ -348,14 +355,26 @@ class LinearStack:
         self.peer = peer if (peer is not None and fusable) else None
         n_qkv = layers[0]["qkv"][0].shape[0]
         n_ffn = layers[0]["gate"][0].shape[0]
+        for w in layers:
+            if "gate_up" not in w:
+                qg, sg = w["gate"]
+                qu, su = w["up"]
+                q = torch.cat([qg, qu])
+                sc = torch.cat([sg, su])
+                w["gate_up"] = (q, sc)
+                w["gate"] = (q[:n_ffn], sc[:n_ffn])
+                w["up"] = (q[n_ffn:], sc[n_ffn:])
         if n_qkv < self.k_o:
             raise ValueError("qkv shard narrower than the o projection's input slice")
         f32 = torch.float32
         self.a = torch.empty((M, n_qkv), dtype=f32, device=device)
         self.xo = torch.empty((M, self.k_o), dtype=f32, device=device)
         self.h1 = torch.empty((M, h), dtype=f32, device=device)
+        self.n_ffn = n_ffn
+        self.merged = M <= 4
+        self.gu = torch.empty((M, 2 * n_ffn), dtype=f32, device=device) if self.merged else None
         self.g = torch.empty((M, n_ffn), dtype=f32, device=device)
-        self.u = torch.empty((M, n_ffn), dtype=f32, device=device)
+        self.u = None if self.merged else torch.empty((M, n_ffn), dtype=f32, device=device)
         self.h2 = torch.empty((M, h), dtype=f32, device=device)
         self._lib = None if local_matmul is not None else load_library()
 
@@ -390,9 +409,18 @@ class LinearStack:
                 self.xo.copy_(self.a[:, : self.k_o])
                 xo = self.xo
             self._row(self.h1, xo, *w["o"])
-            self._mm(self.g, self.h1, *w["gate"])
-            self._mm(self.u, self.h1, *w["up"])
-            self._row(self.h2, self.g, *w["down"])
+            if self.merged:
+                self._mm(self.gu, self.h1, *w["gate_up"])
+                if self.M == 1:
+                    g = self.gu[:, : self.n_ffn]           # contiguous for a single row
+                else:
+                    self.g.copy_(self.gu[:, : self.n_ffn])
+                    g = self.g
+            else:
+                self._mm(self.g, self.h1, *w["gate"])
+                self._mm(self.u, self.h1, *w["up"])
+                g = self.g
+            self._row(self.h2, g, *w["down"])
             h = self.h2
         return h
 
@@ -400,7 +428,7 @@ class LinearStack:
 
     def weight_bytes(self) -> int:
         """int8 weight bytes this rank streams per pass."""
-        return sum(q.numel() for w in self.layers for (q, _) in w.values())
+        return sum(w[part][0].numel() for w in self.layers for part in STACK_PARTS)
 
     def launches_per_pass(self) -> int:
         """Library kernel launches per pass (NCCL and copies not counted)."""
@@ -408,8 +436,9 @@ class LinearStack:
             return 0
         n = 0
         M = self.M
+        parts = ("qkv", "o", "gate_up", "down") if self.merged else STACK_PARTS
         for w in self.layers:
-            for part in STACK_PARTS:
+            for part in parts:
                 q = w[part][0]
                 n += self._lib.popcornDequantizeMatmulLaunchCount(0x10000, q.data_ptr(), M, q.shape[0],
                                                                   q.shape[1], 0)

@@ -141,7 +141,7 @@ def _stack_worker(rank, world, port, M, layers, ret):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("M", [1, 3])
+@pytest.mark.parametrize("M", [1, 3, 6])
 def test_linear_stack_gloo_world2(M):
     world, layers = 2, 2
     ctx = mp.get_context("spawn")
