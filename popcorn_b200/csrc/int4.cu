@@ -21,6 +21,10 @@
 //    codes become floats without a conversion instruction: a nibble placed in
 //    the low mantissa bits of 2^23 reads as 2^23 + c; the high nibble is taken
 //    in place (2^23 + 16 c) and its activation pre-scaled by 1/16, exactly.
+//  * i4_mma_kernel -- decode (M = 1, K = 1024 or 2048, group size a
+//    multiple of 64): staged rows, codes unpacked to bytes and summed against
+//    fixed-point digits of x with mma.sync (u8 x s8), the zero point applied
+//    through the exact group sum of x.
 //  * i4_quantize_kernel -- one warp per (row, group): min and max by shuffles,
 //    ties between +0 and -0 broken the way popcorn's 256-thread block breaks
 //    them, then (even group sizes) the packed codes of the group;
@@ -28,6 +32,7 @@
 //    from the stored parameters. Codes, scales and zero points are
 //    bit-identical to popcorn's kernels; no temporary buffer.
 #include "common.cuh"
+#include "mma_frag.cuh"
 #include "sm100.cuh"
 
 namespace pcb {
@@ -696,6 +701,281 @@ bool launch_i4_stage(popcornStatus_t* stp, float* out, const float* x, const uin
     return true;
 }
 
+// Decode (M = 1, K = 1024 or 2048) on the warp-level tensor path: the
+// staging of i4_stage_kernel (each row's packed codes, group scales and zero
+// points as 1-D bulk copies before griddepcontrol.wait, two CTAs per SM),
+// codes at a pitch of K / 2 + 16 bytes (an odd multiple of 16, so the
+// ldmatrix phases are free of bank conflicts), and the arithmetic of the
+// per-channel gemv_mma_kernel: warp w owns the k-steps [w KSMAX,
+// (w + 1) KSMAX) of 32 codes, its activations become 30-bit fixed point
+// X = rint(x 2^s) held as four signed base-256 digits, and
+// mma.sync m16n8k32 (u8 codes x s8 digits -> s32) sums them exactly.
+//
+// One ldmatrix.x4 brings a lane the 4 bytes (8 codes, k = 8t .. 8t + 7) of
+// rows g and g + 8 for two k-steps; the low nibbles (even k) form A's first
+// k-half and the high nibbles (odd k) its second, and B is built in the
+// same order (digits of x at 8t, 8t + 2, ... in b0, at 8t + 1, 8t + 3, ...
+// in b1). After each group of GSTEPS steps the exact sums give
+//     sum_k (c_k - z) x_k = 2^-s (sum_k c_k X_k - z sum_k X_k)
+// in double (sum_k X_k exact), times the group scale; the 16 warp partials
+// are added in warp order and rounded once. Warps holding a non-finite or
+// extreme activation use popcorn's per-element form (w = (c - z) s, fma).
+constexpr int kI4MmaStageBytes = (228 * 1024 - 2 * 1024) / 2 - 64;
+constexpr int kI4MmaMaxRows = 64;
+
+// B fragment of k-step c in the int4 k-order, and this lane's sum of the
+// eight fixed-point activations it read (lanes g < 4; zero above).
+__device__ __forceinline__ void i4_b_fragment(const float* x, int c, float up, int lane, uint32_t& b0, uint32_t& b1,
+                                              double& xsum) {
+    const int g = lane >> 2;
+    const float4* p = reinterpret_cast<const float4*>(x + 32 * c + 8 * (lane & 3));
+    const float4 v0 = __ldg(p);
+    const float4 v1 = __ldg(p + 1);
+    const int i0 = __float2int_rn(v0.x * up), i1 = __float2int_rn(v0.y * up);
+    const int i2 = __float2int_rn(v0.z * up), i3 = __float2int_rn(v0.w * up);
+    const int i4 = __float2int_rn(v1.x * up), i5 = __float2int_rn(v1.y * up);
+    const int i6 = __float2int_rn(v1.z * up), i7 = __float2int_rn(v1.w * up);
+    const uint32_t sel = static_cast<uint32_t>((g & 3) | (((g & 3) + 4) << 4));
+    const uint32_t o = 0x80808080u;
+    const uint32_t ev = __byte_perm(__byte_perm(static_cast<uint32_t>(i0) + o, static_cast<uint32_t>(i2) + o, sel),
+                                    __byte_perm(static_cast<uint32_t>(i4) + o, static_cast<uint32_t>(i6) + o, sel),
+                                    0x5410) ^ o;
+    const uint32_t od = __byte_perm(__byte_perm(static_cast<uint32_t>(i1) + o, static_cast<uint32_t>(i3) + o, sel),
+                                    __byte_perm(static_cast<uint32_t>(i5) + o, static_cast<uint32_t>(i7) + o, sel),
+                                    0x5410) ^ o;
+    b0 = g < 4 ? ev : 0u;
+    b1 = g < 4 ? od : 0u;
+    const int64_t s8 = static_cast<int64_t>(i0) + i1 + i2 + i3 + i4 + i5 + i6 + i7;  // |s8| < 2^33
+    xsum = g == 0 ? static_cast<double>(s8) : 0.0;
+}
+
+template <int KSMAX, int GSTEPS, int GROUPS, int SETS>
+__global__ void __launch_bounds__(kMmaThreads, 2)
+i4_mma_kernel(float* __restrict__ out, const float* __restrict__ x, const uint8_t* __restrict__ q,
+              const float* __restrict__ scale, const float* __restrict__ zero, int64_t N, int64_t K, int64_t gs) {
+    constexpr int NG = KSMAX / GSTEPS;  // groups of one warp
+    extern __shared__ __align__(16) uint8_t st[];  // codes [rows][K/2 + 16], scales, zeros [rows][groups]
+    __shared__ __align__(8) uint64_t s_full;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t G = gridDim.x;
+    const int64_t r0 = N * blockIdx.x / G;
+    const int rows = static_cast<int>(N * (blockIdx.x + 1) / G - r0);
+    const int rows_max = static_cast<int>((N + G - 1) / G);
+    const int row_bytes = static_cast<int>(K >> 1);
+    const int pitch = row_bytes + 16;
+    const int groups = static_cast<int>(K / gs);
+    float* sc_s = reinterpret_cast<float*>(st + rows_max * pitch);
+    float* zp_s = sc_s + rows_max * groups;
+    const uint32_t full = sm100::smem_addr(&s_full);
+    const uint32_t base = sm100::smem_addr(st);
+
+    if (threadIdx.x == 0) {
+        sm100::mbar_init(full, 1);
+        sm100::fence_barrier_init();
+        sm100::mbar_arrive_expect_tx(full, static_cast<uint32_t>(rows * (row_bytes + 8 * groups)));
+    }
+    pdl_launch_dependents();
+    __syncthreads();
+    if (threadIdx.x < rows) {
+        const int r = threadIdx.x;
+        sm100::bulk_load_1d(base + r * pitch, q + (r0 + r) * row_bytes, static_cast<uint32_t>(row_bytes), full);
+    } else if (threadIdx.x >= 128 && threadIdx.x < 128 + rows) {
+        const int r = threadIdx.x - 128;
+        sm100::bulk_load_1d(sm100::smem_addr(sc_s + r * groups), scale + (r0 + r) * groups,
+                            static_cast<uint32_t>(4 * groups), full);
+    } else if (threadIdx.x >= 256 && threadIdx.x < 256 + rows) {
+        const int r = threadIdx.x - 256;
+        sm100::bulk_load_1d(sm100::smem_addr(zp_s + r * groups), zero + (r0 + r) * groups,
+                            static_cast<uint32_t>(4 * groups), full);
+    } else if (threadIdx.x == kMmaThreads - 1) {
+        prefetch_l2_range(x, K * static_cast<int64_t>(sizeof(float)), 0, 1);
+    }
+    pdl_wait();
+    const int c0 = warp * KSMAX;
+    const int steps = static_cast<int>(K >> 5);
+    const WarpScale ws = warp_scale<KSMAX, true>(x, steps, c0, KSMAX, lane);
+    const int64_t grp0 = static_cast<int64_t>(32) * c0 / gs;
+
+    if (!sm100::mbar_wait(full, 0, &g_i4_error, kI4StageTimeoutBit)) {
+        sm100::mbar_wait(full, 0, &g_i4_error, kI4StageTimeoutBit);
+    }
+
+    const int g = lane >> 2;
+    const int rgroups = (rows + 15) >> 4;
+    double part_lo[GROUPS], part_hi[GROUPS];
+    #pragma unroll
+    for (int j = 0; j < GROUPS; ++j) part_lo[j] = part_hi[j] = 0.0;
+    if (ws.fixed) {
+        const double down = __longlong_as_double(static_cast<long long>(1023 - ws.s) << 52);
+        const int mi = lane >> 3;
+        const int mrow = (lane & 7) + 8 * (mi & 1);
+        const int mk = 16 * (mi >> 1);
+        #pragma unroll
+        for (int n = 0; n < NG; ++n) {
+            int d[GROUPS][SETS][4];
+            #pragma unroll
+            for (int j = 0; j < GROUPS; ++j) {
+                #pragma unroll
+                for (int e2 = 0; e2 < SETS; ++e2) d[j][e2][0] = d[j][e2][1] = d[j][e2][2] = d[j][e2][3] = 0;
+            }
+            double xs = 0.0;  // sum of this group's X over this warp's steps (lanes g == 0, per t)
+            #pragma unroll
+            for (int i2 = 0; i2 < GSTEPS; i2 += 2) {
+                const int c = c0 + n * GSTEPS + i2;  // steps c and c + 1
+                uint32_t b[2][2];
+                #pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    double sx;
+                    i4_b_fragment(x, c + h, ws.up, lane, b[h][0], b[h][1], sx);
+                    xs += sx;
+                }
+                #pragma unroll
+                for (int j = 0; j < GROUPS; ++j) {
+                    if (j < rgroups) {
+                        int r = 16 * j + mrow;
+                        r = r < rows ? r : rows - 1;  // past the last row: read it again, never stored
+                        uint32_t m[4];
+                        ldmatrix_x4(m, base + r * pitch + 16 * c + mk);
+                        #pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const uint32_t a[4] = {m[2 * h] & 0x0F0F0F0Fu, m[2 * h + 1] & 0x0F0F0F0Fu,
+                                                   (m[2 * h] >> 4) & 0x0F0F0F0Fu, (m[2 * h + 1] >> 4) & 0x0F0F0F0Fu};
+                            mma_u8s8_16832(d[j][(i2 + h) % SETS], a, b[h][0], b[h][1]);
+                        }
+                    }
+                }
+            }
+            // sum over t of the g == 0 lanes, then to every lane
+            xs += __shfl_xor_sync(0xffffffffu, xs, 1);
+            xs += __shfl_xor_sync(0xffffffffu, xs, 2);
+            xs = __shfl_sync(0xffffffffu, xs, 0);
+            const double sxs = xs * down;
+            const int64_t grp = grp0 + n;
+            #pragma unroll
+            for (int j = 0; j < GROUPS; ++j) {
+                #pragma unroll
+                for (int e2 = 1; e2 < SETS; ++e2) {  // exact: |column sum| < 2^22
+                    #pragma unroll
+                    for (int v = 0; v < 4; ++v) d[j][0][v] += d[j][e2][v];
+                }
+                double lo, hi;
+                combine_digits(d[j][0], ws.s, lo, hi);
+                const int ra = min(16 * j + g, rows - 1);
+                const int rb = min(16 * j + g + 8, rows - 1);
+                part_lo[j] += (lo - static_cast<double>(zp_s[ra * groups + grp]) * sxs) *
+                              static_cast<double>(sc_s[ra * groups + grp]);
+                part_hi[j] += (hi - static_cast<double>(zp_s[rb * groups + grp]) * sxs) *
+                              static_cast<double>(sc_s[rb * groups + grp]);
+            }
+        }
+    } else {
+        // popcorn's per-element form (rare); lane r % 32 keeps row r's sum.
+        float fb0 = 0.0f, fb1 = 0.0f;
+        for (int r = 0; r < rows; ++r) {
+            const uint8_t* codes = st + r * pitch;
+            float a = 0.0f;
+            for (int c = c0; c < c0 + KSMAX; ++c) {
+                const int k = 32 * c + lane;
+                const int code = (codes[k >> 1] >> ((k & 1) * 4)) & 0xF;
+                const int gi = static_cast<int>(k / gs);
+                const float w = (static_cast<float>(code) - zp_s[r * groups + gi]) * sc_s[r * groups + gi];
+                a = fmaf(__ldg(x + k), w, a);
+            }
+            #pragma unroll
+            for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+            if (lane == (r & 31)) {
+                if (r < 32) fb0 = a;
+                else fb1 = a;
+            }
+        }
+        part_lo[0] = static_cast<double>(fb0);
+        part_hi[0] = static_cast<double>(fb1);
+    }
+    __syncthreads();  // every read of the staged codes is done: reuse them as [16][rows] doubles
+    double* part = reinterpret_cast<double*>(st);
+    if (ws.fixed) {
+        if ((lane & 3) == 0) {
+            #pragma unroll
+            for (int j = 0; j < GROUPS; ++j) {
+                if (16 * j + g < rows) part[warp * rows + 16 * j + g] = part_lo[j];
+                if (16 * j + g + 8 < rows) part[warp * rows + 16 * j + g + 8] = part_hi[j];
+            }
+        }
+    } else {
+        if (lane < rows) part[warp * rows + lane] = part_lo[0];
+        if (lane + 32 < rows) part[warp * rows + lane + 32] = part_hi[0];
+    }
+    __syncthreads();
+    if (static_cast<int>(threadIdx.x) < rows) {
+        const int i = threadIdx.x;
+        double sum = 0.0;
+        #pragma unroll
+        for (int w = 0; w < kMmaWarps; ++w) sum += part[w * rows + i];
+        out[r0 + i] = static_cast<float>(sum);
+    }
+}
+
+template <int KSMAX, int GSTEPS, int GROUPS, int SETS>
+popcornStatus_t launch_i4_mma_t(float* out, const float* x, const uint8_t* q, const float* scale, const float* zero,
+                                int64_t N, int64_t K, int64_t gs, int64_t G, int64_t smem, cudaStream_t stream) {
+    auto kern = i4_mma_kernel<KSMAX, GSTEPS, GROUPS, SETS>;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const bool known = dev >= 0 && dev < 64;
+    if (!known || !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kI4MmaStageBytes);
+        if (e == cudaSuccess) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     cudaSharedmemCarveoutMaxShared);
+        }
+        if (e != cudaSuccess) return record_cuda(e);
+        if (known) attr_set[dev] = true;
+    }
+    cudaLaunchAttribute attr[1];
+    const cudaLaunchConfig_t cfg = pdl_config(dim3(static_cast<unsigned>(G)), dim3(kMmaThreads),
+                                              static_cast<size_t>(smem), stream, attr);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, out, x, q, scale, zero, N, K, gs);
+    return (e != cudaSuccess) ? record_cuda(e) : check_launch();
+}
+
+// Tensor-path int4 decode: M = 1, K of 1024 or 2048, group_size a multiple
+// of 64 with a warp's K / 16 columns holding whole groups (or lying in one),
+// K / group_size % 4 == 0 (16-byte scale rows), 16-byte aligned operands,
+// each CTA's rows within kI4MmaStageBytes and at most 20 MMAs per warp.
+// Returns false (nothing launched) otherwise. At K = 4096 the kernel builds
+// and passes its tests but measured slower than i4_stage_kernel (5.39 against
+// 4.32 us at N = 4096, group 128: unpacking x into digits for the int4
+// k-order and the per-group zero-point terms cost more issue time than the
+// dp4a form), so that K keeps i4_stage_kernel.
+bool launch_i4_mma(popcornStatus_t* stp, float* out, const float* x, const uint8_t* q, const float* scale,
+                   const float* zero, int64_t N, int64_t K, int64_t gs, cudaStream_t stream) {
+    if (K != 1024 && K != 2048) return false;
+    const int64_t groups = K / gs;
+    if (gs % 64 != 0 || groups % 4 != 0) return false;
+    if (!aligned16(x) || !aligned16(q) || !aligned16(scale) || !aligned16(zero)) return false;
+    const int64_t ksmax = K / 512;
+    const int64_t span = 32 * ksmax;
+    if (!(span % gs == 0 || gs % span == 0)) return false;
+    const int64_t gsteps = gs >= span ? ksmax : gs / 32;
+    const int64_t G = device_sm_count() < N ? device_sm_count() : N;
+    const int64_t rows_max = ceil_div(N, G);
+    const int64_t pitch = K / 2 + 16;
+    const int64_t smem = rows_max * (pitch + 8 * groups);
+    if (rows_max > kI4MmaMaxRows || smem > kI4MmaStageBytes) return false;
+    if (ceil_div(rows_max, 16) * ksmax > 20) return false;
+    popcornStatus_t r = POPCORN_SUCCESS;
+    if (ksmax == 2) {
+        r = launch_i4_mma_t<2, 2, 4, 2>(out, x, q, scale, zero, N, K, gs, G, smem, stream);
+    } else if (ksmax == 4) {
+        if (gsteps == 2) return false;  // group 64 at K = 2048: spills at 64 registers; the staged dp4a kernel
+        r = launch_i4_mma_t<4, 4, 4, 2>(out, x, q, scale, zero, N, K, gs, G, smem, stream);
+    }
+    *stp = r;
+    return true;
+}
+
 template <int MT, int U, int R>
 popcornStatus_t launch_i4_xs(float* out, const float* x, const uint8_t* q, const float* scale, const float* zero,
                              int64_t M, int64_t N, int64_t K, int64_t gs, cudaStream_t stream) {
@@ -744,6 +1024,7 @@ extern "C" popcornStatus_t popcornDequantizeMatmulGrouped_i4f32(float* out, cons
     if (!tiny && aligned && group_size % 16 == 0 && slices <= 4 && grid_ok) {
         if (M == 1) {
             popcornStatus_t st = POPCORN_SUCCESS;
+            if (launch_i4_mma(&st, out, x, qweight, scale, zero, N, K, group_size, stream)) return st;
             if (launch_i4_stage(&st, out, x, qweight, scale, zero, N, K, group_size, stream)) return st;
             if (slices == 1) return launch_i4_xs<1, 1, 8>(out, x, qweight, scale, zero, M, N, K, group_size, stream);
             if (slices == 2) return launch_i4_xs<1, 2, 4>(out, x, qweight, scale, zero, M, N, K, group_size, stream);

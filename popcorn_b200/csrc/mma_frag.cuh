@@ -1,5 +1,5 @@
 // Warp-level int8 tensor-path helpers of the staged decode kernels
-// (gemv.cu, grouped.cu): mma.sync m16n8k32 s8 x s8 -> s32 with the weight
+// (gemv.cu, grouped.cu, int4.cu): mma.sync m16n8k32 s8 x s8 -> s32 with the weight
 // codes as A (16 rows x 32 codes from ldmatrix) and the activations as B
 // (columns 0..3 the four signed base-256 digits of a per-warp 30-bit fixed
 // point value, columns 4..7 zero).
@@ -15,6 +15,15 @@ constexpr int kMmaThreads = kMmaWarps * 32;
 __device__ __forceinline__ void mma_s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// The same with unsigned 8-bit A (int4 codes widened to bytes).
+__device__ __forceinline__ void mma_u8s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
         "{%0, %1, %2, %3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));

@@ -111,6 +111,24 @@ def test_random_shapes_match_oracle(cuda, shape):
     assert oracle.normwise_rel_err(got, ref) <= TOL_F32
 
 
+@pytest.mark.parametrize("N,K,gs", [(8192, 1024, 64), (6000, 2048, 128), (6000, 1024, 256), (3000, 2048, 512)])
+def test_tensor_path_decode_vs_oracle_and_row_split(cuda, N, K, gs):
+    # The M = 1 tensor-path kernel (codes unpacked to bytes, mma.sync against
+    # fixed-point digits, zero points through exact group sums of x): the
+    # oracle within the f32 tolerance, and each row's bits independent of
+    # how rows share a CTA.
+    import torch
+
+    x, q, s, z = _case(1, N, K, gs, N + K + gs)
+    got = _matmul(torch, cuda, x, q, s, z, gs)
+    ref = oracle.dequant_matmul_grouped_i4(x, q, s, z, gs, fused=True, threads=8)
+    assert oracle.normwise_rel_err(got, ref) <= TOL_F32
+    lo, n2 = 29, (1 << 22) // K + 51  # above the sequential kernel's 2^22 multiply-adds
+    sub = _matmul(torch, cuda, x, np.ascontiguousarray(q[lo:lo + n2]), np.ascontiguousarray(s[lo:lo + n2]),
+                  np.ascontiguousarray(z[lo:lo + n2]), gs)
+    assert np.array_equal(sub.view(np.uint32), got[:, lo:lo + n2].view(np.uint32))
+
+
 @pytest.mark.parametrize("kind", ["nan", "inf", "tiny"])
 def test_decode_nonfinite_and_tiny_activations(cuda, kind):
     # M = 1 with a NaN, an infinity or a slice of denormals in x: those warps
