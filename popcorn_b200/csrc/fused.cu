@@ -12,6 +12,8 @@
 //    layout of the f32 GEMV; a block spans all of K, so it forms the row's sum
 //    of squares itself (NORM) and normalises its x slices in registers; with
 //    GLU it streams R rows of both weight matrices and writes silu(g) * u.
+//    At M = 1 the dot products are exact dp2a sums on 30-bit fixed-point
+//    slices, as in the per-channel decode GEMV.
 //  * tensor cores (M > 4, >= 2^27 multiply-adds): the RMSNorm runs inside the
 //    x -> f16 prologue; the gate GEMM writes g to `out` and the up GEMM's
 //    epilogue turns it into silu(g) * u (tc_gemm.cu).
@@ -26,6 +28,19 @@ constexpr int kFThreads = 256;
 constexpr int kFWarps = kFThreads / 32;
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
+
+// dp2a with unsigned 16-bit halves in the first operand (low or high pair
+// of signed bytes in the second).
+__device__ __forceinline__ int dp2a_lo_u(uint32_t a, int b, int c) {
+    int d;
+    asm("dp2a.lo.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp2a_hi_u(uint32_t a, int b, int c) {
+    int d;
+    asm("dp2a.hi.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
 
 // Four int8 codes (one word) -> four exact floats (byte ^ 0x80 in the low
 // mantissa byte of 2^23 is 2^23 + 128 + code).
@@ -178,6 +193,70 @@ fused_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const floa
     float acc[V];
     #pragma unroll
     for (int i = 0; i < V; ++i) acc[i] = 0.0f;
+    // M = 1: each thread's (normalised) slices as 30-bit fixed point from
+    // the slices' max |x|, X = hi * 2^16 + lo, and exact dp2a products with
+    // the codes (the per-channel decode GEMV's arithmetic); a warp holding a
+    // non-finite value or a max |x| outside [2^-90, 2^100] keeps the float
+    // path below.
+    bool fixed = false;
+    float up = 1.0f, down = 1.0f;
+    if constexpr (MT == 1) {
+        uint32_t mb = 0;
+        #pragma unroll
+        for (int u = 0; u < U; ++u) {
+            #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float4 v = xr[0][u][c];
+                mb = max(mb, max(max(__float_as_uint(v.x) & 0x7FFFFFFFu, __float_as_uint(v.y) & 0x7FFFFFFFu),
+                                 max(__float_as_uint(v.z) & 0x7FFFFFFFu, __float_as_uint(v.w) & 0x7FFFFFFFu)));
+            }
+        }
+        const bool bad = mb != 0u && (mb < 0x12800000u || mb > 0x71800000u);
+        fixed = !__any_sync(0xffffffffu, bad);
+        if (fixed && mb != 0u) {
+            const int ex = 156 - static_cast<int>(mb >> 23);  // max |x| * 2^ex in [2^29, 2^30)
+            up = __int_as_float((ex + 127) << 23);
+            down = __int_as_float((127 - ex) << 23);
+        }
+    }
+    if (MT == 1 && fixed) {
+        uint32_t xh[U][8], xl[U][8];
+        #pragma unroll
+        for (int u = 0; u < U; ++u) {
+            #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float4 v = xr[0][u][c];
+                const uint32_t a0 = static_cast<uint32_t>(__float2int_rn(v.x * up));
+                const uint32_t a1 = static_cast<uint32_t>(__float2int_rn(v.y * up));
+                const uint32_t a2 = static_cast<uint32_t>(__float2int_rn(v.z * up));
+                const uint32_t a3 = static_cast<uint32_t>(__float2int_rn(v.w * up));
+                xl[u][2 * c] = __byte_perm(a0, a1, 0x5410);
+                xh[u][2 * c] = __byte_perm(a0, a1, 0x7632);
+                xl[u][2 * c + 1] = __byte_perm(a2, a3, 0x5410);
+                xh[u][2 * c + 1] = __byte_perm(a2, a3, 0x7632);
+            }
+        }
+        #pragma unroll
+        for (int mat = 0; mat < NM; ++mat) {
+            #pragma unroll
+            for (int r = 0; r < R; ++r) {
+                int sh = 0, sl = 0;
+                #pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int words[4] = {static_cast<int>(w[mat][r][u].x), static_cast<int>(w[mat][r][u].y),
+                                          static_cast<int>(w[mat][r][u].z), static_cast<int>(w[mat][r][u].w)};
+                    #pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        sh = __dp2a_lo(static_cast<int>(xh[u][2 * c]), words[c], sh);
+                        sh = __dp2a_hi(static_cast<int>(xh[u][2 * c + 1]), words[c], sh);
+                        sl = dp2a_lo_u(xl[u][2 * c], words[c], sl);
+                        sl = dp2a_hi_u(xl[u][2 * c + 1], words[c], sl);
+                    }
+                }
+                acc[mat * R + r] = fmaf(static_cast<float>(sh), 65536.0f, static_cast<float>(sl)) * down;
+            }
+        }
+    } else {
     #pragma unroll
     for (int u = 0; u < U; ++u) {
         #pragma unroll
@@ -203,6 +282,7 @@ fused_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const floa
                 for (int m = 0; m < MT; ++m) acc[(mat * R + r) * MT + m] += a[m].x + a[m].y;
             }
         }
+    }
     }
     const float total = fused_reduce_scatter<V>(acc, lane);
     constexpr int span = 32 / V;
