@@ -48,9 +48,8 @@ def test_throughput_and_roofline_units():
 def test_traffic_is_close_to_the_algorithmic_bytes():
     # DRAM traffic per launch well above the algorithmic bytes would mean
     # re-reads; each recorded figure stays within 5 % above them (the fused
-    # MLP capture counts 3.5 MB of writes, L2 write-backs of lines dirtied
-    # before the launch that its 90 MB stream evicts; its reads are the
-    # weights to within 0.2 %).
+    # MLP capture counts 3.5 MB of DRAM writes against the kernel's 44 KB of
+    # stores; its reads are the weights to within 0.2 %).
     for name, traffic in bench.NCU_TRAFFIC.items():
         wl = bench.WORKLOADS[name]
         if wl["unit"] != "GB/s":
