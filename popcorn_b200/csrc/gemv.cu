@@ -347,6 +347,17 @@ gemv_xs_kernel(float* __restrict__ out, const float* __restrict__ x, const int8_
                         #pragma unroll
                         for (int u = 0; u < U; ++u) w[r][u] = wn[r][u];
                     if (rb + R < r1) load_group(rb + R, wn);
+                    // The group after next into L2 (its R rows are contiguous):
+                    // more bytes in flight than the registers hold. A same-box
+                    // A/B, us per call: K = 11008, N = 4096 11.52 -> 10.24;
+                    // N = 12288 10.50 -> 10.32; N = 32000 21.9 -> 21.3 (a
+                    // distance of three or four groups was slower).
+                    if (tid == 0 && rb + 2 * R < r1) {
+                        const int64_t nb = ((r1 - rb - 2 * R) < R ? (r1 - rb - 2 * R) : R) * K;
+                        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(q + (rb + 2 * R) * K),
+                                     "r"(static_cast<uint32_t>(nb))
+                                     : "memory");
+                    }
                     dot(w, acc);
                 } else {
                     if (rb != r0) load_group(rb, wn);
