@@ -27,9 +27,9 @@ constexpr int kQuantThreads = 256;
 constexpr int kWarpsPerBlock = kQuantThreads / 32;
 
 __device__ __forceinline__ float absmax_step(float m, float v) {
-    float a = fabsf(v);
-    // NaN compares false and is skipped, exactly like popcorn's `abs_v > max`.
-    return (a > m) ? a : m;
+    // fmaxf returns the non-NaN operand, so a NaN |v| is skipped exactly like
+    // popcorn's `if (abs_v > max)`; m itself is never NaN (it starts at 0).
+    return fmaxf(m, fabsf(v));
 }
 
 __device__ __forceinline__ int8_t quantize_one(float v, float sc) {
@@ -50,11 +50,11 @@ __device__ __forceinline__ int8_t quantize_one(float v, float sc) {
 // compare is false) the exact division decides, ties to even included.
 __device__ __forceinline__ int8_t quantize_one_rcp(float v, float sc, float rcp) {
     const float t = v * rcp;
-    float q = rintf(t);
-    if (!(fabsf(t - q) <= 0.4999f)) q = rintf(v / sc);
-    if (q > 127.0f) q = 127.0f;
-    if (q < -128.0f) q = -128.0f;
-    return static_cast<int8_t>(q);
+    const float q = rintf(t);
+    // |v| <= max |row| and rcp = 1/sc to 1 ulp put |t| within a few ulps of
+    // 127 at most, so a q that passes the test needs no clamp.
+    if (fabsf(t - q) <= 0.4999f) return static_cast<int8_t>(q);
+    return quantize_one(v, sc);
 }
 
 // Rows whose scale is not a finite normal number (a zero, denormal or
