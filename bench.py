@@ -328,6 +328,8 @@ class Setup:
             sms = self.torch.cuda.get_device_properties(self.x[0].device).multi_processor_count
             if self.bits != 4 and self.M == 1 and staged_mma_grouped(self.K, self.Nl, self.gs, sms):
                 return f"grouped_f32 (group {self.gs}, staged rows, mma.sync s8)"
+            if self.bits == 4 and self.M == 1 and staged_mma_i4(self.K, self.Nl, self.gs, sms):
+                return f"int4 (group {self.gs}, staged rows, mma.sync u8)"
             return f"{fmt}_{'tensor_f16' if self.grouped_tensor() else 'f32'} (group {self.gs})"
         path = self.pc.select_path(self.x[0].data_ptr(), self.q[0].data_ptr(), self.M, self.Nl, self.K)
         if path == self.pc.PATH_TENSOR_F16 and self.M <= 128 and self.K <= 65536:
@@ -599,6 +601,26 @@ def staged_mma_grouped(K, N, gs, sms):
     return rows <= 64 and rows * (K + 16) <= 115648 and -(-rows // 16) * (K // 512) <= 20
 
 
+def staged_mma_i4(K, N, gs, sms):
+    """Whether an M = 1 int4 call runs the staged mma.sync decode: K of 1024,
+    2048 or 4096, group_size a multiple of 64 (of 128 at K = 4096; not 64 at
+    K = 2048) with a warp's K / 16 columns holding whole groups or lying in
+    one, K / group_size % 4 == 0, each SM's rows (at most 64) within 115,648
+    bytes of codes at a pitch of K / 2 + 16, scales, zero points and 4 K
+    bytes of converted activations, and at most 20 MMAs per warp."""
+    if K not in (1024, 2048, 4096) or gs % 64 or (K // gs) % 4 or N < 1:
+        return False
+    span = K // 16
+    if span % gs and gs % span:
+        return False
+    gsteps = K // 512 if gs >= span else gs // 32
+    if (K == 4096 and gsteps < 4) or (K == 2048 and gsteps < 4):
+        return False
+    rows = -(-N // min(sms, N))
+    smem = rows * (K // 2 + 16 + 8 * (K // gs + 4)) + 4 * K
+    return rows <= 64 and smem <= 115648 and -(-rows // 16) * (K // 512) <= 20
+
+
 def compute_dtype(path, M, K, grouped):
     """Arithmetic of the path a workload takes. The staged M = 1 decode
     (per channel, K % 32 == 0, K <= 8192, rows fitting): x as 30-bit fixed point per warp in
@@ -609,6 +631,8 @@ def compute_dtype(path, M, K, grouped):
     with M <= 128 (K <= 65536) run tcgen05 kind::i8 on activations held as
     16-bit fixed point in two int8 digits, everything else f16 x f16 with
     f32 accumulation."""
+    if "mma.sync u8" in path:
+        return "s30 fixed-point as 4 s8 digits x u4 codes (mma.sync u8.s8) -> s32/f64"
     if "mma.sync" in path:
         return "s30 fixed-point as 4 s8 digits x s8 (mma.sync) -> s32/f64"
     if "tensor" not in path:

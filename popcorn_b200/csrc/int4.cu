@@ -21,8 +21,8 @@
 //    codes become floats without a conversion instruction: a nibble placed in
 //    the low mantissa bits of 2^23 reads as 2^23 + c; the high nibble is taken
 //    in place (2^23 + 16 c) and its activation pre-scaled by 1/16, exactly.
-//  * i4_mma_kernel -- decode (M = 1, K = 1024 or 2048, group size a
-//    multiple of 64): staged rows, codes unpacked to bytes and summed against
+//  * i4_mma_kernel -- decode (M = 1, K = 1024, 2048 or 4096, group size a
+//    multiple of 64, of 128 at K = 4096): staged rows, codes unpacked to bytes and summed against
 //    fixed-point digits of x with mma.sync (u8 x s8), the zero point applied
 //    through the exact group sum of x.
 //  * i4_quantize_kernel -- one warp per (row, group): min and max by shuffles,
@@ -701,7 +701,7 @@ bool launch_i4_stage(popcornStatus_t* stp, float* out, const float* x, const uin
     return true;
 }
 
-// Decode (M = 1, K = 1024 or 2048) on the warp-level tensor path: the
+// Decode (M = 1, K = 1024, 2048 or 4096) on the warp-level tensor path: the
 // staging of i4_stage_kernel (each row's packed codes, group scales and zero
 // points as 1-D bulk copies before griddepcontrol.wait, two CTAs per SM),
 // codes at a pitch of K / 2 + 16 bytes (an odd multiple of 16, so the
@@ -715,7 +715,8 @@ bool launch_i4_stage(popcornStatus_t* stp, float* out, const float* x, const uin
 // rows g and g + 8 for two k-steps; the low nibbles (even k) form A's first
 // k-half and the high nibbles (odd k) its second, and B is built in the
 // same order (digits of x at 8t, 8t + 2, ... in b0, at 8t + 1, 8t + 3, ...
-// in b1). After each group of GSTEPS steps the exact sums give
+// in b1) from the warp's activations, converted once (one value per lane
+// and step) into shared memory; sum_k X_k comes from the digit sums. After each group of GSTEPS steps the exact sums give
 //     sum_k (c_k - z) x_k = 2^-s (sum_k c_k X_k - z sum_k X_k)
 // in double (sum_k X_k exact), times the group scale; the 16 warp partials
 // are added in warp order and rounded once. Warps holding a non-finite or
@@ -723,30 +724,22 @@ bool launch_i4_stage(popcornStatus_t* stp, float* out, const float* x, const uin
 constexpr int kI4MmaStageBytes = (228 * 1024 - 2 * 1024) / 2 - 64;
 constexpr int kI4MmaMaxRows = 64;
 
-// B fragment of k-step c in the int4 k-order, and this lane's sum of the
-// eight fixed-point activations it read (lanes g < 4; zero above).
-__device__ __forceinline__ void i4_b_fragment(const float* x, int c, float up, int lane, uint32_t& b0, uint32_t& b1,
-                                              double& xsum) {
+// B fragment of a k-step in the int4 k-order from the warp's converted
+// activations y (Y = X + 0x80808080 per value, 32 per step): lane (g, t)
+// takes the eight values 8t .. 8t + 7 of the step, digit g % 4 of the even
+// ones in b0 and of the odd ones in b1 (lanes g >= 4: zero); *dsum gains
+// the sum of those eight digits.
+__device__ __forceinline__ void i4_b_fragment(const uint32_t* y, int lane, uint32_t& b0, uint32_t& b1, int& dsum) {
     const int g = lane >> 2;
-    const float4* p = reinterpret_cast<const float4*>(x + 32 * c + 8 * (lane & 3));
-    const float4 v0 = __ldg(p);
-    const float4 v1 = __ldg(p + 1);
-    const int i0 = __float2int_rn(v0.x * up), i1 = __float2int_rn(v0.y * up);
-    const int i2 = __float2int_rn(v0.z * up), i3 = __float2int_rn(v0.w * up);
-    const int i4 = __float2int_rn(v1.x * up), i5 = __float2int_rn(v1.y * up);
-    const int i6 = __float2int_rn(v1.z * up), i7 = __float2int_rn(v1.w * up);
+    const uint4 p = *reinterpret_cast<const uint4*>(y + 8 * (lane & 3));
+    const uint4 r = *reinterpret_cast<const uint4*>(y + 8 * (lane & 3) + 4);
     const uint32_t sel = static_cast<uint32_t>((g & 3) | (((g & 3) + 4) << 4));
     const uint32_t o = 0x80808080u;
-    const uint32_t ev = __byte_perm(__byte_perm(static_cast<uint32_t>(i0) + o, static_cast<uint32_t>(i2) + o, sel),
-                                    __byte_perm(static_cast<uint32_t>(i4) + o, static_cast<uint32_t>(i6) + o, sel),
-                                    0x5410) ^ o;
-    const uint32_t od = __byte_perm(__byte_perm(static_cast<uint32_t>(i1) + o, static_cast<uint32_t>(i3) + o, sel),
-                                    __byte_perm(static_cast<uint32_t>(i5) + o, static_cast<uint32_t>(i7) + o, sel),
-                                    0x5410) ^ o;
+    const uint32_t ev = __byte_perm(__byte_perm(p.x, p.z, sel), __byte_perm(r.x, r.z, sel), 0x5410) ^ o;
+    const uint32_t od = __byte_perm(__byte_perm(p.y, p.w, sel), __byte_perm(r.y, r.w, sel), 0x5410) ^ o;
     b0 = g < 4 ? ev : 0u;
     b1 = g < 4 ? od : 0u;
-    const int64_t s8 = static_cast<int64_t>(i0) + i1 + i2 + i3 + i4 + i5 + i6 + i7;  // |s8| < 2^33
-    xsum = g == 0 ? static_cast<double>(s8) : 0.0;
+    dsum = __dp4a(static_cast<int>(b0), 0x01010101, __dp4a(static_cast<int>(b1), 0x01010101, dsum));
 }
 
 template <int KSMAX, int GSTEPS, int GROUPS, int SETS>
@@ -754,7 +747,9 @@ __global__ void __launch_bounds__(kMmaThreads, 2)
 i4_mma_kernel(float* __restrict__ out, const float* __restrict__ x, const uint8_t* __restrict__ q,
               const float* __restrict__ scale, const float* __restrict__ zero, int64_t N, int64_t K, int64_t gs) {
     constexpr int NG = KSMAX / GSTEPS;  // groups of one warp
-    extern __shared__ __align__(16) uint8_t st[];  // codes [rows][K/2 + 16], scales, zeros [rows][groups]
+    // codes [rows][K/2 + 16], scales and zeros [rows][groups + 4] (the pad
+    // spreads the rows of one scale read over the banks), then Y
+    extern __shared__ __align__(16) uint8_t st[];
     __shared__ __align__(8) uint64_t s_full;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -766,7 +761,9 @@ i4_mma_kernel(float* __restrict__ out, const float* __restrict__ x, const uint8_
     const int pitch = row_bytes + 16;
     const int groups = static_cast<int>(K / gs);
     float* sc_s = reinterpret_cast<float*>(st + rows_max * pitch);
-    float* zp_s = sc_s + rows_max * groups;
+    const int gstride = groups + 4;
+    float* zp_s = sc_s + rows_max * gstride;
+    uint32_t* ybuf = reinterpret_cast<uint32_t*>(zp_s + rows_max * gstride) + warp * (32 * KSMAX);  // this warp's Y
     const uint32_t full = sm100::smem_addr(&s_full);
     const uint32_t base = sm100::smem_addr(st);
 
@@ -782,19 +779,39 @@ i4_mma_kernel(float* __restrict__ out, const float* __restrict__ x, const uint8_
         sm100::bulk_load_1d(base + r * pitch, q + (r0 + r) * row_bytes, static_cast<uint32_t>(row_bytes), full);
     } else if (threadIdx.x >= 128 && threadIdx.x < 128 + rows) {
         const int r = threadIdx.x - 128;
-        sm100::bulk_load_1d(sm100::smem_addr(sc_s + r * groups), scale + (r0 + r) * groups,
+        sm100::bulk_load_1d(sm100::smem_addr(sc_s + r * gstride), scale + (r0 + r) * groups,
                             static_cast<uint32_t>(4 * groups), full);
     } else if (threadIdx.x >= 256 && threadIdx.x < 256 + rows) {
         const int r = threadIdx.x - 256;
-        sm100::bulk_load_1d(sm100::smem_addr(zp_s + r * groups), zero + (r0 + r) * groups,
+        sm100::bulk_load_1d(sm100::smem_addr(zp_s + r * gstride), zero + (r0 + r) * groups,
                             static_cast<uint32_t>(4 * groups), full);
     } else if (threadIdx.x == kMmaThreads - 1) {
         prefetch_l2_range(x, K * static_cast<int64_t>(sizeof(float)), 0, 1);
     }
     pdl_wait();
     const int c0 = warp * KSMAX;
-    const int steps = static_cast<int>(K >> 5);
-    const WarpScale ws = warp_scale<KSMAX, true>(x, steps, c0, KSMAX, lane);
+    // This warp's 32 * KSMAX activations, one per lane and step (coalesced),
+    // their max |x| (the rule of warp_scale), then Y = X + 0x80808080 into
+    // shared memory once, where every step's B fragments are built from.
+    float xv[KSMAX];
+    uint32_t mb = 0;
+    #pragma unroll
+    for (int i = 0; i < KSMAX; ++i) {
+        xv[i] = __ldg(x + 32 * (c0 + i) + lane);
+        mb = max(mb, __float_as_uint(xv[i]) & 0x7FFFFFFFu);
+    }
+    mb = __reduce_max_sync(0xffffffffu, mb);
+    WarpScale ws;
+    ws.fixed = mb == 0u || (mb >= 0x12800000u && mb <= 0x71800000u);
+    ws.s = mb == 0u ? 0 : 29 - (static_cast<int>(mb >> 23) - 127);
+    ws.up = mb == 0u ? 1.0f : __int_as_float((ws.s + 127) << 23);
+    if (ws.fixed) {
+        #pragma unroll
+        for (int i = 0; i < KSMAX; ++i) {
+            ybuf[32 * i + lane] = static_cast<uint32_t>(__float2int_rn(xv[i] * ws.up)) + 0x80808080u;
+        }
+    }
+    __syncwarp();
     const int64_t grp0 = static_cast<int64_t>(32) * c0 / gs;
 
     if (!sm100::mbar_wait(full, 0, &g_i4_error, kI4StageTimeoutBit)) {
@@ -819,16 +836,14 @@ i4_mma_kernel(float* __restrict__ out, const float* __restrict__ x, const uint8_
                 #pragma unroll
                 for (int e2 = 0; e2 < SETS; ++e2) d[j][e2][0] = d[j][e2][1] = d[j][e2][2] = d[j][e2][3] = 0;
             }
-            double xs = 0.0;  // sum of this group's X over this warp's steps (lanes g == 0, per t)
+            int dsum = 0;  // this lane's digit-g sum over the group's steps (lanes g < 4)
             #pragma unroll
             for (int i2 = 0; i2 < GSTEPS; i2 += 2) {
                 const int c = c0 + n * GSTEPS + i2;  // steps c and c + 1
                 uint32_t b[2][2];
                 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    double sx;
-                    i4_b_fragment(x, c + h, ws.up, lane, b[h][0], b[h][1], sx);
-                    xs += sx;
+                    i4_b_fragment(ybuf + 32 * (n * GSTEPS + i2 + h), lane, b[h][0], b[h][1], dsum);
                 }
                 #pragma unroll
                 for (int j = 0; j < GROUPS; ++j) {
@@ -846,10 +861,16 @@ i4_mma_kernel(float* __restrict__ out, const float* __restrict__ x, const uint8_
                     }
                 }
             }
-            // sum over t of the g == 0 lanes, then to every lane
-            xs += __shfl_xor_sync(0xffffffffu, xs, 1);
-            xs += __shfl_xor_sync(0xffffffffu, xs, 2);
-            xs = __shfl_sync(0xffffffffu, xs, 0);
+            // The group's sum of X = sum_d 256^d (sum of digit d): digit sums
+            // over t, then from lanes 0, 4, 8, 12 (exact in double).
+            dsum += __shfl_xor_sync(0xffffffffu, dsum, 1);
+            dsum += __shfl_xor_sync(0xffffffffu, dsum, 2);
+            const int s0 = __shfl_sync(0xffffffffu, dsum, 0);
+            const int s1 = __shfl_sync(0xffffffffu, dsum, 4);
+            const int s2 = __shfl_sync(0xffffffffu, dsum, 8);
+            const int s3 = __shfl_sync(0xffffffffu, dsum, 12);
+            const double xs = static_cast<double>(s0) + 256.0 * static_cast<double>(s1) +
+                              65536.0 * static_cast<double>(s2) + 16777216.0 * static_cast<double>(s3);
             const double sxs = xs * down;
             const int64_t grp = grp0 + n;
             #pragma unroll
@@ -863,10 +884,10 @@ i4_mma_kernel(float* __restrict__ out, const float* __restrict__ x, const uint8_
                 combine_digits(d[j][0], ws.s, lo, hi);
                 const int ra = min(16 * j + g, rows - 1);
                 const int rb = min(16 * j + g + 8, rows - 1);
-                part_lo[j] += (lo - static_cast<double>(zp_s[ra * groups + grp]) * sxs) *
-                              static_cast<double>(sc_s[ra * groups + grp]);
-                part_hi[j] += (hi - static_cast<double>(zp_s[rb * groups + grp]) * sxs) *
-                              static_cast<double>(sc_s[rb * groups + grp]);
+                part_lo[j] += (lo - static_cast<double>(zp_s[ra * gstride + grp]) * sxs) *
+                              static_cast<double>(sc_s[ra * gstride + grp]);
+                part_hi[j] += (hi - static_cast<double>(zp_s[rb * gstride + grp]) * sxs) *
+                              static_cast<double>(sc_s[rb * gstride + grp]);
             }
         }
     } else {
@@ -879,7 +900,7 @@ i4_mma_kernel(float* __restrict__ out, const float* __restrict__ x, const uint8_
                 const int k = 32 * c + lane;
                 const int code = (codes[k >> 1] >> ((k & 1) * 4)) & 0xF;
                 const int gi = static_cast<int>(k / gs);
-                const float w = (static_cast<float>(code) - zp_s[r * groups + gi]) * sc_s[r * groups + gi];
+                const float w = (static_cast<float>(code) - zp_s[r * gstride + gi]) * sc_s[r * gstride + gi];
                 a = fmaf(__ldg(x + k), w, a);
             }
             #pragma unroll
@@ -940,18 +961,14 @@ popcornStatus_t launch_i4_mma_t(float* out, const float* x, const uint8_t* q, co
     return (e != cudaSuccess) ? record_cuda(e) : check_launch();
 }
 
-// Tensor-path int4 decode: M = 1, K of 1024 or 2048, group_size a multiple
-// of 64 with a warp's K / 16 columns holding whole groups (or lying in one),
-// K / group_size % 4 == 0 (16-byte scale rows), 16-byte aligned operands,
-// each CTA's rows within kI4MmaStageBytes and at most 20 MMAs per warp.
-// Returns false (nothing launched) otherwise. At K = 4096 the kernel builds
-// and passes its tests but measured slower than i4_stage_kernel (5.39 against
-// 4.32 us at N = 4096, group 128: unpacking x into digits for the int4
-// k-order and the per-group zero-point terms cost more issue time than the
-// dp4a form), so that K keeps i4_stage_kernel.
+// Tensor-path int4 decode: M = 1, K of 1024, 2048 or 4096, group_size a
+// multiple of 64 (of 128 at K = 4096) with a warp's K / 16 columns holding
+// whole groups (or lying in one), K / group_size % 4 == 0 (16-byte scale
+// rows), 16-byte aligned operands, each CTA's rows within kI4MmaStageBytes
+// and at most 20 MMAs per warp. Returns false (nothing launched) otherwise.
 bool launch_i4_mma(popcornStatus_t* stp, float* out, const float* x, const uint8_t* q, const float* scale,
                    const float* zero, int64_t N, int64_t K, int64_t gs, cudaStream_t stream) {
-    if (K != 1024 && K != 2048) return false;
+    if (K != 1024 && K != 2048 && K != 4096) return false;
     const int64_t groups = K / gs;
     if (gs % 64 != 0 || groups % 4 != 0) return false;
     if (!aligned16(x) || !aligned16(q) || !aligned16(scale) || !aligned16(zero)) return false;
@@ -962,7 +979,7 @@ bool launch_i4_mma(popcornStatus_t* stp, float* out, const float* x, const uint8
     const int64_t G = device_sm_count() < N ? device_sm_count() : N;
     const int64_t rows_max = ceil_div(N, G);
     const int64_t pitch = K / 2 + 16;
-    const int64_t smem = rows_max * (pitch + 8 * groups);
+    const int64_t smem = rows_max * (pitch + 8 * (groups + 4)) + 4 * K;  // + 16 warps x (K / 16) Y words
     if (rows_max > kI4MmaMaxRows || smem > kI4MmaStageBytes) return false;
     if (ceil_div(rows_max, 16) * ksmax > 20) return false;
     popcornStatus_t r = POPCORN_SUCCESS;
@@ -971,6 +988,12 @@ bool launch_i4_mma(popcornStatus_t* stp, float* out, const float* x, const uint8
     } else if (ksmax == 4) {
         if (gsteps == 2) return false;  // group 64 at K = 2048: spills at 64 registers; the staged dp4a kernel
         r = launch_i4_mma_t<4, 4, 4, 2>(out, x, q, scale, zero, N, K, gs, G, smem, stream);
+    } else {
+        // Group 64 at K = 4096 (four flushes per warp) measured slower than
+        // i4_stage_kernel: 5.28 against 4.34 us at N = 4096.
+        if (rows_max > 32 || gsteps == 2) return false;
+        if (gsteps == 4) r = launch_i4_mma_t<8, 4, 2, 4>(out, x, q, scale, zero, N, K, gs, G, smem, stream);
+        else r = launch_i4_mma_t<8, 8, 2, 2>(out, x, q, scale, zero, N, K, gs, G, smem, stream);
     }
     *stp = r;
     return true;

@@ -80,6 +80,9 @@ def test_compute_dtype_routes():
     assert not bench.staged_mma_grouped(4096, 4096, 64, 148)  # four scale flushes per warp: slower
     assert not bench.staged_mma_grouped(2048, 6000, 32, 148)  # 32 scales per lane
     assert bench.compute_dtype("grouped_f32 (group 128, staged rows, mma.sync s8)", 1, 4096, True).endswith("f64")
+    assert bench.staged_mma_i4(4096, 4096, 128, 148) and bench.staged_mma_i4(1024, 8192, 64, 148)
+    assert not bench.staged_mma_i4(4096, 4096, 64, 148) and not bench.staged_mma_i4(4096, 4096, 4096, 148)
+    assert "u4" in bench.compute_dtype("int4 (group 128, staged rows, mma.sync u8)", 1, 4096, True)
     assert bench.compute_dtype("simt_f32", 2, 4096, False) == "f32"
     assert bench.compute_dtype("simt_f32", 1, 4096, True) == "f32"
     assert bench.compute_dtype("tensor_f16", 32, 4096, False).startswith("s8")

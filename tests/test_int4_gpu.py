@@ -111,7 +111,8 @@ def test_random_shapes_match_oracle(cuda, shape):
     assert oracle.normwise_rel_err(got, ref) <= TOL_F32
 
 
-@pytest.mark.parametrize("N,K,gs", [(8192, 1024, 64), (6000, 2048, 128), (6000, 1024, 256), (3000, 2048, 512)])
+@pytest.mark.parametrize("N,K,gs", [(8192, 1024, 64), (6000, 2048, 128), (6000, 1024, 256), (3000, 2048, 512),
+                                    (4096, 4096, 128), (3000, 4096, 512), (2000, 4096, 1024)])
 def test_tensor_path_decode_vs_oracle_and_row_split(cuda, N, K, gs):
     # The M = 1 tensor-path kernel (codes unpacked to bytes, mma.sync against
     # fixed-point digits, zero points through exact group sums of x): the
