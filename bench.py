@@ -79,8 +79,8 @@ NCU_TRAFFIC = {
     "skinny": 45440256,    # profiles/tc_i8_skinny_m32_k4096_n11008.md
     "prefill": 35509504,   # profiles/tc_gemm_pair_prefill_m2048_k4096_n4096.md
     "grouped_decode": 17352704,  # profiles/grouped_mma_decode_m1_k4096_n4096_g128.md
-    "int4_decode": 9502464,      # profiles/i4_stage_decode_m1_k4096_n4096_g128.md
-    "mlp_decode": 93792512,      # profiles/fused_xs_mlp_decode_m1_k4096_n11008.md
+    "int4_decode": 9487360,      # profiles/i4_mma_decode_m1_k4096_n4096_g128.md
+    "mlp_decode": 94391296,      # profiles/fused_xs_mlp_decode_m1_k4096_n11008.md
     "qkv_m128": 51826176,        # profiles/tc_i8_pair_m128_k4096_n12288.md
 }
 
