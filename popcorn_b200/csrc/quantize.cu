@@ -278,17 +278,32 @@ dequantize_bf16_kernel(uint16_t* __restrict__ out, const int8_t* __restrict__ q,
         const int warp = threadIdx.x >> 5;
         const int64_t pairs = K >> 3;  // 8-code pairs of words per row
         const int64_t chunks = (K + 511) >> 9;
-        for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
+        // This warp's (row, chunk) items in order; the codes of the next item
+        // are requested before the current one is expanded and stored, so two
+        // items' loads are in flight per warp.
+        auto load = [&](int64_t r, int64_t cc, uint2 (&w)[2]) {
+            const uint2* qr = reinterpret_cast<const uint2*>(q + r * K);
+            #pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int64_t i = cc * 64 + j * 32 + lane;
+                w[j] = i < pairs ? __ldg(qr + i) : make_uint2(0u, 0u);
+            }
+        };
+        int64_t row = blockIdx.x;
+        int64_t c = warp;
+        uint2 wn[2] = {make_uint2(0u, 0u), make_uint2(0u, 0u)};
+        if (c < chunks && row < N) load(row, c, wn);
+        while (c < chunks && row < N) {
+            int64_t row2 = row, c2 = c + kDeqWarps;
+            if (c2 >= chunks) {
+                c2 = warp;
+                row2 += gridDim.x;
+            }
+            const uint2 w[2] = {wn[0], wn[1]};
+            if (row2 < N) load(row2, c2, wn);
             const float sc = __ldg(scale + row);
-            const uint2* qr = reinterpret_cast<const uint2*>(q + row * K);
             uint4* orow = reinterpret_cast<uint4*>(out + row * K);
-            for (int64_t c = warp; c < chunks; c += kDeqWarps) {
-                uint2 w[2];
-                #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const int64_t i = c * 64 + j * 32 + lane;
-                    w[j] = i < pairs ? __ldg(qr + i) : make_uint2(0u, 0u);
-                }
+            {
                 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
                     const int64_t i = c * 64 + j * 32 + lane;
@@ -306,6 +321,8 @@ dequantize_bf16_kernel(uint16_t* __restrict__ out, const int8_t* __restrict__ q,
                     }
                 }
             }
+            row = row2;
+            c = c2;
         }
     } else {
         const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
