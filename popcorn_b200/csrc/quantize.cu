@@ -238,23 +238,37 @@ dequantize_kernel(float* __restrict__ out, const int8_t* __restrict__ q,
         const int warp = threadIdx.x >> 5;
         const int64_t words = K >> 2;  // code words per row
         const int64_t chunks = (K + 511) >> 9;
-        for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
-            const float sc = __ldg(scale + row);
-            const uint32_t* qr = reinterpret_cast<const uint32_t*>(q + row * K);
-            float4* orow = reinterpret_cast<float4*>(out + row * K);
-            for (int64_t c = warp; c < chunks; c += kDeqWarps) {
-                uint32_t w[4];
-                #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int64_t i = c * 128 + j * 32 + lane;
-                    w[j] = i < words ? __ldg(qr + i) : 0u;
-                }
-                #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int64_t i = c * 128 + j * 32 + lane;
-                    if (i < words) orow[i] = expand4(w[j], sc);
-                }
+        // This warp's (row, chunk) items in order, the next item's codes
+        // requested before the current one is expanded and stored.
+        auto load = [&](int64_t r, int64_t cc, uint32_t (&w)[4]) {
+            const uint32_t* qr = reinterpret_cast<const uint32_t*>(q + r * K);
+            #pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int64_t i = cc * 128 + j * 32 + lane;
+                w[j] = i < words ? __ldg(qr + i) : 0u;
             }
+        };
+        int64_t row = blockIdx.x;
+        int64_t c = warp;
+        uint32_t wn[4] = {0u, 0u, 0u, 0u};
+        if (c < chunks && row < N) load(row, c, wn);
+        while (c < chunks && row < N) {
+            int64_t row2 = row, c2 = c + kDeqWarps;
+            if (c2 >= chunks) {
+                c2 = warp;
+                row2 += gridDim.x;
+            }
+            const uint32_t w[4] = {wn[0], wn[1], wn[2], wn[3]};
+            if (row2 < N) load(row2, c2, wn);
+            const float sc = __ldg(scale + row);
+            float4* orow = reinterpret_cast<float4*>(out + row * K);
+            #pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int64_t i = c * 128 + j * 32 + lane;
+                if (i < words) orow[i] = expand4(w[j], sc);
+            }
+            row = row2;
+            c = c2;
         }
     } else {
         const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
